@@ -1,0 +1,212 @@
+/*
+ * titan_moe.h — C ABI of the B200-native quantised mixture-of-experts block.
+ *
+ * Plain pointers and sizes only.  Every pointer argument is a device pointer
+ * unless stated otherwise; `stream` is a cudaStream_t (NULL = the legacy
+ * default stream).  No entry point allocates memory: callers pass buffers and
+ * a workspace sized by the matching *_workspace_size() query.  No entry point
+ * synchronises the host; all launch on `stream` and return immediately.
+ *
+ * Tensor conventions (MLX layout, as in the reference):
+ *   bf16 values are uint16_t bit patterns;
+ *   packed int4 weights w [E, N, K/8] uint32, element 8j+i of a word in
+ *   bits 4i..4i+3 (low nibble first);  scales/biases [E, N, K/64] bf16;
+ *   dequantised weight = q * scale + bias, group size 64, 4 bits, affine.
+ *   A fused gate_up tensor holds the gate rows [0, I) then the up rows [I, 2I).
+ *
+ * Return value: TMOE_OK or an error code; tmoe_last_error() describes the
+ * last failure on the calling thread.
+ */
+#ifndef TITAN_MOE_H
+#define TITAN_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  TMOE_OK = 0,
+  TMOE_ERR_INVALID = 1,     /* bad argument or inconsistent shape            */
+  TMOE_ERR_UNSUPPORTED = 2, /* shape outside what the kernels implement      */
+  TMOE_ERR_CUDA = 3,        /* a CUDA launch or runtime call failed          */
+  TMOE_ERR_NCCL = 4,        /* an NCCL call failed (expert parallelism)      */
+  TMOE_ERR_TIMEOUT = 5,     /* a bounded device wait gave up                 */
+  TMOE_ERR_WORKSPACE = 6    /* workspace missing or smaller than required    */
+};
+
+#define TMOE_ABI_VERSION 1
+
+int tmoe_abi_version(void);
+const char* tmoe_last_error(void);
+
+/* Profiling hook (no reference counterpart: the reference times whole MLX
+ * graphs).  When set, every entry point calls fn(ctx, name) on the calling
+ * host thread immediately before each kernel launch, so a caller can record
+ * events on the stream between kernels (and one after the call returns) or
+ * count launches.  Per calling thread; NULL disables. */
+typedef void (*tmoe_stage_fn)(void* ctx, const char* name);
+void tmoe_set_stage_hook(tmoe_stage_fn fn, void* ctx);
+
+/* ------------------------------------------------------------ weight prep */
+
+/* MLX mx.quantize(w, group_size=64, bits=4, mode="affine") on the GPU
+ * (call sites: titan/adapters/mlx/vendor/mlx_lm/models/switch_layers.py:42,179).
+ * w fp32 [rows, K] -> wq uint32 [rows, K/8], scales/biases bf16 [rows, K/64]. */
+int tmoe_affine_quantize(const float* w, int64_t rows, int K, uint32_t* wq, uint16_t* scales,
+                         uint16_t* biases, void* stream);
+
+/* Transposed [E, K/64, N] scale and bias tables streamed by the grouped GEMMs.
+ * Replaces the table builder of titan/kernels/moe_gather_int8.py:227-248
+ * (build_tables / Int8Tables) and engine/patches/moe-int8/kernel.py:432-446
+ * (prepare_weights); the int8 kernel folds b + 8s itself and needs no qsum. */
+int tmoe_prepare_tables(const uint16_t* scales, const uint16_t* biases, int E, int N, int K,
+                        uint16_t* scales_t, uint16_t* biases_t, void* stream);
+
+/* Nibble sums qsum [E, K/64, N] uint16 — the reference table of
+ * titan/kernels/moe_gather_int8.py:189-202 (titan_i8_qsum), for callers that
+ * still hold Int8Tables. */
+int tmoe_qsum(const uint32_t* w, int E, int N, int K, uint16_t* qsum, void* stream);
+
+/* -------------------------------------------------------------- activations */
+
+/* Per (row, 64-group) uint8 activation quantiser, zero point 128, scale
+ * amax/127 — titan/kernels/moe_gather_int8.py:168-182 (quantize_activations).
+ * Writes signed codes xq = xu - 128 [R, K] int8, xsc / xrs [R, K/64] fp32
+ * (scale and exact group sum of the unquantised row). */
+int tmoe_quantize_activations(const uint16_t* x, int R, int K, int8_t* xq, float* xsc, float* xrs,
+                              void* stream);
+
+/* ------------------------------------------------------------------ router */
+
+/* Router Linear + softmax(precise) + top-k + renormalisation —
+ * titan/adapters/mlx/vendor/mlx_vlm/models/qwen3_5_moe/language.py:65-71 and the
+ * fused router of engine/patches/decode-fusion/fused_kernels.py:348-374.
+ * x [T, H] bf16, router_w [E, H] bf16; logits_ws [T, E] bf16 scratch (also the
+ * router logits on return); idx [T, k] int32 in selection order (descending
+ * probability, lowest index first on ties); scores [T, k] bf16; probs_out
+ * [T, E] bf16 or NULL.  E <= 1024, k <= 32, H % 64 == 0. */
+int tmoe_router_topk(const uint16_t* x, const uint16_t* router_w, int T, int H, int E, int k,
+                     uint16_t* logits_ws, int32_t* idx, uint16_t* scores, uint16_t* probs_out,
+                     void* stream);
+
+/* ------------------------------------------------------------ routing plan */
+
+/* Stable sort of flat expert ids and the ragged tile table —
+ * switch_layers.py:13-25 (_gather_sort / _scatter_unsort) and
+ * titan/kernels/moe_gather_ws.py:176-202 (build_tiles, TileTable).
+ * order [R]: sorted row -> flat index; inv_order [R]: flat -> sorted row;
+ * offsets [E+1]; tile_row / tile_exp [maxt] (tiles of 128 rows, may be NULL);
+ * ntiles [1].  maxt >= ceil(R/128) + E. */
+size_t tmoe_route_workspace_size(int R, int E);
+int tmoe_route_sort(const int32_t* idx, int R, int E, void* ws, size_t ws_bytes, int32_t* order,
+                    int32_t* inv_order, int32_t* offsets, int32_t* tile_row, int32_t* tile_exp,
+                    int32_t* ntiles, int maxt, void* stream);
+
+/* ---------------------------------------------------------------- gathers */
+
+/* int8-activation x int4-weight sorted gather: y[r] = x[r] @ dequant(w[rhs[r]])^T
+ * with x quantised per (row, 64-group) — the drop-in for
+ * mx.gather_qmm(..., sorted_indices=True) installed by
+ * engine/patches/moe-int8/patch.py:105-122 (kernel.py:482-501,
+ * titan/kernels/moe_gather_int8.py:393-425).
+ * x [R, K] bf16, rhs [R] int32 (sorted by expert), scales_t / biases_t from
+ * tmoe_prepare_tables; y [R, N] bf16.  N % 128 == 0, K % 64 == 0. */
+size_t tmoe_gather_qmm_int8_workspace_size(int R, int E, int N, int K);
+int tmoe_gather_qmm_int8(const uint16_t* x, const uint32_t* w, const uint16_t* scales_t,
+                         const uint16_t* biases_t, const int32_t* rhs, int R, int E, int N, int K,
+                         void* ws, size_t ws_bytes, uint16_t* y, void* stream);
+
+/* bf16-activation gather with exact dequantisation and fp32 accumulation —
+ * the stock mx.gather_qmm of switch_layers.py:86-98 (sorted or unsorted rhs).
+ * x [R, K] bf16, rhs [R] int32 (any order); scales_t / biases_t may be NULL
+ * when R <= 256 (decode GEMV path), otherwise required; y [R, N] bf16.
+ * N % 128 == 0, K % 64 == 0. */
+size_t tmoe_gather_qmm_bf16_workspace_size(int R, int E, int N, int K);
+int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
+                         const uint16_t* biases, const uint16_t* scales_t,
+                         const uint16_t* biases_t, const int32_t* rhs, int R, int E, int N, int K,
+                         void* ws, size_t ws_bytes, uint16_t* y, void* stream);
+
+/* ------------------------------------------------------- decode-fused ops */
+
+/* h[t, j, :] = silu(Wg[e] x_t) * (Wu[e] x_t), fp32 —
+ * engine/patches/decode-fusion/fused_kernels.py:194-210 (gate_up_silu).
+ * x [T, K] bf16, w [E, 2I, K/8], idx [T, k]; h [T, k, I] fp32. */
+size_t tmoe_decode_workspace_size(int T, int k, int E, int K, int I);
+int tmoe_gate_up_silu(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
+                      const uint16_t* biases, const int32_t* idx, int T, int k, int E, int K, int I,
+                      void* ws, size_t ws_bytes, float* h, void* stream);
+
+/* y[t] = sum_j scores[t, j] * (Wd[idx[t, j]] h[t, j]) in fp32, bf16 out —
+ * fused_kernels.py:213-229 (down_wsum).  h [T, k, I] fp32, w [E, D, I/8],
+ * scores [T, k] fp32; y [T, D] bf16. */
+int tmoe_down_wsum(const float* h, const uint32_t* w, const uint16_t* scales,
+                   const uint16_t* biases, const int32_t* idx, const float* scores, int T, int k,
+                   int E, int I, int D, void* ws, size_t ws_bytes, uint16_t* y, void* stream);
+
+/* SwiGLU with bf16 rounding after each op —
+ * titan/adapters/mlx/vendor/mlx_lm/models/activations.py:9-11 with the gate/up
+ * split of switch_layers.py:229-237.  gate_up [R, 2I] bf16 (gate columns
+ * first) -> h [R, I] bf16 = silu(gate) * up. */
+int tmoe_swiglu(const uint16_t* gate_up, int R, int I, uint16_t* h, void* stream);
+
+/* ------------------------------------------------------------ weighted sum */
+
+/* Unsort + routed weighted top-k sum — titan/kernels/moe_weighted_sum.py:163-195.
+ * ys [T*k, D] bf16 in sorted order with inv_order [T*k] (flat -> sorted row),
+ * or token-major when inv_order is NULL; scores [T, k] bf16; out [T, D] bf16.
+ * mode 0 = clone (bit-identical to MLX's 8-partial bf16 reduce), 1 = fast. */
+int tmoe_weighted_sum(const uint16_t* ys, const int32_t* inv_order, const uint16_t* scores, int T,
+                      int k, int D, int mode, uint16_t* out, void* stream);
+
+/* ------------------------------------------------------------- whole block */
+
+/* One MoE layer's device weights (MLX layout) plus the prepared tables. */
+typedef struct tmoe_layer {
+  int hidden;           /* H */
+  int num_experts;      /* E */
+  int top_k;            /* k */
+  int moe_inter;        /* I (expert intermediate) */
+  int shared_inter;     /* Is (0: no shared expert) */
+  const uint16_t* router_w;                                      /* [E, H] */
+  const uint32_t* gate_up_w; const uint16_t* gate_up_s; const uint16_t* gate_up_b;  /* [E, 2I, .] */
+  const uint32_t* down_w; const uint16_t* down_s; const uint16_t* down_b;           /* [E, H, .] */
+  const uint16_t* gate_up_st; const uint16_t* gate_up_bt;        /* [E, H/64, 2I] */
+  const uint16_t* down_st; const uint16_t* down_bt;              /* [E, I/64, H] */
+  const uint32_t* shared_gate_up_w; const uint16_t* shared_gate_up_s;
+  const uint16_t* shared_gate_up_b;                              /* [2Is, H/8], [2Is, H/64] */
+  const uint32_t* shared_down_w; const uint16_t* shared_down_s;
+  const uint16_t* shared_down_b;                                 /* [H, Is/8], [H, Is/64] */
+  const uint16_t* shared_gate_up_st; const uint16_t* shared_gate_up_bt; /* [H/64, 2Is] */
+  const uint16_t* shared_down_st; const uint16_t* shared_down_bt;       /* [Is/64, H] */
+  const uint16_t* shared_gate_w;                                 /* [H] bf16 */
+} tmoe_layer;
+
+typedef struct tmoe_options {
+  int min_tokens;   /* T >= min_tokens: grouped-GEMM prefill path (default 512,
+                       OMLX_MOE_INT8_MIN_TOKENS of patch.py:24-27); below it
+                       the fp32 decode path */
+  int down_int8;    /* 1: int8 down projection; 0: bf16-activation down
+                       (OMLX_MOE_INT8_SKIP_DOWN=1) */
+  int wsum_mode;    /* 0 clone, 1 fast */
+  int int8_prefill; /* 1: int8 gate_up (the overlay installed); 0: the stock
+                       bf16-activation grouped GEMMs for the prefill path */
+} tmoe_options;     /* NULL options = {512, 1, 0, 1} */
+
+/* Qwen3_5MoeSparseMoeBlock.__call__ —
+ * titan/adapters/mlx/vendor/mlx_vlm/models/qwen3_5_moe/language.py:60-91 with
+ * the int8 overlay installed.  x [T, H] bf16 -> y [T, H] bf16; idx_out [T, k]
+ * int32 and scores_out [T, k] bf16 may be NULL. */
+size_t tmoe_moe_workspace_size(const tmoe_layer* layer, int T, const tmoe_options* opt);
+int tmoe_moe_forward(const tmoe_layer* layer, const uint16_t* x, int T, const tmoe_options* opt,
+                     void* ws, size_t ws_bytes, uint16_t* y, int32_t* idx_out,
+                     uint16_t* scores_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TITAN_MOE_H */

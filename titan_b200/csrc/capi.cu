@@ -1,0 +1,862 @@
+// C ABI (include/titan_moe.h): argument checks, workspace carving and the
+// launch sequence of each entry point.  No entry point allocates device
+// memory or synchronises the host; errors come back as status codes with a
+// per-thread message.
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/titan_moe.h"
+#include "tmoe_internal.h"
+
+using namespace tmoe;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return TMOE_OK;
+  return fail(TMOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+thread_local tmoe_stage_fn g_hook = nullptr;
+thread_local void* g_hook_ctx = nullptr;
+
+inline void stage(const char* name) {
+  if (g_hook) g_hook(g_hook_ctx, name);
+}
+
+#define TMOE_TRY(expr, what)                                   \
+  do {                                                         \
+    stage(what);                                               \
+    int _rc = cuda_status((expr), what);                       \
+    if (_rc != TMOE_OK) return _rc;                            \
+  } while (0)
+
+// Carves 256-byte aligned pieces out of the caller's workspace.  With a null
+// base it only measures.
+struct Carve {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carve(void* b) : base(static_cast<uint8_t*>(b)) {}
+  template <class T>
+  T* take(size_t n) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return p;
+  }
+};
+
+cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+int max_tiles(int R, int E) { return (R + kTileM - 1) / kTileM + E; }
+
+bool bad_k(int K) { return K <= 0 || K % 64 != 0; }
+
+}  // namespace
+
+extern "C" {
+
+int tmoe_abi_version(void) { return TMOE_ABI_VERSION; }
+
+void tmoe_set_stage_hook(tmoe_stage_fn fn, void* ctx) {
+  g_hook = fn;
+  g_hook_ctx = ctx;
+}
+
+const char* tmoe_last_error(void) { return g_err.c_str(); }
+
+// ---------------------------------------------------------------- weight prep
+
+int tmoe_affine_quantize(const float* w, int64_t rows, int K, uint32_t* wq, uint16_t* scales,
+                         uint16_t* biases, void* stream) {
+  if (!w || !wq || !scales || !biases || rows < 0 || bad_k(K))
+    return fail(TMOE_ERR_INVALID, "tmoe_affine_quantize: bad arguments (rows=%lld K=%d)",
+                (long long)rows, K);
+  TMOE_TRY(launch_affine_quantize(w, rows, K, wq, scales, biases, S(stream)), "affine_quantize");
+  return TMOE_OK;
+}
+
+int tmoe_prepare_tables(const uint16_t* scales, const uint16_t* biases, int E, int N, int K,
+                        uint16_t* scales_t, uint16_t* biases_t, void* stream) {
+  if (!scales || !biases || !scales_t || !biases_t || E <= 0 || N <= 0 || bad_k(K))
+    return fail(TMOE_ERR_INVALID, "tmoe_prepare_tables: bad arguments");
+  TMOE_TRY(launch_prepare_tables(scales, biases, E, N, K / 64, scales_t, biases_t, S(stream)),
+           "prepare_tables");
+  return TMOE_OK;
+}
+
+int tmoe_qsum(const uint32_t* w, int E, int N, int K, uint16_t* qsum, void* stream) {
+  if (!w || !qsum || E <= 0 || N <= 0 || bad_k(K))
+    return fail(TMOE_ERR_INVALID, "tmoe_qsum: bad arguments");
+  TMOE_TRY(launch_qsum(w, E, N, K, qsum, S(stream)), "qsum");
+  return TMOE_OK;
+}
+
+int tmoe_quantize_activations(const uint16_t* x, int R, int K, int8_t* xq, float* xsc, float* xrs,
+                              void* stream) {
+  if (!x || !xq || !xsc || !xrs || R < 0 || bad_k(K))
+    return fail(TMOE_ERR_INVALID, "tmoe_quantize_activations: bad arguments");
+  TMOE_TRY(launch_quantize_rows(x, R, K, xq, xsc, xrs, S(stream)), "quantize_activations");
+  return TMOE_OK;
+}
+
+// --------------------------------------------------------------------- router
+
+static int check_router(int T, int H, int E, int k) {
+  if (T < 0 || H <= 0 || H % 64 || E <= 0 || E > 1024 || k <= 0 || k > 32 || k > E)
+    return fail(TMOE_ERR_UNSUPPORTED,
+                "router: need H %% 64 == 0, 0 < E <= 1024, 0 < k <= min(32, E) (H=%d E=%d k=%d)",
+                H, E, k);
+  return TMOE_OK;
+}
+
+int tmoe_router_topk(const uint16_t* x, const uint16_t* router_w, int T, int H, int E, int k,
+                     uint16_t* logits_ws, int32_t* idx, uint16_t* scores, uint16_t* probs_out,
+                     void* stream) {
+  if (!x || !router_w || !logits_ws || !idx || !scores)
+    return fail(TMOE_ERR_INVALID, "tmoe_router_topk: null pointer");
+  if (int rc = check_router(T, H, E, k)) return rc;
+  if (T == 0) return TMOE_OK;
+  TMOE_TRY(launch_router_logits(x, router_w, nullptr, T, H, E, logits_ws, nullptr, S(stream)),
+           "router_logits");
+  TMOE_TRY(launch_router_topk(logits_ws, T, E, k, idx, scores, probs_out, S(stream)), "router_topk");
+  return TMOE_OK;
+}
+
+// -------------------------------------------------------------- routing plan
+
+size_t tmoe_route_workspace_size(int R, int E) {
+  if (R < 0 || E <= 0) return 0;
+  return route_plan_scratch_bytes(R, E);
+}
+
+int tmoe_route_sort(const int32_t* idx, int R, int E, void* ws, size_t ws_bytes, int32_t* order,
+                    int32_t* inv_order, int32_t* offsets, int32_t* tile_row, int32_t* tile_exp,
+                    int32_t* ntiles, int maxt, void* stream) {
+  if (!idx || !order || !inv_order || !offsets || R < 0 || E <= 0 || E > 1024)
+    return fail(TMOE_ERR_INVALID, "tmoe_route_sort: bad arguments");
+  if ((tile_row != nullptr) != (tile_exp != nullptr) || (tile_row && (!ntiles || maxt < 1)))
+    return fail(TMOE_ERR_INVALID, "tmoe_route_sort: tile_row, tile_exp, ntiles and maxt go together");
+  if (tile_row && maxt < max_tiles(R, E))
+    return fail(TMOE_ERR_INVALID, "tmoe_route_sort: maxt %d < ceil(R/128)+E = %d", maxt,
+                max_tiles(R, E));
+  const size_t need = route_plan_scratch_bytes(R, E);
+  if (need && (!ws || ws_bytes < need))
+    return fail(TMOE_ERR_WORKSPACE, "tmoe_route_sort: workspace %zu < %zu bytes", ws_bytes, need);
+  if (R == 0) return TMOE_OK;
+  RoutePlan p{};
+  p.order = order;
+  p.inv = inv_order;
+  p.offsets = offsets;
+  p.tile_row = tile_row;
+  p.tile_exp = tile_exp;
+  p.ntiles = ntiles;
+  TMOE_TRY(launch_route_plan(idx, R, E, kTileM, maxt, p, ws, S(stream)), "route_plan");
+  return TMOE_OK;
+}
+
+// ------------------------------------------------------------------ gathers
+
+namespace {
+
+struct Int8GatherWs {
+  int32_t *order, *inv, *offsets, *tile_row, *tile_exp, *ntiles;
+  int8_t* xq;
+  float *xsc, *xrs;
+  void* route_scratch;
+};
+
+size_t carve_int8_gather(Carve& c, int R, int E, int K, Int8GatherWs* w) {
+  const int maxt = max_tiles(R, E);
+  Int8GatherWs t;
+  t.order = c.take<int32_t>(R);
+  t.inv = c.take<int32_t>(R);
+  t.offsets = c.take<int32_t>(E + 1);
+  t.tile_row = c.take<int32_t>(maxt);
+  t.tile_exp = c.take<int32_t>(maxt);
+  t.ntiles = c.take<int32_t>(1);
+  t.xq = c.take<int8_t>((size_t)R * K);
+  t.xsc = c.take<float>((size_t)R * (K / 64));
+  t.xrs = c.take<float>((size_t)R * (K / 64));
+  t.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(R, E));
+  if (w) *w = t;
+  return c.off;
+}
+
+}  // namespace
+
+size_t tmoe_gather_qmm_int8_workspace_size(int R, int E, int N, int K) {
+  (void)N;
+  if (R < 0 || E <= 0 || bad_k(K)) return 0;
+  Carve c(nullptr);
+  return carve_int8_gather(c, R, E, K, nullptr);
+}
+
+int tmoe_gather_qmm_int8(const uint16_t* x, const uint32_t* w, const uint16_t* scales_t,
+                         const uint16_t* biases_t, const int32_t* rhs, int R, int E, int N, int K,
+                         void* ws, size_t ws_bytes, uint16_t* y, void* stream) {
+  if (!x || !w || !scales_t || !biases_t || !rhs || !y || R < 0 || E <= 0 || E > 1024)
+    return fail(TMOE_ERR_INVALID, "tmoe_gather_qmm_int8: bad arguments");
+  if (bad_k(K) || N <= 0 || N % 128)
+    return fail(TMOE_ERR_UNSUPPORTED, "tmoe_gather_qmm_int8: need K %% 64 == 0 and N %% 128 == 0 (K=%d N=%d)", K, N);
+  const size_t need = tmoe_gather_qmm_int8_workspace_size(R, E, N, K);
+  if (!ws || ws_bytes < need)
+    return fail(TMOE_ERR_WORKSPACE, "tmoe_gather_qmm_int8: workspace %zu < %zu bytes", ws_bytes, need);
+  if (R == 0) return TMOE_OK;
+  Carve c(ws);
+  Int8GatherWs b;
+  carve_int8_gather(c, R, E, K, &b);
+  const int maxt = max_tiles(R, E);
+  RoutePlan p{};
+  p.order = b.order;
+  p.inv = b.inv;
+  p.offsets = b.offsets;
+  p.tile_row = b.tile_row;
+  p.tile_exp = b.tile_exp;
+  p.ntiles = b.ntiles;
+  cudaStream_t s = S(stream);
+  TMOE_TRY(launch_route_plan(rhs, R, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
+  TMOE_TRY(launch_quantize_rows(x, R, K, b.xq, b.xsc, b.xrs, s), "quantize_rows");
+  GemmParams g{};
+  g.A = b.xq;
+  g.asc = b.xsc;
+  g.ars = b.xrs;
+  g.s_r = K / 64;
+  g.s_g = 1;
+  g.a_rows = b.order;
+  g.a_div = 1;
+  g.W = w;
+  g.st = scales_t;
+  g.bt = biases_t;
+  g.tile_row = b.tile_row;
+  g.tile_exp = b.tile_exp;
+  g.ntiles = b.ntiles;
+  g.offsets = b.offsets;
+  g.K = K;
+  g.N = N;
+  g.Y = y;
+  g.y_rows = b.order;
+  TMOE_TRY(launch_gemm_grouped(true, kEpiStore, g, maxt, s), "gemm_int8");
+  return TMOE_OK;
+}
+
+namespace {
+
+constexpr int kGemvMaxRows = 256;
+
+struct Bf16GatherWs {
+  int32_t *order, *inv, *offsets, *tile_row, *tile_exp, *ntiles, *uexp, *ustart, *nuniq;
+  uint16_t* x16p;
+  float* xsum;
+  void* route_scratch;
+};
+
+size_t carve_bf16_gather(Carve& c, int R, int E, int K, Bf16GatherWs* w) {
+  const int maxt = max_tiles(R, E);
+  const int U = R < E ? R : E;
+  Bf16GatherWs t;
+  t.order = c.take<int32_t>(R);
+  t.inv = c.take<int32_t>(R);
+  t.offsets = c.take<int32_t>(E + 1);
+  t.tile_row = c.take<int32_t>(maxt);
+  t.tile_exp = c.take<int32_t>(maxt);
+  t.ntiles = c.take<int32_t>(1);
+  t.uexp = c.take<int32_t>(U > 0 ? U : 1);
+  t.ustart = c.take<int32_t>(U + 1);
+  t.nuniq = c.take<int32_t>(1);
+  t.x16p = c.take<uint16_t>((size_t)R * K);
+  t.xsum = c.take<float>((size_t)R * (K / 64));
+  t.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(R, E));
+  if (w) *w = t;
+  return c.off;
+}
+
+}  // namespace
+
+size_t tmoe_gather_qmm_bf16_workspace_size(int R, int E, int N, int K) {
+  (void)N;
+  if (R < 0 || E <= 0 || bad_k(K)) return 0;
+  Carve c(nullptr);
+  return carve_bf16_gather(c, R, E, K, nullptr);
+}
+
+int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
+                         const uint16_t* biases, const uint16_t* scales_t,
+                         const uint16_t* biases_t, const int32_t* rhs, int R, int E, int N, int K,
+                         void* ws, size_t ws_bytes, uint16_t* y, void* stream) {
+  if (!x || !w || !scales || !biases || !rhs || !y || R < 0 || E <= 0 || E > 1024)
+    return fail(TMOE_ERR_INVALID, "tmoe_gather_qmm_bf16: bad arguments");
+  if (bad_k(K) || N <= 0 || N % 128)
+    return fail(TMOE_ERR_UNSUPPORTED, "tmoe_gather_qmm_bf16: need K %% 64 == 0 and N %% 128 == 0 (K=%d N=%d)", K, N);
+  const bool gemv = R <= kGemvMaxRows;
+  if (!gemv && (!scales_t || !biases_t))
+    return fail(TMOE_ERR_INVALID, "tmoe_gather_qmm_bf16: R=%d > %d needs the prepared tables", R,
+                kGemvMaxRows);
+  const size_t need = tmoe_gather_qmm_bf16_workspace_size(R, E, N, K);
+  if (!ws || ws_bytes < need)
+    return fail(TMOE_ERR_WORKSPACE, "tmoe_gather_qmm_bf16: workspace %zu < %zu bytes", ws_bytes, need);
+  if (R == 0) return TMOE_OK;
+  Carve c(ws);
+  Bf16GatherWs b;
+  carve_bf16_gather(c, R, E, K, &b);
+  cudaStream_t s = S(stream);
+  const int maxt = max_tiles(R, E);
+  const int U = R < E ? R : E;
+  RoutePlan p{};
+  p.order = b.order;
+  p.inv = b.inv;
+  p.offsets = b.offsets;
+  if (gemv) {
+    p.uexp = b.uexp;
+    p.ustart = b.ustart;
+    p.nuniq = b.nuniq;
+  } else {
+    p.tile_row = b.tile_row;
+    p.tile_exp = b.tile_exp;
+    p.ntiles = b.ntiles;
+  }
+  TMOE_TRY(launch_route_plan(rhs, R, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
+  const int G = K / 64;
+  TMOE_TRY(launch_prep_x(x, R, K, b.x16p, b.xsum, G, 1, s), "prep_x");
+  if (gemv) {
+    GemvParams q{};
+    q.bh = b.x16p;
+    q.bsum = b.xsum;
+    q.K = K;
+    q.W = w;
+    q.S = scales;
+    q.B = biases;
+    q.N = N;
+    q.uexp = b.uexp;
+    q.ustart = b.ustart;
+    q.nuniq = b.nuniq;
+    q.order = b.order;
+    q.umax = U;
+    q.col_div = 1;
+    q.swiglu = 0;
+    q.outb = y;
+    TMOE_TRY(launch_gemv_tc(q, s), "gemv");
+  } else {
+    GemmParams g{};
+    g.A = b.x16p;
+    g.ars = b.xsum;
+    g.s_r = G;
+    g.s_g = 1;
+    g.a_rows = b.order;
+    g.a_div = 1;
+    g.W = w;
+    g.st = scales_t;
+    g.bt = biases_t;
+    g.tile_row = b.tile_row;
+    g.tile_exp = b.tile_exp;
+    g.ntiles = b.ntiles;
+    g.offsets = b.offsets;
+    g.K = K;
+    g.N = N;
+    g.Y = y;
+    g.y_rows = b.order;
+    TMOE_TRY(launch_gemm_grouped(false, kEpiStore, g, maxt, s), "gemm_f16");
+  }
+  return TMOE_OK;
+}
+
+// -------------------------------------------------------- decode-fused ops
+
+namespace {
+
+struct DecodeOpWs {
+  int32_t *order, *inv, *offsets, *uexp, *ustart, *nuniq;
+  uint16_t *a16, *a16lo;
+  float* asum;
+  float* part;
+  void* route_scratch;
+};
+
+size_t carve_decode_op(Carve& c, int T, int k, int E, int K, int I, int D, DecodeOpWs* w) {
+  const int R = T * k;
+  const int U = R < E ? R : E;
+  DecodeOpWs t;
+  t.order = c.take<int32_t>(R);
+  t.inv = c.take<int32_t>(R);
+  t.offsets = c.take<int32_t>(E + 1);
+  t.uexp = c.take<int32_t>(U > 0 ? U : 1);
+  t.ustart = c.take<int32_t>(U + 1);
+  t.nuniq = c.take<int32_t>(1);
+  const size_t arows = (size_t)(R > T ? R : T);
+  const int KA = K > I ? K : I;
+  t.a16 = c.take<uint16_t>(arows * KA);
+  t.a16lo = c.take<uint16_t>(arows * KA);
+  t.asum = c.take<float>(arows * (KA / 64));
+  t.part = c.take<float>((size_t)R * (D > 0 ? D : 1));
+  t.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(R, E));
+  if (w) *w = t;
+  return c.off;
+}
+
+}  // namespace
+
+size_t tmoe_decode_workspace_size(int T, int k, int E, int K, int I) {
+  if (T < 0 || k <= 0 || E <= 0 || bad_k(K) || bad_k(I)) return 0;
+  Carve c(nullptr);
+  // down_wsum needs part [R, D]; D = K of the gate_up call (hidden size).
+  return carve_decode_op(c, T, k, E, K, I, K, nullptr);
+}
+
+int tmoe_gate_up_silu(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
+                      const uint16_t* biases, const int32_t* idx, int T, int k, int E, int K, int I,
+                      void* ws, size_t ws_bytes, float* h, void* stream) {
+  if (!x || !w || !scales || !biases || !idx || !h || T < 0 || k <= 0 || E <= 0 || E > 1024)
+    return fail(TMOE_ERR_INVALID, "tmoe_gate_up_silu: bad arguments");
+  if (bad_k(K) || I <= 0 || I % 32)
+    return fail(TMOE_ERR_UNSUPPORTED, "tmoe_gate_up_silu: need K %% 64 == 0, I %% 32 == 0");
+  const size_t need = tmoe_decode_workspace_size(T, k, E, K, I);
+  if (!ws || ws_bytes < need)
+    return fail(TMOE_ERR_WORKSPACE, "tmoe_gate_up_silu: workspace %zu < %zu bytes", ws_bytes, need);
+  if (T == 0) return TMOE_OK;
+  Carve c(ws);
+  DecodeOpWs b;
+  carve_decode_op(c, T, k, E, K, I, K, &b);
+  cudaStream_t s = S(stream);
+  const int R = T * k, U = R < E ? R : E;
+  RoutePlan p{};
+  p.order = b.order;
+  p.inv = b.inv;
+  p.offsets = b.offsets;
+  p.uexp = b.uexp;
+  p.ustart = b.ustart;
+  p.nuniq = b.nuniq;
+  TMOE_TRY(launch_route_plan(idx, R, E, kTileM, 1, p, b.route_scratch, s), "route_plan");
+  TMOE_TRY(launch_prep_x(x, T, K, b.a16, b.asum, K / 64, 1, s), "prep_x");
+  GemvParams q{};
+  q.bh = b.a16;
+  q.bsum = b.asum;
+  q.K = K;
+  q.W = w;
+  q.S = scales;
+  q.B = biases;
+  q.N = 2 * I;
+  q.uexp = b.uexp;
+  q.ustart = b.ustart;
+  q.nuniq = b.nuniq;
+  q.order = b.order;
+  q.umax = U;
+  q.col_div = k;
+  q.swiglu = 1;
+  q.out = h;
+  TMOE_TRY(launch_gemv_tc(q, s), "gemv_gate_up");
+  return TMOE_OK;
+}
+
+int tmoe_down_wsum(const float* h, const uint32_t* w, const uint16_t* scales,
+                   const uint16_t* biases, const int32_t* idx, const float* scores, int T, int k,
+                   int E, int I, int D, void* ws, size_t ws_bytes, uint16_t* y, void* stream) {
+  if (!h || !w || !scales || !biases || !idx || !scores || !y || T < 0 || k <= 0 || E <= 0 ||
+      E > 1024)
+    return fail(TMOE_ERR_INVALID, "tmoe_down_wsum: bad arguments");
+  if (bad_k(I) || D <= 0 || D % 64)
+    return fail(TMOE_ERR_UNSUPPORTED, "tmoe_down_wsum: need I %% 64 == 0, D %% 64 == 0");
+  Carve m(nullptr);
+  const size_t need = carve_decode_op(m, T, k, E, D, I, D, nullptr);
+  if (!ws || ws_bytes < need)
+    return fail(TMOE_ERR_WORKSPACE, "tmoe_down_wsum: workspace %zu < %zu bytes", ws_bytes, need);
+  if (T == 0) return TMOE_OK;
+  Carve c(ws);
+  DecodeOpWs b;
+  carve_decode_op(c, T, k, E, D, I, D, &b);
+  cudaStream_t s = S(stream);
+  const int R = T * k, U = R < E ? R : E;
+  RoutePlan p{};
+  p.order = b.order;
+  p.inv = b.inv;
+  p.offsets = b.offsets;
+  p.uexp = b.uexp;
+  p.ustart = b.ustart;
+  p.nuniq = b.nuniq;
+  TMOE_TRY(launch_route_plan(idx, R, E, kTileM, 1, p, b.route_scratch, s), "route_plan");
+  TMOE_TRY(launch_prep_h(h, R, I, b.a16, b.a16lo, b.asum, s), "prep_h");
+  GemvParams q{};
+  q.bh = b.a16;
+  q.bl = b.a16lo;
+  q.bsum = b.asum;
+  q.K = I;
+  q.W = w;
+  q.S = scales;
+  q.B = biases;
+  q.N = D;
+  q.uexp = b.uexp;
+  q.ustart = b.ustart;
+  q.nuniq = b.nuniq;
+  q.order = b.order;
+  q.umax = U;
+  q.col_div = 1;
+  q.swiglu = 0;
+  q.out = b.part;
+  TMOE_TRY(launch_gemv_tc(q, s), "gemv_down");
+  TMOE_TRY(launch_decode_combine(b.part, nullptr, scores, T, k, D, nullptr, nullptr, y, s),
+           "combine");
+  return TMOE_OK;
+}
+
+// ---------------------------------------------------------------------- SwiGLU
+
+int tmoe_swiglu(const uint16_t* gate_up, int R, int I, uint16_t* h, void* stream) {
+  if (!gate_up || !h || R < 0 || I <= 0) return fail(TMOE_ERR_INVALID, "tmoe_swiglu: bad arguments");
+  TMOE_TRY(launch_swiglu(gate_up, R, I, h, S(stream)), "swiglu");
+  return TMOE_OK;
+}
+
+// --------------------------------------------------------------- weighted sum
+
+int tmoe_weighted_sum(const uint16_t* ys, const int32_t* inv_order, const uint16_t* scores, int T,
+                      int k, int D, int mode, uint16_t* out, void* stream) {
+  if (!ys || !scores || !out || T < 0 || k <= 0 || (mode != 0 && mode != 1))
+    return fail(TMOE_ERR_INVALID, "tmoe_weighted_sum: bad arguments");
+  if (D <= 0 || D % 8) return fail(TMOE_ERR_UNSUPPORTED, "tmoe_weighted_sum: need D %% 8 == 0");
+  TMOE_TRY(launch_wsum(ys, inv_order, scores, T, k, D, mode, nullptr, nullptr, out, S(stream)),
+           "weighted_sum");
+  return TMOE_OK;
+}
+
+// ---------------------------------------------------------------- whole block
+
+namespace {
+
+struct BlockWs {
+  uint16_t* logits;
+  float* gate_logit;
+  int32_t* idx;
+  uint16_t* scores;
+  int32_t *order, *inv, *offsets, *tile_row, *tile_exp, *ntiles, *uexp, *ustart, *nuniq;
+  void* route_scratch;
+  // decode
+  uint16_t *x16p, *hhi, *hlo, *shhi, *shlo;
+  float *xsum, *h, *hs, *hsum, *shsum, *part, *part_sh;
+  // prefill
+  int8_t *xq, *hq;
+  float *xsc, *xrs, *hsc, *hrs;
+  uint16_t *h16p, *ys;
+  int32_t *s_tile_row, *s_tile_exp, *s_ntiles, *s_offsets;
+  uint16_t *sx16p, *sh16p, *ys_sh;  // sx16p/sxsum: fp16 operand copy of x (F16 GEMMs)
+  float *sxsum, *shrs;
+};
+
+int opt_min_tokens(const tmoe_options* o) { return (o && o->min_tokens > 0) ? o->min_tokens : 512; }
+int opt_down_int8(const tmoe_options* o) { return o ? (o->down_int8 != 0) : 1; }
+int opt_wsum(const tmoe_options* o) { return o ? o->wsum_mode : 0; }
+int opt_int8(const tmoe_options* o) { return o ? (o->int8_prefill != 0) : 1; }
+
+size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt, BlockWs* out) {
+  const int H = L->hidden, E = L->num_experts, k = L->top_k, I = L->moe_inter,
+            Is = L->shared_inter;
+  const int R = T * k, U = R < E ? R : E, G = H / 64;
+  const bool prefill = T >= opt_min_tokens(opt);
+  const int maxt = max_tiles(R, E);
+  BlockWs b{};
+  b.logits = c.take<uint16_t>((size_t)T * E);
+  b.gate_logit = c.take<float>(T > 0 ? T : 1);
+  b.idx = c.take<int32_t>(R);
+  b.scores = c.take<uint16_t>(R);
+  b.order = c.take<int32_t>(R);
+  b.inv = c.take<int32_t>(R);
+  b.offsets = c.take<int32_t>(E + 1);
+  b.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(R, E));
+  if (!prefill) {
+    b.uexp = c.take<int32_t>(U > 0 ? U : 1);
+    b.ustart = c.take<int32_t>(U + 1);
+    b.nuniq = c.take<int32_t>(1);
+    b.x16p = c.take<uint16_t>((size_t)T * H);
+    b.xsum = c.take<float>((size_t)T * G);
+    b.h = c.take<float>((size_t)R * I);
+    b.hhi = c.take<uint16_t>((size_t)R * I);
+    b.hlo = c.take<uint16_t>((size_t)R * I);
+    b.hsum = c.take<float>((size_t)R * (I / 64));
+    b.part = c.take<float>((size_t)R * H);
+    if (Is > 0) {
+      b.hs = c.take<float>((size_t)T * Is);
+      b.shhi = c.take<uint16_t>((size_t)T * Is);
+      b.shlo = c.take<uint16_t>((size_t)T * Is);
+      b.shsum = c.take<float>((size_t)T * (Is / 64));
+      b.part_sh = c.take<float>((size_t)T * H);
+    }
+  } else {
+    const bool i8 = opt_int8(opt), d8 = i8 && opt_down_int8(opt);
+    b.tile_row = c.take<int32_t>(maxt);
+    b.tile_exp = c.take<int32_t>(maxt);
+    b.ntiles = c.take<int32_t>(1);
+    if (i8) {
+      b.xq = c.take<int8_t>((size_t)T * H);
+      b.xsc = c.take<float>((size_t)T * G);
+      b.xrs = c.take<float>((size_t)T * G);
+    }
+    if (!i8 || Is > 0) {
+      b.sx16p = c.take<uint16_t>((size_t)T * H);
+      b.sxsum = c.take<float>((size_t)T * G);
+    }
+    if (d8) {
+      b.hq = c.take<int8_t>((size_t)R * I);
+      b.hsc = c.take<float>((size_t)R * (I / 64));
+    } else {
+      b.h16p = c.take<uint16_t>((size_t)R * I);
+    }
+    b.hrs = c.take<float>((size_t)R * (I / 64));
+    b.ys = c.take<uint16_t>((size_t)R * H);
+    if (Is > 0) {
+      const int st = (T + kTileM - 1) / kTileM;
+      b.s_tile_row = c.take<int32_t>(st);
+      b.s_tile_exp = c.take<int32_t>(st);
+      b.s_ntiles = c.take<int32_t>(1);
+      b.s_offsets = c.take<int32_t>(2);
+      b.sh16p = c.take<uint16_t>((size_t)T * Is);
+      b.shrs = c.take<float>((size_t)T * (Is / 64));
+      b.ys_sh = c.take<uint16_t>((size_t)T * H);
+    }
+  }
+  if (out) *out = b;
+  return c.off;
+}
+
+int check_layer(const tmoe_layer* L, int T, const tmoe_options* opt) {
+  if (!L) return fail(TMOE_ERR_INVALID, "tmoe_moe_forward: null layer");
+  const int H = L->hidden, E = L->num_experts, k = L->top_k, I = L->moe_inter,
+            Is = L->shared_inter;
+  if (T < 0 || I <= 0 || Is < 0) return fail(TMOE_ERR_INVALID, "tmoe_moe_forward: bad sizes");
+  if (int rc = check_router(T, H, E, k)) return rc;
+  if (!L->router_w || !L->gate_up_w || !L->gate_up_s || !L->gate_up_b || !L->down_w ||
+      !L->down_s || !L->down_b)
+    return fail(TMOE_ERR_INVALID, "tmoe_moe_forward: missing routed weights");
+  if (I % 64 || H % 128)
+    return fail(TMOE_ERR_UNSUPPORTED, "tmoe_moe_forward: need I %% 64 == 0 and H %% 128 == 0 (H=%d I=%d)", H, I);
+  if (Is > 0) {
+    if (!L->shared_gate_up_w || !L->shared_gate_up_s || !L->shared_gate_up_b ||
+        !L->shared_down_w || !L->shared_down_s || !L->shared_down_b || !L->shared_gate_w)
+      return fail(TMOE_ERR_INVALID, "tmoe_moe_forward: missing shared-expert weights");
+    if (Is % 64) return fail(TMOE_ERR_UNSUPPORTED, "tmoe_moe_forward: need Is %% 64 == 0");
+  }
+  if (T >= opt_min_tokens(opt)) {
+    if (!L->gate_up_st || !L->gate_up_bt || !L->down_st || !L->down_bt)
+      return fail(TMOE_ERR_INVALID, "tmoe_moe_forward: the int8 path needs the prepared tables");
+    if (Is > 0 && (!L->shared_gate_up_st || !L->shared_gate_up_bt || !L->shared_down_st ||
+                   !L->shared_down_bt))
+      return fail(TMOE_ERR_INVALID, "tmoe_moe_forward: the shared expert needs its prepared tables");
+  }
+  return TMOE_OK;
+}
+
+}  // namespace
+
+size_t tmoe_moe_workspace_size(const tmoe_layer* L, int T, const tmoe_options* opt) {
+  if (!L || T < 0) return 0;
+  Carve c(nullptr);
+  return carve_block(c, L, T, opt, nullptr);
+}
+
+int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_options* opt,
+                     void* ws, size_t ws_bytes, uint16_t* y, int32_t* idx_out,
+                     uint16_t* scores_out, void* stream) {
+  if (int rc = check_layer(L, T, opt)) return rc;
+  if (!x || !y) return fail(TMOE_ERR_INVALID, "tmoe_moe_forward: null x or y");
+  const size_t need = tmoe_moe_workspace_size(L, T, opt);
+  if (!ws || ws_bytes < need)
+    return fail(TMOE_ERR_WORKSPACE, "tmoe_moe_forward: workspace %zu < %zu bytes", ws_bytes, need);
+  if (T == 0) return TMOE_OK;
+  const int H = L->hidden, E = L->num_experts, k = L->top_k, I = L->moe_inter,
+            Is = L->shared_inter;
+  const int R = T * k, U = R < E ? R : E, G = H / 64;
+  const bool prefill = T >= opt_min_tokens(opt);
+  const int maxt = max_tiles(R, E);
+  Carve c(ws);
+  BlockWs b;
+  carve_block(c, L, T, opt, &b);
+  int32_t* idx = idx_out ? idx_out : b.idx;
+  uint16_t* scores = scores_out ? scores_out : b.scores;
+  cudaStream_t s = S(stream);
+
+  TMOE_TRY(launch_router_logits(x, L->router_w, Is > 0 ? L->shared_gate_w : nullptr, T, H, E,
+                                b.logits, b.gate_logit, s),
+           "router_logits");
+  TMOE_TRY(launch_router_topk(b.logits, T, E, k, idx, scores, nullptr, s), "router_topk");
+  RoutePlan p{};
+  p.order = b.order;
+  p.inv = b.inv;
+  p.offsets = b.offsets;
+
+  if (!prefill) {
+    p.uexp = b.uexp;
+    p.ustart = b.ustart;
+    p.nuniq = b.nuniq;
+    TMOE_TRY(launch_route_plan(idx, R, E, kTileM, 1, p, b.route_scratch, s), "route_plan");
+    TMOE_TRY(launch_prep_x(x, T, H, b.x16p, b.xsum, G, 1, s), "prep_x");
+    GemvParams q{};
+    q.bh = b.x16p;
+    q.bsum = b.xsum;
+    q.K = H;
+    q.W = L->gate_up_w;
+    q.S = L->gate_up_s;
+    q.B = L->gate_up_b;
+    q.N = 2 * I;
+    if (Is > 0) {
+      q.bh_sh = b.x16p;
+      q.bsum_sh = b.xsum;
+      q.K_sh = H;
+      q.Wsh = L->shared_gate_up_w;
+      q.Ssh = L->shared_gate_up_s;
+      q.Bsh = L->shared_gate_up_b;
+      q.Nsh = 2 * Is;
+      q.out_sh = b.hs;
+    }
+    q.uexp = b.uexp;
+    q.ustart = b.ustart;
+    q.nuniq = b.nuniq;
+    q.order = b.order;
+    q.umax = U;
+    q.col_div = k;
+    q.nsh = T;
+    q.swiglu = 1;
+    q.out = b.h;
+    TMOE_TRY(launch_gemv_tc(q, s), "gemv_gate_up");
+    TMOE_TRY(launch_prep_h(b.h, R, I, b.hhi, b.hlo, b.hsum, s), "prep_h");
+    if (Is > 0) TMOE_TRY(launch_prep_h(b.hs, T, Is, b.shhi, b.shlo, b.shsum, s), "prep_h_shared");
+    GemvParams d{};
+    d.bh = b.hhi;
+    d.bl = b.hlo;
+    d.bsum = b.hsum;
+    d.K = I;
+    d.W = L->down_w;
+    d.S = L->down_s;
+    d.B = L->down_b;
+    d.N = H;
+    if (Is > 0) {
+      d.bh_sh = b.shhi;
+      d.bl_sh = b.shlo;
+      d.bsum_sh = b.shsum;
+      d.K_sh = Is;
+      d.Wsh = L->shared_down_w;
+      d.Ssh = L->shared_down_s;
+      d.Bsh = L->shared_down_b;
+      d.Nsh = H;
+      d.out_sh = b.part_sh;
+    }
+    d.uexp = b.uexp;
+    d.ustart = b.ustart;
+    d.nuniq = b.nuniq;
+    d.order = b.order;
+    d.umax = U;
+    d.col_div = 1;
+    d.nsh = T;
+    d.swiglu = 0;
+    d.out = b.part;
+    TMOE_TRY(launch_gemv_tc(d, s), "gemv_down");
+    TMOE_TRY(launch_decode_combine(b.part, scores, nullptr, T, k, H, Is > 0 ? b.part_sh : nullptr,
+                                   b.gate_logit, y, s),
+             "combine");
+    return TMOE_OK;
+  }
+
+  // ---- prefill: expert-sorted grouped GEMMs (int8 or stock bf16 gate_up)
+  p.tile_row = b.tile_row;
+  p.tile_exp = b.tile_exp;
+  p.ntiles = b.ntiles;
+  TMOE_TRY(launch_route_plan(idx, R, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
+  const bool i8 = opt_int8(opt);
+  const bool d8 = i8 && opt_down_int8(opt);
+  if (i8) TMOE_TRY(launch_quantize_rows(x, T, H, b.xq, b.xsc, b.xrs, s), "quantize_rows");
+  if (!i8 || Is > 0) TMOE_TRY(launch_prep_x(x, T, H, b.sx16p, b.sxsum, G, 1, s), "prep_x");
+  GemmParams g{};
+  g.A = i8 ? static_cast<const void*>(b.xq) : static_cast<const void*>(b.sx16p);
+  g.asc = b.xsc;
+  g.ars = i8 ? b.xrs : b.sxsum;
+  g.s_r = G;
+  g.s_g = 1;
+  g.a_rows = b.order;
+  g.a_div = k;
+  g.W = L->gate_up_w;
+  g.st = L->gate_up_st;
+  g.bt = L->gate_up_bt;
+  g.tile_row = b.tile_row;
+  g.tile_exp = b.tile_exp;
+  g.ntiles = b.ntiles;
+  g.offsets = b.offsets;
+  g.K = H;
+  g.N = 2 * I;
+  g.hq = b.hq;
+  g.hsc = b.hsc;
+  g.hrs = b.hrs;
+  g.Rpad_h = R;
+  g.h16p = b.h16p;
+  TMOE_TRY(launch_gemm_grouped(i8, d8 ? kEpiSwigluQ8 : kEpiSwigluH16, g, maxt, s), "gemm_gate_up");
+  GemmParams dn{};
+  dn.A = d8 ? static_cast<const void*>(b.hq) : static_cast<const void*>(b.h16p);
+  dn.asc = b.hsc;
+  dn.ars = b.hrs;
+  dn.s_r = 1;
+  dn.s_g = R;
+  dn.W = L->down_w;
+  dn.st = L->down_st;
+  dn.bt = L->down_bt;
+  dn.tile_row = b.tile_row;
+  dn.tile_exp = b.tile_exp;
+  dn.ntiles = b.ntiles;
+  dn.offsets = b.offsets;
+  dn.K = I;
+  dn.N = H;
+  dn.Y = b.ys;
+  TMOE_TRY(launch_gemm_grouped(d8, kEpiStore, dn, maxt, s), "gemm_down");
+  if (Is > 0) {
+    const int st = (T + kTileM - 1) / kTileM;
+    TMOE_TRY(launch_dense_tiles(T, kTileM, b.s_tile_row, b.s_tile_exp, b.s_ntiles, b.s_offsets, s),
+             "dense_tiles");
+    GemmParams sg{};
+    sg.A = b.sx16p;
+    sg.ars = b.sxsum;
+    sg.s_r = G;
+    sg.s_g = 1;
+    sg.W = L->shared_gate_up_w;
+    sg.st = L->shared_gate_up_st;
+    sg.bt = L->shared_gate_up_bt;
+    sg.tile_row = b.s_tile_row;
+    sg.tile_exp = b.s_tile_exp;
+    sg.ntiles = b.s_ntiles;
+    sg.offsets = b.s_offsets;
+    sg.K = H;
+    sg.N = 2 * Is;
+    sg.hrs = b.shrs;
+    sg.Rpad_h = T;
+    sg.h16p = b.sh16p;
+    TMOE_TRY(launch_gemm_grouped(false, kEpiSwigluH16, sg, st, s), "gemm_shared_gate_up");
+    GemmParams sd{};
+    sd.A = b.sh16p;
+    sd.ars = b.shrs;
+    sd.s_r = 1;
+    sd.s_g = T;
+    sd.W = L->shared_down_w;
+    sd.st = L->shared_down_st;
+    sd.bt = L->shared_down_bt;
+    sd.tile_row = b.s_tile_row;
+    sd.tile_exp = b.s_tile_exp;
+    sd.ntiles = b.s_ntiles;
+    sd.offsets = b.s_offsets;
+    sd.K = Is;
+    sd.N = H;
+    sd.Y = b.ys_sh;
+    TMOE_TRY(launch_gemm_grouped(false, kEpiStore, sd, st, s), "gemm_shared_down");
+  }
+  TMOE_TRY(launch_wsum(b.ys, b.inv, scores, T, k, H, opt_wsum(opt), Is > 0 ? b.ys_sh : nullptr,
+                       b.gate_logit, y, s),
+           "weighted_sum");
+  return TMOE_OK;
+}
+
+}  // extern "C"

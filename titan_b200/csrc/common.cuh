@@ -1,0 +1,141 @@
+// Shared device helpers for the titan_b200 MoE kernels (sm_100a).
+//
+// Canonical arithmetic: wherever the reference leaves an order or a rounding
+// unspecified, these kernels evaluate one fixed sequence of IEEE binary32
+// operations (explicit __fmaf_rn / __fadd_rn / __fmul_rn / __fdiv_rn, so the
+// compiler cannot contract or reassociate them).  The sequences are:
+//   * bf16 dot product (router Linear): 8 partials; the 8-element chunk c
+//     (elements 8c..8c+7) feeds partial c mod 8 with fma in ascending order,
+//     then the xor tree over offsets 4,2,1 (8 lanes of a warp, __shfl_xor);
+//   * softmax denominator: 32 lane partials over e = 32c + l, xor butterfly
+//     over offsets 16,8,4,2,1;
+//   * exp: Cody-Waite reduction + degree-7 Taylor polynomial, 2^n applied in
+//     two exact steps;
+//   * group sum of the activation quantiser: pair sums, then the butterfly.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define TMOE_DEV __device__ __forceinline__
+
+namespace tmoe {
+
+constexpr int kGroup = 64;   // affine quantisation group (MLX group_size=64)
+
+TMOE_DEV float bf2f(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
+
+TMOE_DEV uint16_t f2bf(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+TMOE_DEV float bfround(float f) { return bf2f(f2bf(f)); }
+
+// e^x, the canonical sequence (see file header).
+TMOE_DEV float cexp(float x) {
+  if (x != x) return x;
+  if (x > 88.7228393554688f) return __int_as_float(0x7f800000);
+  if (x < -103.972084045410f) return 0.0f;
+  float n = rintf(__fmul_rn(x, 1.44269504088896341f));
+  float r = __fmaf_rn(-n, 0.693145751953125f, x);
+  r = __fmaf_rn(-n, 1.42860682030941723e-06f, r);
+  float p = 1.98412698412698413e-4f;
+  p = __fmaf_rn(p, r, 1.38888888888888889e-3f);
+  p = __fmaf_rn(p, r, 8.33333333333333333e-3f);
+  p = __fmaf_rn(p, r, 4.16666666666666667e-2f);
+  p = __fmaf_rn(p, r, 1.66666666666666667e-1f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  int ni = (int)n;
+  int n1 = ni / 2;
+  int n2 = ni - n1;
+  float s1 = __int_as_float((n1 + 127) << 23);
+  float s2 = __int_as_float((n2 + 127) << 23);
+  return __fmul_rn(__fmul_rn(p, s1), s2);
+}
+
+TMOE_DEV float csigmoid(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, cexp(-x)));
+}
+
+// SwiGLU with the reference's bf16 rounding after each op:
+// sg = bf16(sigmoid(g)); a = bf16(g*sg); h = bf16(a*u).
+TMOE_DEV float swiglu_bf16(float g, float u) {
+  float sg = bfround(csigmoid(g));
+  float a = bfround(__fmul_rn(g, sg));
+  return bfround(__fmul_rn(a, u));
+}
+
+// fp32 SiLU(g)*u of the decode path (decode-fusion semantics).
+TMOE_DEV float silu_mul_f32(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, cexp(-g))), u);
+}
+
+TMOE_DEV float warp_butterfly_sum(float v) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
+TMOE_DEV float warp_max(float v) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
+// The canonical 32-way butterfly evaluated by one thread over 32 values held
+// in memory (lane l's value at p[l*stride]); same tree as warp_butterfly_sum.
+TMOE_DEV float serial_butterfly32(const float* p, int stride) {
+  float a[16];
+#pragma unroll
+  for (int l = 0; l < 16; ++l) a[l] = __fadd_rn(p[l * stride], p[(l + 16) * stride]);
+#pragma unroll
+  for (int l = 0; l < 8; ++l) a[l] = __fadd_rn(a[l], a[l + 8]);
+#pragma unroll
+  for (int l = 0; l < 4; ++l) a[l] = __fadd_rn(a[l], a[l + 4]);
+#pragma unroll
+  for (int l = 0; l < 2; ++l) a[l] = __fadd_rn(a[l], a[l + 2]);
+  return __fadd_rn(a[0], a[1]);
+}
+
+// 8 packed bf16 (one 16-byte load) -> float.
+TMOE_DEV void unpack8_bf16(uint4 v, float* f) {
+  f[0] = __uint_as_float(v.x << 16); f[1] = __uint_as_float(v.x & 0xffff0000u);
+  f[2] = __uint_as_float(v.y << 16); f[3] = __uint_as_float(v.y & 0xffff0000u);
+  f[4] = __uint_as_float(v.z << 16); f[5] = __uint_as_float(v.z & 0xffff0000u);
+  f[6] = __uint_as_float(v.w << 16); f[7] = __uint_as_float(v.w & 0xffff0000u);
+}
+
+TMOE_DEV uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+TMOE_DEV void cp_async16(void* smem, const void* gmem) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem));
+}
+TMOE_DEV void cp_async16_zfill(void* smem, const void* gmem, bool valid) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  int src_bytes = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
+TMOE_DEV void cp_async8(void* smem, const void* gmem) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(s), "l"(gmem));
+}
+TMOE_DEV void cp_async4(void* smem, const void* gmem) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem));
+}
+TMOE_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+TMOE_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
+
+}  // namespace tmoe

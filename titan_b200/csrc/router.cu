@@ -1,0 +1,261 @@
+// Router: logits = bf16(x @ Wr^T) (canonical 8-partial order), softmax in
+// fp32 -> bf16 probabilities, top-k with the lowest index winning ties, and
+// bf16 renormalised scores.  Follows qwen3_5_moe/language.py:65-71 and the
+// fused router of engine/patches/decode-fusion/fused_kernels.py:234-327.
+//
+// Two logits kernels compute bit-identical results:
+//   * router_logits_gemv  — decode shapes: 4 experts per warp (8 lanes = the
+//     8 canonical partials each), every weight row streamed once from HBM;
+//   * router_logits_tiled — prefill shapes: a 64-token x 32-expert CTA tile,
+//     x and W staged through shared memory by cp.async, 64 accumulators per
+//     thread (8 tokens x 8 experts) for one canonical partial.
+// The optional shared-expert gate row wg is evaluated as expert row E; its
+// fp32 logit goes to gate_logit[T].
+#include "common.cuh"
+#include "tmoe_internal.h"
+
+namespace tmoe {
+
+TMOE_DEV float tree8_sum(float v) {
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return v;
+}
+
+__global__ void __launch_bounds__(64) router_logits_gemv(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
+    const uint16_t* __restrict__ wg, int T, int H, int E, uint16_t* __restrict__ logits,
+    float* __restrict__ gate_logit) {
+  const int lane = threadIdx.x & 31;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int p = lane & 7;
+  const int e = warp * 4 + (lane >> 3);
+  const int nrows = E + (wg ? 1 : 0);
+  const bool valid = e < nrows;
+  const uint16_t* row = valid ? ((e < E) ? wr + (size_t)e * H : wg) : wr;
+  const int nch = H >> 3;
+  for (int t0 = 0; t0 < T; t0 += 8) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll 2
+    for (int c = p; c < nch; c += 8) {
+      float wf[8];
+      uint4 wv = valid ? ldg_nc_v4(row + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
+      unpack8_bf16(wv, wf);
+#pragma unroll
+      for (int tt = 0; tt < 8; ++tt) {
+        if (t0 + tt < T) {
+          float xf[8];
+          unpack8_bf16(__ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + tt) * H + c * 8)), xf);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) acc[tt] = __fmaf_rn(xf[u], wf[u], acc[tt]);
+        }
+      }
+    }
+#pragma unroll
+    for (int tt = 0; tt < 8; ++tt) {
+      float s = tree8_sum(acc[tt]);
+      if (valid && p == tt && t0 + tt < T) {
+        if (e < E)
+          logits[(size_t)(t0 + tt) * E + e] = f2bf(s);
+        else
+          gate_logit[t0 + tt] = s;
+      }
+    }
+  }
+}
+
+// CTA tile: 64 tokens x 32 experts, K step 64 elements (8 chunks).
+// Thread roles: p = lane & 7 is the canonical partial (chunk p of each step),
+// gid = warp*4 + (lane>>3) in [0,32): gt = gid & 7 selects tokens
+// tt*8 + gt, ge = gid >> 3 selects experts ee*4 + ge (conflict-free smem).
+__global__ void __launch_bounds__(256) router_logits_tiled(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
+    const uint16_t* __restrict__ wg, int T, int H, int E, uint16_t* __restrict__ logits,
+    float* __restrict__ gate_logit) {
+  __shared__ uint4 xs[2][64][8];
+  __shared__ uint4 ws[2][32][8];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int p = lane & 7;
+  const int gid = warp * 4 + (lane >> 3);
+  const int gt = gid & 7, ge = gid >> 3;
+  const int tok0 = blockIdx.x * 64, exp0 = blockIdx.y * 32;
+  const int nrows = E + (wg ? 1 : 0);
+  const int nk = H / 64;
+
+  auto load_stage = [&](int stage, int ks) {
+    for (int i = tid; i < 768; i += 256) {
+      if (i < 512) {
+        int r = i >> 3, ch = i & 7;
+        int t = tok0 + r;
+        bool ok = t < T;
+        const uint16_t* src = x + (size_t)(ok ? t : 0) * H + ks * 64 + ch * 8;
+        cp_async16_zfill(&xs[stage][r][ch], src, ok);
+      } else {
+        int j = i - 512;
+        int r = j >> 3, ch = j & 7;
+        int e = exp0 + r;
+        bool ok = e < nrows;
+        const uint16_t* rowp = ok ? ((e < E) ? wr + (size_t)e * H : wg) : wr;
+        cp_async16_zfill(&ws[stage][r][ch], rowp + ks * 64 + ch * 8, ok);
+      }
+    }
+    cp_async_commit();
+  };
+
+  float acc[8][8];
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) acc[a][b] = 0.0f;
+
+  load_stage(0, 0);
+  for (int ks = 0; ks < nk; ++ks) {
+    if (ks + 1 < nk) {
+      load_stage((ks + 1) & 1, ks + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int st = ks & 1;
+    float xf[8][8];
+#pragma unroll
+    for (int tt = 0; tt < 8; ++tt) unpack8_bf16(xs[st][tt * 8 + gt][p], xf[tt]);
+#pragma unroll
+    for (int ee = 0; ee < 8; ++ee) {
+      float wf[8];
+      unpack8_bf16(ws[st][ee * 4 + ge][p], wf);
+#pragma unroll
+      for (int tt = 0; tt < 8; ++tt)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[tt][ee] = __fmaf_rn(xf[tt][u], wf[u], acc[tt][ee]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int tt = 0; tt < 8; ++tt)
+#pragma unroll
+    for (int ee = 0; ee < 8; ++ee) acc[tt][ee] = tree8_sum(acc[tt][ee]);
+  // lane p stores token tt = p of its group.
+#pragma unroll
+  for (int tt = 0; tt < 8; ++tt) {
+    if (tt != p) continue;
+    int t = tok0 + tt * 8 + gt;
+    if (t >= T) continue;
+#pragma unroll
+    for (int ee = 0; ee < 8; ++ee) {
+      int e = exp0 + ee * 4 + ge;
+      if (e < E)
+        logits[(size_t)t * E + e] = f2bf(acc[tt][ee]);
+      else if (e == E && wg)
+        gate_logit[t] = acc[tt][ee];
+    }
+  }
+}
+
+// One warp per token: lane l holds experts e = 32c + l.
+template <int PER>
+__global__ void __launch_bounds__(128) router_topk_kernel(
+    const uint16_t* __restrict__ logits, int T, int E, int k, int32_t* __restrict__ idx,
+    uint16_t* __restrict__ scores, uint16_t* __restrict__ probs_out) {
+  const int lane = threadIdx.x & 31;
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t >= T) return;
+  float lv[PER];
+  float m = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int c = 0; c < PER; ++c) {
+    int e = 32 * c + lane;
+    lv[c] = (e < E) ? bf2f(logits[(size_t)t * E + e]) : -__int_as_float(0x7f800000);
+    m = fmaxf(m, lv[c]);
+  }
+  m = warp_max(m);
+  float ex[PER];
+  float part = 0.0f;
+#pragma unroll
+  for (int c = 0; c < PER; ++c) {
+    int e = 32 * c + lane;
+    if (e < E) {
+      ex[c] = cexp(__fsub_rn(lv[c], m));
+      part = __fadd_rn(part, ex[c]);
+    } else {
+      ex[c] = 0.0f;
+    }
+  }
+  const float sum = warp_butterfly_sum(part);
+  const float inv = __fdiv_rn(1.0f, sum);
+  uint32_t pb[PER];
+#pragma unroll
+  for (int c = 0; c < PER; ++c) {
+    pb[c] = f2bf(__fmul_rn(ex[c], inv));
+    int e = 32 * c + lane;
+    if (probs_out && e < E) probs_out[(size_t)t * E + e] = (uint16_t)pb[c];
+  }
+  uint32_t taken = 0;
+  float ssum = 0.0f;
+  uint32_t my_p = 0;
+  int my_e = 0;
+  for (int j = 0; j < k; ++j) {
+    uint32_t best = 0;
+#pragma unroll
+    for (int c = 0; c < PER; ++c) {
+      int e = 32 * c + lane;
+      if (e < E && !((taken >> c) & 1u)) {
+        uint32_t key = (pb[c] << 16) | (uint32_t)(0xffff - e);
+        best = key > best ? key : best;
+      }
+    }
+    const uint32_t win = __reduce_max_sync(0xffffffffu, best);
+    const int e_sel = 0xffff - (int)(win & 0xffffu);
+    const uint32_t p_sel = win >> 16;
+    if ((e_sel & 31) == lane) taken |= 1u << (e_sel >> 5);
+    ssum = __fadd_rn(ssum, bf2f((uint16_t)p_sel));
+    if (lane == j) {
+      my_p = p_sel;
+      my_e = e_sel;
+    }
+  }
+  const float sb = bfround(ssum);
+  if (lane < k) {
+    idx[(size_t)t * k + lane] = my_e;
+    scores[(size_t)t * k + lane] = f2bf(__fdiv_rn(bf2f((uint16_t)my_p), sb));
+  }
+}
+
+cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* wg, int T,
+                                 int H, int E, uint16_t* logits, float* gate_logit,
+                                 cudaStream_t s) {
+  const int nrows = E + (wg ? 1 : 0);
+  if (T <= 32) {
+    const int warps = (nrows + 3) / 4;
+    const int blocks = (warps + 1) / 2;
+    router_logits_gemv<<<blocks, 64, 0, s>>>(x, wr, wg, T, H, E, logits, gate_logit);
+  } else {
+    dim3 grid((T + 63) / 64, (nrows + 31) / 32);
+    router_logits_tiled<<<grid, 256, 0, s>>>(x, wr, wg, T, H, E, logits, gate_logit);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_router_topk(const uint16_t* logits, int T, int E, int k, int32_t* idx,
+                               uint16_t* scores, uint16_t* probs_out, cudaStream_t s) {
+  const int blocks = (T + 3) / 4;
+  const int per = (E + 31) / 32;
+  if (per <= 2)
+    router_topk_kernel<2><<<blocks, 128, 0, s>>>(logits, T, E, k, idx, scores, probs_out);
+  else if (per <= 4)
+    router_topk_kernel<4><<<blocks, 128, 0, s>>>(logits, T, E, k, idx, scores, probs_out);
+  else if (per <= 8)
+    router_topk_kernel<8><<<blocks, 128, 0, s>>>(logits, T, E, k, idx, scores, probs_out);
+  else if (per <= 16)
+    router_topk_kernel<16><<<blocks, 128, 0, s>>>(logits, T, E, k, idx, scores, probs_out);
+  else
+    router_topk_kernel<32><<<blocks, 128, 0, s>>>(logits, T, E, k, idx, scores, probs_out);
+  return cudaGetLastError();
+}
+
+}  // namespace tmoe

@@ -1,0 +1,115 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tmoe {
+
+constexpr int kSmallRows = 2048;   // route plans up to this many rows use one CTA
+constexpr int kTileM = 128;        // grouped-GEMM row tile
+constexpr int kEpiStore = 0;       // bf16 store
+constexpr int kEpiSwigluQ8 = 1;    // SwiGLU + int8 requantisation of h
+constexpr int kEpiSwigluH16 = 2;   // SwiGLU + fp16 operand copy of h
+
+struct RoutePlan {
+  int32_t* order;       // [R] sorted row -> flat (token*k + slot)
+  int32_t* inv;         // [R] flat -> sorted row
+  int32_t* offsets;     // [E+1]
+  int32_t* sorted_ids;  // [R] expert of each sorted row (optional)
+  int32_t* tile_row;    // [maxt] (optional)
+  int32_t* tile_exp;    // [maxt]
+  int32_t* ntiles;      // [1]
+  int32_t* uexp;        // [min(R,E)] distinct experts, ascending (optional)
+  int32_t* ustart;      // [min(R,E)+1] first sorted row of each distinct expert, then R
+  int32_t* nuniq;       // [1]
+};
+
+struct GemmParams {
+  const void* A;        // I8: int8 codes [rows][K]; F16: fp16 operand layout [rows][K]
+  const float* asc;     // row scale (I8 only), element (row, g) at row*s_r + g*s_g
+  const float* ars;     // exact group sum of the unquantised row, same strides
+  long long s_r, s_g;
+  const int32_t* a_rows;  // optional: sorted row r reads A row a_rows[r] / a_div
+  int a_div;
+  const uint32_t* W;    // [E][N][K/8] packed int4
+  const uint16_t* st;   // [E][G][N] bf16 scales
+  const uint16_t* bt;   // [E][G][N] bf16 biases
+  const int32_t* tile_row;
+  const int32_t* tile_exp;
+  const int32_t* ntiles;
+  const int32_t* offsets;  // [E+1]
+  int K, N;             // N = weight rows (2I for the SwiGLU epilogues)
+  uint16_t* Y;          // store: bf16 [R][N]
+  const int32_t* y_rows;  // optional: sorted row r is stored at Y row y_rows[r]
+  int8_t* hq;           // SwiGLU-Q8: int8 h [Rpad][N/2]
+  float* hsc;           // [N/128][Rpad_h]
+  float* hrs;           // [N/128][Rpad_h]
+  int Rpad_h;
+  uint16_t* h16p;       // SwiGLU-H16: fp16 operand layout [Rpad][N/2]
+  uint16_t* hbf;        // optional bf16 h [R][N/2]
+};
+
+struct GemvParams {
+  const uint16_t* bh;   // activation hi part, fp16 operand layout [rows][K]
+  const uint16_t* bl;   // lo part or null
+  const float* bsum;    // [rows][K/64] group sums
+  int K;
+  const uint32_t* W;    // routed [E][N][K/8]
+  const uint16_t* S;    // [E][N][K/64]
+  const uint16_t* B;
+  int N;
+  const uint16_t* bh_sh;  // shared-expert activation (rows t), same layouts
+  const uint16_t* bl_sh;
+  const float* bsum_sh;
+  int K_sh;
+  const uint32_t* Wsh;  // shared expert [Nsh][K_sh/8] or null
+  const uint16_t* Ssh;
+  const uint16_t* Bsh;
+  int Nsh;
+  const int32_t* uexp;
+  const int32_t* ustart;
+  const int32_t* nuniq;
+  const int32_t* order;
+  int umax;
+  int col_div;          // activation row of sorted column p: order[p] / col_div
+  int nsh;              // shared expert columns (tokens)
+  int swiglu;
+  float* out;           // routed output rows order[p] (fp32)
+  float* out_sh;        // shared output rows t
+  uint16_t* outb;       // plain mode: bf16 output instead of fp32 (routed rows)
+};
+
+cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* wg, int T,
+                                 int H, int E, uint16_t* logits, float* gate_logit, cudaStream_t s);
+cudaError_t launch_router_topk(const uint16_t* logits, int T, int E, int k, int32_t* idx,
+                               uint16_t* scores, uint16_t* probs_out, cudaStream_t s);
+size_t route_plan_scratch_bytes(int R, int E);
+cudaError_t launch_route_plan(const int32_t* idx, int R, int E, int tile_m, int maxt,
+                              const RoutePlan& plan, void* scratch, cudaStream_t s);
+cudaError_t launch_quantize_rows(const uint16_t* x, int R, int K, int8_t* xq, float* xsc,
+                                 float* xrs, cudaStream_t s);
+cudaError_t launch_gemm_grouped(bool int8, int epi, const GemmParams& P, int maxt, cudaStream_t s);
+cudaError_t launch_to_f16p(const uint16_t* x, long long n, uint16_t* y, cudaStream_t s);
+cudaError_t launch_prep_x(const uint16_t* x, int R, int K, uint16_t* x16p, float* xsum,
+                          long long sum_sm, long long sum_sg, cudaStream_t s);
+cudaError_t launch_prep_h(const float* h, int R, int K, uint16_t* hhi, uint16_t* hlo, float* hsum,
+                          cudaStream_t s);
+cudaError_t launch_gemv_tc(const GemvParams& P, cudaStream_t s);
+cudaError_t launch_decode_combine(const float* part, const uint16_t* scores,
+                                  const float* scores_f32, int T, int k, int D,
+                                  const float* shared, const float* gate_logit, uint16_t* y,
+                                  cudaStream_t s);
+cudaError_t launch_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
+                        int D, int mode, const uint16_t* sh, const float* gate_logit, uint16_t* out,
+                        cudaStream_t s);
+cudaError_t launch_swiglu(const uint16_t* gu, int R, int I, uint16_t* h, cudaStream_t s);
+cudaError_t launch_affine_quantize(const float* w, long long rows, int K, uint32_t* wq,
+                                   uint16_t* scales, uint16_t* biases, cudaStream_t s);
+cudaError_t launch_prepare_tables(const uint16_t* scales, const uint16_t* biases, int E, int N, int G,
+                                  uint16_t* st, uint16_t* bt, cudaStream_t s);
+cudaError_t launch_qsum(const uint32_t* w, int E, int N, int K, uint16_t* qsum, cudaStream_t s);
+cudaError_t launch_dense_tiles(int R, int tile_m, int32_t* tile_row, int32_t* tile_exp,
+                               int32_t* ntiles, int32_t* offsets, cudaStream_t s);
+
+}  // namespace tmoe

@@ -1,0 +1,159 @@
+"""The sparse MoE block: router, routed SwitchGLU, weighted sum, shared expert.
+
+``SparseMoeBlock`` mirrors Qwen3_5MoeSparseMoeBlock
+(titan/adapters/mlx/vendor/mlx_vlm/models/qwen3_5_moe/language.py:44-91):
+
+  gates  = softmax(x @ Wr^T); top-k; renormalise
+  y      = SwitchGLU(x, inds) weighted by the scores
+  y     += sigmoid(x @ wg^T) * shared_expert(x)
+
+``forward`` runs the whole block through one C-ABI call
+(``tmoe_moe_forward``): the canonical router, the routing plan, then either
+the decode-shaped tensor-core GEMVs (T < min_tokens) or the expert-sorted
+grouped GEMMs (int8 gate_up when the overlay is installed, the stock bf16
+semantics otherwise), and the fused unsort + weighted sum + shared add.
+``forward_modular`` runs the same block op by op through the reference's
+operator surface (router_topk, SwitchGLU -> gather_qmm, weighted_sum).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import torch
+from torch import nn
+
+from . import _lib, ops, patch
+from .switch_layers import QuantizedSwitchLinear, SwitchGLU
+
+
+class SharedExpert(nn.Module):
+    """Qwen3_5MLP (qwen3_5/language.py:1590-1601) with the gate and up
+    projections stored fused, gate rows first: weight [2Is, H/8]."""
+
+    def __init__(self, hidden: int, inter: int, device=None, init: bool = True,
+                 weight_std: float | None = None):
+        super().__init__()
+        self.gate_up_proj = QuantizedSwitchLinear(hidden, 2 * inter, 1, device=device, init=init,
+                                                  weight_std=weight_std)
+        self.down_proj = QuantizedSwitchLinear(inter, hidden, 1, device=device, init=init,
+                                               weight_std=weight_std)
+
+    def forward(self, x):
+        T = x.shape[0]
+        zeros = torch.zeros(T, dtype=torch.int32, device=x.device)
+        gu = self.gate_up_proj(x.unsqueeze(-2), zeros).squeeze(-2)
+        g, u = gu.chunk(2, dim=-1)
+        h = ops.swiglu(u.contiguous(), g.contiguous())
+        return self.down_proj(h.unsqueeze(-2), zeros).squeeze(-2)
+
+
+class SparseMoeBlock(nn.Module):
+    def __init__(self, hidden: int, num_experts: int, top_k: int, moe_inter: int,
+                 shared_inter: int = 0, device=None, init: bool = True, router_std: float = 0.02,
+                 weight_std: float | None = None):
+        super().__init__()
+        device = torch.device(device or "cuda")
+        self.hidden, self.num_experts, self.top_k = hidden, num_experts, top_k
+        self.moe_inter, self.shared_inter = moe_inter, shared_inter
+        gate = torch.randn(num_experts, hidden, device=device) * router_std if init else \
+            torch.zeros(num_experts, hidden, device=device)
+        self.register_buffer("gate_weight", gate.to(torch.bfloat16))
+        self.switch_mlp = SwitchGLU(hidden, moe_inter, num_experts, device=device, init=init,
+                                    weight_std=weight_std)
+        if shared_inter:
+            self.shared_expert = SharedExpert(hidden, shared_inter, device=device, init=init,
+                                              weight_std=weight_std)
+            sg = torch.randn(1, hidden, device=device) * 0.02 if init else \
+                torch.zeros(1, hidden, device=device)
+            self.register_buffer("shared_expert_gate_weight", sg.to(torch.bfloat16))
+        else:
+            self.shared_expert = None
+            self.shared_expert_gate_weight = None
+        self._layer = None
+        self._tables = None
+
+    # ------------------------------------------------------------ weights
+    def prepare(self) -> int:
+        """Build the transposed scale/bias tables of every projection (the
+        reference's warmup(), patch.py:179-198).  Returns their bytes."""
+        self._layer = None
+        mods = [self.switch_mlp.gate_up_proj, self.switch_mlp.down_proj]
+        if self.shared_expert is not None:
+            mods += [self.shared_expert.gate_up_proj, self.shared_expert.down_proj]
+        self._tables = [ops.cached_tables(m.weight, m.scales, m.biases) for m in mods]
+        return sum(t.nbytes for t in self._tables)
+
+    def layer_struct(self) -> _lib.Layer:
+        if self._layer is not None:
+            return self._layer
+        if self._tables is None:
+            self.prepare()
+        sm = self.switch_mlp
+        L = _lib.Layer()
+        L.hidden, L.num_experts, L.top_k = self.hidden, self.num_experts, self.top_k
+        L.moe_inter, L.shared_inter = self.moe_inter, self.shared_inter
+        L.router_w = self.gate_weight.data_ptr()
+        L.gate_up_w, L.gate_up_s, L.gate_up_b = (sm.gate_up_proj.weight.data_ptr(),
+                                                 sm.gate_up_proj.scales.data_ptr(),
+                                                 sm.gate_up_proj.biases.data_ptr())
+        L.down_w, L.down_s, L.down_b = (sm.down_proj.weight.data_ptr(),
+                                        sm.down_proj.scales.data_ptr(),
+                                        sm.down_proj.biases.data_ptr())
+        t = self._tables
+        L.gate_up_st, L.gate_up_bt = t[0].scales_t.data_ptr(), t[0].biases_t.data_ptr()
+        L.down_st, L.down_bt = t[1].scales_t.data_ptr(), t[1].biases_t.data_ptr()
+        if self.shared_expert is not None:
+            se = self.shared_expert
+            L.shared_gate_up_w = se.gate_up_proj.weight.data_ptr()
+            L.shared_gate_up_s = se.gate_up_proj.scales.data_ptr()
+            L.shared_gate_up_b = se.gate_up_proj.biases.data_ptr()
+            L.shared_down_w = se.down_proj.weight.data_ptr()
+            L.shared_down_s = se.down_proj.scales.data_ptr()
+            L.shared_down_b = se.down_proj.biases.data_ptr()
+            L.shared_gate_up_st, L.shared_gate_up_bt = (t[2].scales_t.data_ptr(),
+                                                        t[2].biases_t.data_ptr())
+            L.shared_down_st, L.shared_down_bt = t[3].scales_t.data_ptr(), t[3].biases_t.data_ptr()
+            L.shared_gate_w = self.shared_expert_gate_weight.data_ptr()
+        self._layer = L
+        return L
+
+    # ------------------------------------------------------------ forward
+    def forward(self, x: torch.Tensor, options: _lib.Options | None = None,
+                return_routing: bool = False):
+        shape = x.shape
+        xf = x.reshape(-1, self.hidden)
+        if xf.dtype != torch.bfloat16:
+            raise _lib.InvalidArgument("SparseMoeBlock takes bf16 activations")
+        xf = xf.contiguous()
+        T = xf.shape[0]
+        L = self.layer_struct()
+        opt = options if options is not None else patch.block_options()
+        lib = _lib.load()
+        nb = lib.tmoe_moe_workspace_size(C.byref(L), T, C.byref(opt))
+        ws = ops.workspace(nb, xf.device, "moe")
+        y = torch.empty_like(xf)
+        idx = torch.empty(T, self.top_k, dtype=torch.int32, device=xf.device) if return_routing else None
+        sc = torch.empty(T, self.top_k, dtype=torch.bfloat16, device=xf.device) if return_routing else None
+        _lib.check(lib.tmoe_moe_forward(C.byref(L), xf.data_ptr(), T, C.byref(opt), ws.data_ptr(),
+                                        ws.numel(), y.data_ptr(),
+                                        idx.data_ptr() if idx is not None else None,
+                                        sc.data_ptr() if sc is not None else None,
+                                        ops.stream_ptr(xf.device)), "tmoe_moe_forward")
+        y = y.reshape(shape)
+        return (y, idx, sc) if return_routing else y
+
+    def forward_modular(self, x: torch.Tensor):
+        """The reference block op by op (qwen3_5_moe/language.py:60-91)."""
+        shape = x.shape
+        xf = x.reshape(-1, self.hidden).contiguous()
+        inds, scores = ops.router_topk(xf, self.gate_weight, self.top_k)
+        y = self.switch_mlp(xf, inds)
+        y = ops.weighted_sum(y, None, scores, (xf.shape[0], self.hidden))
+        if self.shared_expert is not None:
+            sh = self.shared_expert(xf)
+            gl = (xf.float() @ self.shared_expert_gate_weight.float().t())
+            sg = torch.sigmoid(gl.to(torch.bfloat16).float()).to(torch.bfloat16)
+            sh = (sg.float() * sh.float()).to(torch.bfloat16)
+            y = (y.float() + sh.float()).to(torch.bfloat16)
+        return y.reshape(shape)
