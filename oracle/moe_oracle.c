@@ -582,6 +582,18 @@ static void shared_prefill(const orc_moe_desc* d, const uint16_t* x, uint16_t* s
  * down (the overlay's default).  Adding 4 evaluates the int8 gathers in the
  * re-centred order (order = 1 of orc_gather_qmm_int8) instead of the
  * reference's FMA order. */
+/* Optional capture of the two operands of the final bf16 add (routed sum and
+ * gated shared term), for tests that count ULPs where that add cancels. */
+static uint16_t* g_routed_out = NULL;
+static uint16_t* g_shared_out = NULL;
+static uint16_t* g_termmax_out = NULL;  /* max_j |bf16(score_j * Y_j)| per output */
+
+void orc_set_parts_out(uint16_t* routed, uint16_t* shared, uint16_t* termmax) {
+    g_routed_out = routed;
+    g_shared_out = shared;
+    g_termmax_out = termmax;
+}
+
 void orc_moe_prefill(const orc_moe_desc* d, const uint16_t* x, int int8_mode, int32_t* idx_out,
                      uint16_t* scores_out, uint16_t* y) {
     const int gate_up_int8 = int8_mode & 1, down_int8 = (int8_mode & 2) != 0;
@@ -615,11 +627,24 @@ void orc_moe_prefill(const orc_moe_desc* d, const uint16_t* x, int int8_mode, in
         orc_gather_qmm_exact(h, d->dn_w, d->dn_s, d->dn_b, srt, R, H, I, ys, NULL);
     free(h);
     orc_weighted_sum(ys, inv, sc, T, k, H, 0, y);
+    if (g_termmax_out)
+        for (int t = 0; t < T; ++t)
+            for (int c = 0; c < H; ++c) {
+                float m = 0.0f;
+                for (int j = 0; j < k; ++j) {
+                    int p = t * k + j;
+                    float v = fabsf(bf2f(f2bf(bf2f(sc[p]) * bf2f(ys[(size_t)inv[p] * H + c]))));
+                    m = fmaxf(m, v);
+                }
+                g_termmax_out[(size_t)t * H + c] = f2bf(m);
+            }
     free(ys);
+    if (g_routed_out) memcpy(g_routed_out, y, sizeof(uint16_t) * (size_t)T * H);
     if (d->Is > 0 && d->sgu_w) {
         uint16_t* sh = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)T * H);
         shared_prefill(d, x, sh);
         for (size_t i = 0; i < (size_t)T * H; ++i) y[i] = f2bf(bf2f(y[i]) + bf2f(sh[i]));
+        if (g_shared_out) memcpy(g_shared_out, sh, sizeof(uint16_t) * (size_t)T * H);
         free(sh);
     }
     if (idx_out) memcpy(idx_out, idx, sizeof(int32_t) * (size_t)R);

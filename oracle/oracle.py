@@ -48,6 +48,7 @@ def lib():
             "orc_swiglu": ([P, i32, i32, P], None),
             "orc_weighted_sum": ([P, P, P, i32, i32, i32, i32, P], None),
             "orc_moe_prefill": ([P, P, i32, P, P, P], None),
+            "orc_set_parts_out": ([P, P, P], None),
             "orc_moe_decode": ([P, P, P, P, P], None),
         }
         for name, (args, res) in sig.items():
@@ -284,15 +285,28 @@ def make_x(T, H, seed=0, scale=1.0):
     return f32_to_bf16(rng.standard_normal((T, H), dtype=np.float32) * scale)
 
 
-def moe_prefill(layer: Layer, x, int8_mode=3):
-    """int8_mode: 0 stock bf16, 1 int8 gate_up only, 3 int8 gate_up and down."""
+def moe_prefill(layer: Layer, x, int8_mode=3, parts=False):
+    """int8_mode: 0 stock bf16, 1 int8 gate_up only, 3 int8 gate_up and down
+    (+4: re-centred FMA order).  parts=True also returns the rounding
+    operands of the output: (routed, shared_term, term_max) — the routed sum
+    and the gated shared term of the final bf16 add, and the largest bf16
+    product score_j * Y_j of each output's weighted sum."""
     T = x.shape[0]
     d = layer.desc(T)
     y = np.zeros((T, layer.H), np.uint16)
     idx = np.zeros((T, layer.k), np.int32)
     sc = np.zeros((T, layer.k), np.uint16)
-    lib().orc_moe_prefill(C.byref(d), _p(np.ascontiguousarray(x)), int(int8_mode),
-                          _p(idx), _p(sc), _p(y))
+    routed = np.zeros((T, layer.H), np.uint16) if parts else None
+    shared = np.zeros((T, layer.H), np.uint16) if parts else None
+    tmax = np.zeros((T, layer.H), np.uint16) if parts else None
+    lib().orc_set_parts_out(_p(routed), _p(shared), _p(tmax))
+    try:
+        lib().orc_moe_prefill(C.byref(d), _p(np.ascontiguousarray(x)), int(int8_mode),
+                              _p(idx), _p(sc), _p(y))
+    finally:
+        lib().orc_set_parts_out(None, None, None)
+    if parts:
+        return y, idx, sc, (routed, shared, tmax)
     return y, idx, sc
 
 

@@ -92,9 +92,9 @@ def test_prefill_modes_with_shared_expert(cuda, oracle, mode):
     x = oracle.make_x(200, 1024, seed=mode)
     opt = _opts(min_tokens=100, int8=1 if mode else 0, down_int8=1 if mode == 3 else 0)
     y, idx, sc = blk(bf(x), options=opt, return_routing=True)
-    ry, ridx, rsc = oracle.moe_prefill(L, x, int8_mode=mode)
+    ry, ridx, rsc, ops = oracle.moe_prefill(L, x, int8_mode=mode, parts=True)
     assert np.array_equal(idx.cpu().numpy(), ridx)
-    assert_bf16_close(nbf(y), ry, what=f"prefill mode {mode}")
+    assert_bf16_close(nbf(y), ry, what=f"prefill mode {mode}", operands=ops)
 
 
 def test_modular_path_equals_fused_path(cuda, oracle):
@@ -157,9 +157,9 @@ def test_prefill_full_size_config3(cuda, oracle, T):
     assert np.array_equal(idx.cpu().numpy(), ridx)
     assert np.array_equal(nbf(sc), rsc)
     sub = np.r_[0:8, T // 2:T // 2 + 4, T - 4:T]
-    ry, sidx, _ = oracle.moe_prefill(L, np.ascontiguousarray(x[sub]), int8_mode=3)
+    ry, sidx, _, ops = oracle.moe_prefill(L, np.ascontiguousarray(x[sub]), int8_mode=3, parts=True)
     assert np.array_equal(sidx, ridx[sub])
-    assert_bf16_close(nbf(y)[sub], ry, what="config-3 subset")
+    assert_bf16_close(nbf(y)[sub], ry, what="config-3 subset", operands=ops)
     # size-independent properties over every token
     yf = f32(nbf(y))
     assert np.isfinite(yf).all()

@@ -332,9 +332,9 @@ int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* s
   const int G = K / 64;
   TMOE_TRY(launch_prep_x(x, R, K, b.x16p, b.xsum, G, 1, s), "prep_x");
   if (gemv) {
-    GemvParams q{};
-    q.bh = b.x16p;
-    q.bsum = b.xsum;
+    StreamParams q{};
+    q.x16p = b.x16p;
+    q.xsum = b.xsum;
     q.K = K;
     q.W = w;
     q.S = scales;
@@ -346,9 +346,8 @@ int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* s
     q.order = b.order;
     q.umax = U;
     q.col_div = 1;
-    q.swiglu = 0;
     q.outb = y;
-    TMOE_TRY(launch_gemv_tc(q, s), "gemv");
+    TMOE_TRY(launch_gemv_stream(2, q, s), "gemv");
   } else {
     GemmParams g{};
     g.A = b.x16p;
@@ -378,8 +377,8 @@ int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* s
 namespace {
 
 struct DecodeOpWs {
-  int32_t *order, *inv, *offsets, *uexp, *ustart, *nuniq;
-  uint16_t *a16, *a16lo;
+  int32_t *order, *inv, *offsets, *uexp, *ustart, *nuniq, *counters;
+  uint16_t* a16;
   float* asum;
   float* part;
   void* route_scratch;
@@ -395,13 +394,12 @@ size_t carve_decode_op(Carve& c, int T, int k, int E, int K, int I, int D, Decod
   t.uexp = c.take<int32_t>(U > 0 ? U : 1);
   t.ustart = c.take<int32_t>(U + 1);
   t.nuniq = c.take<int32_t>(1);
-  const size_t arows = (size_t)(R > T ? R : T);
-  const int KA = K > I ? K : I;
-  t.a16 = c.take<uint16_t>(arows * KA);
-  t.a16lo = c.take<uint16_t>(arows * KA);
-  t.asum = c.take<float>(arows * (KA / 64));
+  t.counters = c.take<int32_t>((D > 0 ? D : 64) / 64 + 1);
+  t.a16 = c.take<uint16_t>((size_t)T * K);
+  t.asum = c.take<float>((size_t)T * (K / 64));
   t.part = c.take<float>((size_t)R * (D > 0 ? D : 1));
   t.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(R, E));
+  (void)I;
   if (w) *w = t;
   return c.off;
 }
@@ -440,9 +438,9 @@ int tmoe_gate_up_silu(const uint16_t* x, const uint32_t* w, const uint16_t* scal
   p.nuniq = b.nuniq;
   TMOE_TRY(launch_route_plan(idx, R, E, kTileM, 1, p, b.route_scratch, s), "route_plan");
   TMOE_TRY(launch_prep_x(x, T, K, b.a16, b.asum, K / 64, 1, s), "prep_x");
-  GemvParams q{};
-  q.bh = b.a16;
-  q.bsum = b.asum;
+  StreamParams q{};
+  q.x16p = b.a16;
+  q.xsum = b.asum;
   q.K = K;
   q.W = w;
   q.S = scales;
@@ -454,9 +452,8 @@ int tmoe_gate_up_silu(const uint16_t* x, const uint32_t* w, const uint16_t* scal
   q.order = b.order;
   q.umax = U;
   q.col_div = k;
-  q.swiglu = 1;
   q.out = h;
-  TMOE_TRY(launch_gemv_tc(q, s), "gemv_gate_up");
+  TMOE_TRY(launch_gemv_stream(0, q, s), "gemv_gate_up");
   return TMOE_OK;
 }
 
@@ -486,11 +483,9 @@ int tmoe_down_wsum(const float* h, const uint32_t* w, const uint16_t* scales,
   p.ustart = b.ustart;
   p.nuniq = b.nuniq;
   TMOE_TRY(launch_route_plan(idx, R, E, kTileM, 1, p, b.route_scratch, s), "route_plan");
-  TMOE_TRY(launch_prep_h(h, R, I, b.a16, b.a16lo, b.asum, s), "prep_h");
-  GemvParams q{};
-  q.bh = b.a16;
-  q.bl = b.a16lo;
-  q.bsum = b.asum;
+  TMOE_TRY(launch_zero_i32(b.counters, D / 64, s), "zero_counters");
+  StreamParams q{};
+  q.h = h;
   q.K = I;
   q.W = w;
   q.S = scales;
@@ -502,11 +497,13 @@ int tmoe_down_wsum(const float* h, const uint32_t* w, const uint16_t* scales,
   q.order = b.order;
   q.umax = U;
   q.col_div = 1;
-  q.swiglu = 0;
   q.out = b.part;
-  TMOE_TRY(launch_gemv_tc(q, s), "gemv_down");
-  TMOE_TRY(launch_decode_combine(b.part, nullptr, scores, T, k, D, nullptr, nullptr, y, s),
-           "combine");
+  q.counters = b.counters;
+  q.scores_f32 = scores;
+  q.T = T;
+  q.k = k;
+  q.y = y;
+  TMOE_TRY(launch_gemv_stream(1, q, s), "gemv_down");
   return TMOE_OK;
 }
 
@@ -542,8 +539,9 @@ struct BlockWs {
   int32_t *order, *inv, *offsets, *tile_row, *tile_exp, *ntiles, *uexp, *ustart, *nuniq;
   void* route_scratch;
   // decode
-  uint16_t *x16p, *hhi, *hlo, *shhi, *shlo;
-  float *xsum, *h, *hs, *hsum, *shsum, *part, *part_sh;
+  int32_t* counters;
+  uint16_t* x16p;
+  float *xsum, *h, *hs, *part, *part_sh;
   // prefill
   int8_t *xq, *hq;
   float *xsc, *xrs, *hsc, *hrs;
@@ -577,18 +575,13 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
     b.uexp = c.take<int32_t>(U > 0 ? U : 1);
     b.ustart = c.take<int32_t>(U + 1);
     b.nuniq = c.take<int32_t>(1);
+    b.counters = c.take<int32_t>(H / 64);
     b.x16p = c.take<uint16_t>((size_t)T * H);
     b.xsum = c.take<float>((size_t)T * G);
     b.h = c.take<float>((size_t)R * I);
-    b.hhi = c.take<uint16_t>((size_t)R * I);
-    b.hlo = c.take<uint16_t>((size_t)R * I);
-    b.hsum = c.take<float>((size_t)R * (I / 64));
     b.part = c.take<float>((size_t)R * H);
     if (Is > 0) {
       b.hs = c.take<float>((size_t)T * Is);
-      b.shhi = c.take<uint16_t>((size_t)T * Is);
-      b.shlo = c.take<uint16_t>((size_t)T * Is);
-      b.shsum = c.take<float>((size_t)T * (Is / 64));
       b.part_sh = c.take<float>((size_t)T * H);
     }
   } else {
@@ -667,6 +660,7 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
                      void* ws, size_t ws_bytes, uint16_t* y, int32_t* idx_out,
                      uint16_t* scores_out, void* stream) {
   if (int rc = check_layer(L, T, opt)) return rc;
+  if (T == 0) return TMOE_OK;
   if (!x || !y) return fail(TMOE_ERR_INVALID, "tmoe_moe_forward: null x or y");
   const size_t need = tmoe_moe_workspace_size(L, T, opt);
   if (!ws || ws_bytes < need)
@@ -687,7 +681,6 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   TMOE_TRY(launch_router_logits(x, L->router_w, Is > 0 ? L->shared_gate_w : nullptr, T, H, E,
                                 b.logits, b.gate_logit, s),
            "router_logits");
-  TMOE_TRY(launch_router_topk(b.logits, T, E, k, idx, scores, nullptr, s), "router_topk");
   RoutePlan p{};
   p.order = b.order;
   p.inv = b.inv;
@@ -697,20 +690,27 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     p.uexp = b.uexp;
     p.ustart = b.ustart;
     p.nuniq = b.nuniq;
-    TMOE_TRY(launch_route_plan(idx, R, E, kTileM, 1, p, b.route_scratch, s), "route_plan");
-    TMOE_TRY(launch_prep_x(x, T, H, b.x16p, b.xsum, G, 1, s), "prep_x");
-    GemvParams q{};
-    q.bh = b.x16p;
-    q.bsum = b.xsum;
+    if (T <= 32) {
+      // one CTA: top-k + routing plan + fp16 copy of x, counters zeroed
+      TMOE_TRY(launch_route_decode(b.logits, T, E, k, idx, scores, x, H, b.x16p, b.xsum, p,
+                                   b.counters, H / 64, s),
+               "route_decode");
+    } else {
+      TMOE_TRY(launch_router_topk(b.logits, T, E, k, idx, scores, nullptr, s), "router_topk");
+      TMOE_TRY(launch_route_plan(idx, R, E, kTileM, 1, p, b.route_scratch, s), "route_plan");
+      TMOE_TRY(launch_prep_x(x, T, H, b.x16p, b.xsum, G, 1, s), "prep_x");
+      TMOE_TRY(launch_zero_i32(b.counters, H / 64, s), "zero_counters");
+    }
+    StreamParams q{};
+    q.x16p = b.x16p;
+    q.xsum = b.xsum;
     q.K = H;
+    q.K_sh = H;
     q.W = L->gate_up_w;
     q.S = L->gate_up_s;
     q.B = L->gate_up_b;
     q.N = 2 * I;
     if (Is > 0) {
-      q.bh_sh = b.x16p;
-      q.bsum_sh = b.xsum;
-      q.K_sh = H;
       q.Wsh = L->shared_gate_up_w;
       q.Ssh = L->shared_gate_up_s;
       q.Bsh = L->shared_gate_up_b;
@@ -724,30 +724,24 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     q.umax = U;
     q.col_div = k;
     q.nsh = T;
-    q.swiglu = 1;
     q.out = b.h;
-    TMOE_TRY(launch_gemv_tc(q, s), "gemv_gate_up");
-    TMOE_TRY(launch_prep_h(b.h, R, I, b.hhi, b.hlo, b.hsum, s), "prep_h");
-    if (Is > 0) TMOE_TRY(launch_prep_h(b.hs, T, Is, b.shhi, b.shlo, b.shsum, s), "prep_h_shared");
-    GemvParams d{};
-    d.bh = b.hhi;
-    d.bl = b.hlo;
-    d.bsum = b.hsum;
+    TMOE_TRY(launch_gemv_stream(0, q, s), "gemv_gate_up");
+    StreamParams d{};
+    d.h = b.h;
+    d.h_sh = b.hs;
     d.K = I;
+    d.K_sh = Is;
     d.W = L->down_w;
     d.S = L->down_s;
     d.B = L->down_b;
     d.N = H;
     if (Is > 0) {
-      d.bh_sh = b.shhi;
-      d.bl_sh = b.shlo;
-      d.bsum_sh = b.shsum;
-      d.K_sh = Is;
       d.Wsh = L->shared_down_w;
       d.Ssh = L->shared_down_s;
       d.Bsh = L->shared_down_b;
       d.Nsh = H;
       d.out_sh = b.part_sh;
+      d.gate_logit = b.gate_logit;
     }
     d.uexp = b.uexp;
     d.ustart = b.ustart;
@@ -756,14 +750,16 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     d.umax = U;
     d.col_div = 1;
     d.nsh = T;
-    d.swiglu = 0;
     d.out = b.part;
-    TMOE_TRY(launch_gemv_tc(d, s), "gemv_down");
-    TMOE_TRY(launch_decode_combine(b.part, scores, nullptr, T, k, H, Is > 0 ? b.part_sh : nullptr,
-                                   b.gate_logit, y, s),
-             "combine");
+    d.counters = b.counters;
+    d.scores = scores;
+    d.T = T;
+    d.k = k;
+    d.y = y;
+    TMOE_TRY(launch_gemv_stream(1, d, s), "gemv_down");
     return TMOE_OK;
   }
+  TMOE_TRY(launch_router_topk(b.logits, T, E, k, idx, scores, nullptr, s), "router_topk");
 
   // ---- prefill: expert-sorted grouped GEMMs (int8 or stock bf16 gate_up)
   p.tile_row = b.tile_row;

@@ -23,41 +23,60 @@ TMOE_DEV float tree8_sum(float v) {
   return v;
 }
 
-__global__ void __launch_bounds__(64) router_logits_gemv(
+// One warp = 4 expert rows (8 lanes each, one per canonical partial).  The
+// warp first copies its 4 weight rows and up to 8 token rows into shared
+// memory with cp.async (every byte in flight at once), then reduces.
+constexpr int kGemvTok = 8;
+
+__global__ void __launch_bounds__(32) router_logits_gemv(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
     const uint16_t* __restrict__ wg, int T, int H, int E, uint16_t* __restrict__ logits,
     float* __restrict__ gate_logit) {
-  const int lane = threadIdx.x & 31;
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int p = lane & 7;
-  const int e = warp * 4 + (lane >> 3);
+  extern __shared__ __align__(16) uint8_t smem_r[];
+  const int lane = threadIdx.x;
+  const int p = lane & 7, sub = lane >> 3;
+  const int e0 = blockIdx.x * 4;
+  const int e = e0 + sub;
   const int nrows = E + (wg ? 1 : 0);
   const bool valid = e < nrows;
-  const uint16_t* row = valid ? ((e < E) ? wr + (size_t)e * H : wg) : wr;
-  const int nch = H >> 3;
-  for (int t0 = 0; t0 < T; t0 += 8) {
-    float acc[8];
+  const int nch = H >> 3;                     // 16-byte chunks per row
+  uint4* ws = reinterpret_cast<uint4*>(smem_r);                 // [4][nch]
+  uint4* xs = ws + 4 * nch;                                     // [8][nch]
+  for (int i = lane; i < 4 * nch; i += 32) {
+    const int r = i / nch, c = i % nch;
+    const int er = e0 + r;
+    const bool ok = er < nrows;
+    const uint16_t* row = ok ? ((er < E) ? wr + (size_t)er * H : wg) : wr;
+    cp_async16_zfill(&ws[i], row + (size_t)c * 8, ok);
+  }
+  for (int t0 = 0; t0 < T; t0 += kGemvTok) {
+    const int nt = min(kGemvTok, T - t0);
+    __syncwarp();
+    for (int i = lane; i < nt * nch; i += 32)
+      cp_async16(&xs[i], x + (size_t)(t0 + i / nch) * H + (size_t)(i % nch) * 8);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
+    float acc[kGemvTok];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-#pragma unroll 2
+    for (int i = 0; i < kGemvTok; ++i) acc[i] = 0.0f;
     for (int c = p; c < nch; c += 8) {
       float wf[8];
-      uint4 wv = valid ? ldg_nc_v4(row + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
-      unpack8_bf16(wv, wf);
+      unpack8_bf16(ws[sub * nch + c], wf);
 #pragma unroll
-      for (int tt = 0; tt < 8; ++tt) {
-        if (t0 + tt < T) {
+      for (int tt = 0; tt < kGemvTok; ++tt) {
+        if (tt < nt) {
           float xf[8];
-          unpack8_bf16(__ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + tt) * H + c * 8)), xf);
+          unpack8_bf16(xs[tt * nch + c], xf);
 #pragma unroll
           for (int u = 0; u < 8; ++u) acc[tt] = __fmaf_rn(xf[u], wf[u], acc[tt]);
         }
       }
     }
 #pragma unroll
-    for (int tt = 0; tt < 8; ++tt) {
-      float s = tree8_sum(acc[tt]);
-      if (valid && p == tt && t0 + tt < T) {
+    for (int tt = 0; tt < kGemvTok; ++tt) {
+      const float s = tree8_sum(acc[tt]);
+      if (valid && p == tt && tt < nt) {
         if (e < E)
           logits[(size_t)(t0 + tt) * E + e] = f2bf(s);
         else
@@ -231,9 +250,15 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const ui
                                  cudaStream_t s) {
   const int nrows = E + (wg ? 1 : 0);
   if (T <= 32) {
-    const int warps = (nrows + 3) / 4;
-    const int blocks = (warps + 1) / 2;
-    router_logits_gemv<<<blocks, 64, 0, s>>>(x, wr, wg, T, H, E, logits, gate_logit);
+    const size_t smem = (size_t)(4 + kGemvTok) * H * 2;
+    static int attr_h = 0;
+    if (smem > 48 * 1024 && attr_h < H) {
+      cudaError_t e = cudaFuncSetAttribute(router_logits_gemv,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      attr_h = H;
+    }
+    router_logits_gemv<<<(nrows + 3) / 4, 32, smem, s>>>(x, wr, wg, T, H, E, logits, gate_logit);
   } else {
     dim3 grid((T + 63) / 64, (nrows + 31) / 32);
     router_logits_tiled<<<grid, 256, 0, s>>>(x, wr, wg, T, H, E, logits, gate_logit);

@@ -50,20 +50,19 @@ struct GemmParams {
   uint16_t* hbf;        // optional bf16 h [R][N/2]
 };
 
-struct GemvParams {
-  const uint16_t* bh;   // activation hi part, fp16 operand layout [rows][K]
-  const uint16_t* bl;   // lo part or null
-  const float* bsum;    // [rows][K/64] group sums
-  int K;
-  const uint32_t* W;    // routed [E][N][K/8]
-  const uint16_t* S;    // [E][N][K/64]
+
+// Streaming decode GEMV over the distinct experts (decode.cu).
+struct StreamParams {
+  const uint16_t* x16p;   // modes 0/2: activation rows, fp16 operand layout [rows][K]
+  const float* xsum;      // [rows][K/64]
+  const float* h;         // mode 1: routed fp32 h [R][K]
+  const float* h_sh;      // mode 1: shared fp32 h [T][K_sh]
+  int K, K_sh;
+  const uint32_t* W;      // routed weights [E][N][K/8], scales / biases [E][N][K/64]
+  const uint16_t* S;
   const uint16_t* B;
   int N;
-  const uint16_t* bh_sh;  // shared-expert activation (rows t), same layouts
-  const uint16_t* bl_sh;
-  const float* bsum_sh;
-  int K_sh;
-  const uint32_t* Wsh;  // shared expert [Nsh][K_sh/8] or null
+  const uint32_t* Wsh;    // shared expert [Nsh][K_sh/8] or null
   const uint16_t* Ssh;
   const uint16_t* Bsh;
   int Nsh;
@@ -72,13 +71,26 @@ struct GemvParams {
   const int32_t* nuniq;
   const int32_t* order;
   int umax;
-  int col_div;          // activation row of sorted column p: order[p] / col_div
-  int nsh;              // shared expert columns (tokens)
-  int swiglu;
-  float* out;           // routed output rows order[p] (fp32)
-  float* out_sh;        // shared output rows t
-  uint16_t* outb;       // plain mode: bf16 output instead of fp32 (routed rows)
+  int col_div;            // activation row of sorted column p: order[p] / col_div
+  int nsh;                // shared-expert columns (tokens)
+  float* out;             // modes 0/1: routed fp32 output rows order[p]
+  float* out_sh;          // modes 0/1: shared fp32 output rows t
+  uint16_t* outb;         // mode 2: bf16 output rows order[p]
+  int32_t* counters;      // mode 1: [N/64] slab counters, zero on entry, left zero
+  const uint16_t* scores; // mode 1: bf16 [T][k] (or scores_f32)
+  const float* scores_f32;
+  const float* gate_logit;  // mode 1 with a shared expert: fp32 [T]
+  int T, k;
+  uint16_t* y;            // mode 1: bf16 [T][N]
 };
+
+size_t gemv_stream_smem(int K, bool lo);
+cudaError_t launch_gemv_stream(int mode, const StreamParams& P, cudaStream_t s);
+cudaError_t launch_zero_i32(int32_t* p, int n, cudaStream_t s);
+cudaError_t launch_route_decode(const uint16_t* logits, int T, int E, int k, int32_t* idx,
+                                uint16_t* scores, const uint16_t* x, int H, uint16_t* x16p,
+                                float* xsum, const RoutePlan& plan, int32_t* counters,
+                                int ncounters, cudaStream_t s);
 
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* wg, int T,
                                  int H, int E, uint16_t* logits, float* gate_logit, cudaStream_t s);
@@ -93,13 +105,6 @@ cudaError_t launch_gemm_grouped(bool int8, int epi, const GemmParams& P, int max
 cudaError_t launch_to_f16p(const uint16_t* x, long long n, uint16_t* y, cudaStream_t s);
 cudaError_t launch_prep_x(const uint16_t* x, int R, int K, uint16_t* x16p, float* xsum,
                           long long sum_sm, long long sum_sg, cudaStream_t s);
-cudaError_t launch_prep_h(const float* h, int R, int K, uint16_t* hhi, uint16_t* hlo, float* hsum,
-                          cudaStream_t s);
-cudaError_t launch_gemv_tc(const GemvParams& P, cudaStream_t s);
-cudaError_t launch_decode_combine(const float* part, const uint16_t* scores,
-                                  const float* scores_f32, int T, int k, int D,
-                                  const float* shared, const float* gate_logit, uint16_t* y,
-                                  cudaStream_t s);
 cudaError_t launch_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
                         int D, int mode, const uint16_t* sh, const float* gate_logit, uint16_t* out,
                         cudaStream_t s);

@@ -127,6 +127,12 @@ class SparseMoeBlock(nn.Module):
             raise _lib.InvalidArgument("SparseMoeBlock takes bf16 activations")
         xf = xf.contiguous()
         T = xf.shape[0]
+        if T == 0:
+            y = torch.empty_like(xf).reshape(shape)
+            if return_routing:
+                e = torch.empty(0, self.top_k, dtype=torch.int32, device=xf.device)
+                return y, e, e.to(torch.bfloat16)
+            return y
         L = self.layer_struct()
         opt = options if options is not None else patch.block_options()
         lib = _lib.load()
