@@ -37,7 +37,7 @@ enum {
   TMOE_ERR_WORKSPACE = 6    /* workspace missing or smaller than required    */
 };
 
-#define TMOE_ABI_VERSION 1
+#define TMOE_ABI_VERSION 2
 
 int tmoe_abi_version(void);
 const char* tmoe_last_error(void);
@@ -194,7 +194,14 @@ typedef struct tmoe_options {
   int wsum_mode;    /* 0 clone, 1 fast */
   int int8_prefill; /* 1: int8 gate_up (the overlay installed); 0: the stock
                        bf16-activation grouped GEMMs for the prefill path */
-} tmoe_options;     /* NULL options = {512, 1, 0, 1} */
+  int gemm_kernel;  /* prefill GEMMs: 0 = tcgen05 / TMEM (default),
+                       1 = mma.sync (the comparison baseline) */
+} tmoe_options;     /* NULL options = {512, 1, 0, 1, 0} */
+
+/* Device-side error record of the bounded waits inside the tcgen05 kernels
+ * (no reference counterpart).  Synchronises the device; returns 0 when no
+ * wait has timed out since the library was loaded, else TMOE_ERR_TIMEOUT. */
+int tmoe_device_status(void);
 
 /* Qwen3_5MoeSparseMoeBlock.__call__ —
  * titan/adapters/mlx/vendor/mlx_vlm/models/qwen3_5_moe/language.py:60-91 with

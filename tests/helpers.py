@@ -19,7 +19,7 @@ def ulp_bf16(v) -> np.ndarray:
 
 
 def bf16_tolerance(ref: np.ndarray, ulps: float = 2.0, rel: float = 1e-2,
-                   operands=()) -> np.ndarray:
+                   operands=(), operand_ulps: float | None = None) -> np.ndarray:
     """Per-element tolerance of the north-star bar: the looser of `ulps` bf16
     ULP and `rel` relative, plus a floor of one bf16 ULP of max|ref|/256 for
     elements cancelled into the noise (the reference's own convention:
@@ -34,14 +34,16 @@ def bf16_tolerance(ref: np.ndarray, ulps: float = 2.0, rel: float = 1e-2,
     r = np.abs(ref.astype(np.float32))
     floor = ulp_bf16(np.float32(r.max() / 256.0)) if r.size else np.float32(0)
     tol = np.maximum(ulps * ulp_bf16(r), rel * r)
+    ou = ulps if operand_ulps is None else operand_ulps
     for op in operands:
-        tol = np.maximum(tol, ulps * ulp_bf16(np.abs(f32(op))))
+        tol = np.maximum(tol, ou * ulp_bf16(np.abs(f32(op))))
     return tol + floor
 
 
-def assert_bf16_close(got_bits, ref_bits, ulps=2.0, rel=1e-2, what="", operands=()):
+def assert_bf16_close(got_bits, ref_bits, ulps=2.0, rel=1e-2, what="", operands=(),
+                      operand_ulps=None):
     g, r = f32(got_bits), f32(ref_bits)
-    tol = bf16_tolerance(r, ulps, rel, operands)
+    tol = bf16_tolerance(r, ulps, rel, operands, operand_ulps)
     bad = np.abs(g - r) > tol
     if bad.any():
         i = np.argwhere(bad)[0]

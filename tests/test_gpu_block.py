@@ -36,11 +36,16 @@ def _block(oracle, H, E, k, I, Is, seed, cuda):
     return blk, L
 
 
-def _opts(min_tokens, int8=1, down_int8=1, wsum=0):
+def _opts(min_tokens, int8=1, down_int8=1, wsum=0, kernel=0):
+    """kernel 0 = tcgen05 grouped GEMMs (default), 1 = mma.sync baseline."""
     from titan_b200 import _lib
     o = _lib.Options()
     o.min_tokens, o.int8_prefill, o.down_int8, o.wsum_mode = min_tokens, int8, down_int8, wsum
+    o.gemm_kernel = kernel
     return o
+
+
+KERNELS = pytest.mark.parametrize("kernel", [0, 1], ids=["tcgen05", "mma_sync"])
 
 
 @pytest.mark.parametrize("T", [1, 2, 4, 8, 32])
@@ -68,13 +73,14 @@ def test_decode_block_full_expert_count(cuda, oracle):
         assert_bf16_close(nbf(y), ry, what=f"decode E=512 T={T}")
 
 
+@KERNELS
 @pytest.mark.parametrize("T,H,E,k,I", [(128, 2048, 64, 10, 512),
                                        (300, 1024, 48, 6, 256),      # ragged T, E % 32 != 0
                                        (64, 512, 16, 4, 128)])
-def test_prefill_int8_routed_bitexact(cuda, oracle, T, H, E, k, I):
+def test_prefill_int8_routed_bitexact(cuda, oracle, T, H, E, k, I, kernel):
     blk, L = _block(oracle, H, E, k, I, 0, seed=T, cuda=cuda)
     x = oracle.make_x(T, H, seed=T)
-    y, idx, sc = blk(bf(x), options=_opts(min_tokens=1), return_routing=True)
+    y, idx, sc = blk(bf(x), options=_opts(min_tokens=1, kernel=kernel), return_routing=True)
     ry4, ridx, rsc = oracle.moe_prefill(L, x, int8_mode=3 | 4)
     assert np.array_equal(idx.cpu().numpy(), ridx)
     assert np.array_equal(nbf(sc), rsc)
@@ -85,16 +91,24 @@ def test_prefill_int8_routed_bitexact(cuda, oracle, T, H, E, k, I):
     assert rel_rms(f32(nbf(y)), f32(yd)) < 0.03
 
 
+@KERNELS
 @pytest.mark.parametrize("mode", [3, 1, 0])
-def test_prefill_modes_with_shared_expert(cuda, oracle, mode):
-    """int8 both (overlay default), int8 gate_up only (SKIP_DOWN), stock bf16."""
+def test_prefill_modes_with_shared_expert(cuda, oracle, mode, kernel):
+    """int8 both (overlay default), int8 gate_up only (SKIP_DOWN), stock bf16.
+    The bf16-activation GEMMs accumulate in an unspecified order, so an
+    output's operands (the routed sum, the gated shared term, the largest
+    weighted product) may each carry a few ULPs; the bar counts 4 ULPs of the
+    largest operand where the final adds cancel."""
     blk, L = _block(oracle, 1024, 64, 8, 256, 512, seed=mode, cuda=cuda)
     x = oracle.make_x(200, 1024, seed=mode)
-    opt = _opts(min_tokens=100, int8=1 if mode else 0, down_int8=1 if mode == 3 else 0)
+    opt = _opts(min_tokens=100, int8=1 if mode else 0, down_int8=1 if mode == 3 else 0,
+                kernel=kernel)
     y, idx, sc = blk(bf(x), options=opt, return_routing=True)
     ry, ridx, rsc, ops = oracle.moe_prefill(L, x, int8_mode=mode, parts=True)
     assert np.array_equal(idx.cpu().numpy(), ridx)
-    assert_bf16_close(nbf(y), ry, what=f"prefill mode {mode}", operands=ops)
+    assert_bf16_close(nbf(y), ry, what=f"prefill mode {mode}", operands=ops, operand_ulps=4)
+    yd, _, _ = oracle.moe_decode(L, x)
+    assert rel_rms(f32(nbf(y)), f32(yd)) < 0.03
 
 
 def test_modular_path_equals_fused_path(cuda, oracle):

@@ -13,7 +13,7 @@ import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libtitan_moe.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class TmoeError(RuntimeError):
@@ -76,7 +76,8 @@ class Layer(C.Structure):
 class Options(C.Structure):
     """struct tmoe_options."""
 
-    _fields_ = [("min_tokens", I32), ("down_int8", I32), ("wsum_mode", I32), ("int8_prefill", I32)]
+    _fields_ = [("min_tokens", I32), ("down_int8", I32), ("wsum_mode", I32), ("int8_prefill", I32),
+                ("gemm_kernel", I32)]
 
 
 STAGE_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_char_p)
@@ -84,6 +85,7 @@ STAGE_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_char_p)
 _SIGS = {
     "tmoe_abi_version": ([], I32),
     "tmoe_set_stage_hook": ([STAGE_FN, P], None),
+    "tmoe_device_status": ([], I32),
     "tmoe_last_error": ([], C.c_char_p),
     "tmoe_affine_quantize": ([P, I64, I32, P, P, P, P], I32),
     "tmoe_prepare_tables": ([P, P, I32, I32, I32, P, P, P], I32),

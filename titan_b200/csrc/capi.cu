@@ -76,6 +76,12 @@ void tmoe_set_stage_hook(tmoe_stage_fn fn, void* ctx) {
   g_hook_ctx = ctx;
 }
 
+int tmoe_device_status(void) {
+  cudaDeviceSynchronize();
+  if (tc05_error_flag()) return fail(TMOE_ERR_TIMEOUT, "a tcgen05 kernel's bounded wait timed out");
+  return TMOE_OK;
+}
+
 const char* tmoe_last_error(void) { return g_err.c_str(); }
 
 // ---------------------------------------------------------------- weight prep
@@ -555,6 +561,7 @@ int opt_min_tokens(const tmoe_options* o) { return (o && o->min_tokens > 0) ? o-
 int opt_down_int8(const tmoe_options* o) { return o ? (o->down_int8 != 0) : 1; }
 int opt_wsum(const tmoe_options* o) { return o ? o->wsum_mode : 0; }
 int opt_int8(const tmoe_options* o) { return o ? (o->int8_prefill != 0) : 1; }
+int opt_tc05(const tmoe_options* o) { return o ? (o->gemm_kernel == 0) : 1; }
 
 size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt, BlockWs* out) {
   const int H = L->hidden, E = L->num_experts, k = L->top_k, I = L->moe_inter,
@@ -589,8 +596,9 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
     b.tile_row = c.take<int32_t>(maxt);
     b.tile_exp = c.take<int32_t>(maxt);
     b.ntiles = c.take<int32_t>(1);
-    if (i8) {
-      b.xq = c.take<int8_t>((size_t)T * H);
+    const bool tc = opt_tc05(opt);
+    if (i8) {  // int8 codes: one byte each for mma.sync, fp16 for tcgen05
+      b.xq = c.take<int8_t>((size_t)T * H * (tc ? 2 : 1));
       b.xsc = c.take<float>((size_t)T * G);
       b.xrs = c.take<float>((size_t)T * G);
     }
@@ -599,7 +607,10 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
       b.sxsum = c.take<float>((size_t)T * G);
     }
     if (d8) {
-      b.hq = c.take<int8_t>((size_t)R * I);
+      if (tc)
+        b.h16p = c.take<uint16_t>((size_t)R * I);
+      else
+        b.hq = c.take<int8_t>((size_t)R * I);
       b.hsc = c.take<float>((size_t)R * (I / 64));
     } else {
       b.h16p = c.take<uint16_t>((size_t)R * I);
@@ -768,8 +779,21 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   TMOE_TRY(launch_route_plan(idx, R, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
   const bool i8 = opt_int8(opt);
   const bool d8 = i8 && opt_down_int8(opt);
-  if (i8) TMOE_TRY(launch_quantize_rows(x, T, H, b.xq, b.xsc, b.xrs, s), "quantize_rows");
-  if (!i8 || Is > 0) TMOE_TRY(launch_prep_x(x, T, H, b.sx16p, b.sxsum, G, 1, s), "prep_x");
+  const bool tc = opt_tc05(opt);
+  auto gemm = [&](bool int8, int epi, const GemmParams& P, int ntiles_max) {
+    return tc ? launch_gemm_tc05(int8, epi, P, ntiles_max, s)
+              : launch_gemm_grouped(int8, epi, P, ntiles_max, s);
+  };
+  if (tc) {
+    if (i8)
+      TMOE_TRY(launch_prep_a16(x, T, H, true, reinterpret_cast<uint16_t*>(b.xq), b.xsc, b.xrs, s),
+               "quantize_rows");
+    if (!i8 || Is > 0)
+      TMOE_TRY(launch_prep_a16(x, T, H, false, b.sx16p, nullptr, b.sxsum, s), "prep_x");
+  } else {
+    if (i8) TMOE_TRY(launch_quantize_rows(x, T, H, b.xq, b.xsc, b.xrs, s), "quantize_rows");
+    if (!i8 || Is > 0) TMOE_TRY(launch_prep_x(x, T, H, b.sx16p, b.sxsum, G, 1, s), "prep_x");
+  }
   GemmParams g{};
   g.A = i8 ? static_cast<const void*>(b.xq) : static_cast<const void*>(b.sx16p);
   g.asc = b.xsc;
@@ -792,9 +816,9 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   g.hrs = b.hrs;
   g.Rpad_h = R;
   g.h16p = b.h16p;
-  TMOE_TRY(launch_gemm_grouped(i8, d8 ? kEpiSwigluQ8 : kEpiSwigluH16, g, maxt, s), "gemm_gate_up");
+  TMOE_TRY(gemm(i8, d8 ? kEpiSwigluQ8 : kEpiSwigluH16, g, maxt), "gemm_gate_up");
   GemmParams dn{};
-  dn.A = d8 ? static_cast<const void*>(b.hq) : static_cast<const void*>(b.h16p);
+  dn.A = (d8 && !tc) ? static_cast<const void*>(b.hq) : static_cast<const void*>(b.h16p);
   dn.asc = b.hsc;
   dn.ars = b.hrs;
   dn.s_r = 1;
@@ -809,7 +833,7 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   dn.K = I;
   dn.N = H;
   dn.Y = b.ys;
-  TMOE_TRY(launch_gemm_grouped(d8, kEpiStore, dn, maxt, s), "gemm_down");
+  TMOE_TRY(gemm(d8, kEpiStore, dn, maxt), "gemm_down");
   if (Is > 0) {
     const int st = (T + kTileM - 1) / kTileM;
     TMOE_TRY(launch_dense_tiles(T, kTileM, b.s_tile_row, b.s_tile_exp, b.s_ntiles, b.s_offsets, s),
@@ -831,7 +855,7 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     sg.hrs = b.shrs;
     sg.Rpad_h = T;
     sg.h16p = b.sh16p;
-    TMOE_TRY(launch_gemm_grouped(false, kEpiSwigluH16, sg, st, s), "gemm_shared_gate_up");
+    TMOE_TRY(gemm(false, kEpiSwigluH16, sg, st), "gemm_shared_gate_up");
     GemmParams sd{};
     sd.A = b.sh16p;
     sd.ars = b.shrs;
@@ -847,7 +871,7 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     sd.K = Is;
     sd.N = H;
     sd.Y = b.ys_sh;
-    TMOE_TRY(launch_gemm_grouped(false, kEpiStore, sd, st, s), "gemm_shared_down");
+    TMOE_TRY(gemm(false, kEpiStore, sd, st), "gemm_shared_down");
   }
   TMOE_TRY(launch_wsum(b.ys, b.inv, scores, T, k, H, opt_wsum(opt), Is > 0 ? b.ys_sh : nullptr,
                        b.gate_logit, y, s),

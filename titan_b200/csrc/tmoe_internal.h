@@ -102,6 +102,12 @@ cudaError_t launch_route_plan(const int32_t* idx, int R, int E, int tile_m, int 
 cudaError_t launch_quantize_rows(const uint16_t* x, int R, int K, int8_t* xq, float* xsc,
                                  float* xrs, cudaStream_t s);
 cudaError_t launch_gemm_grouped(bool int8, int epi, const GemmParams& P, int maxt, cudaStream_t s);
+// tcgen05 version: A operands are fp16 [rows][K] with every 8-element chunk
+// in (0,4,1,5,2,6,3,7) order (prep_a16); SwiGLU epilogues write h the same way.
+cudaError_t launch_gemm_tc05(bool int8, int epi, const GemmParams& P, int maxt, cudaStream_t s);
+cudaError_t launch_prep_a16(const uint16_t* x, int R, int K, bool quant, uint16_t* a16, float* xsc,
+                            float* xrs, cudaStream_t s);
+int tc05_error_flag();
 cudaError_t launch_to_f16p(const uint16_t* x, long long n, uint16_t* y, cudaStream_t s);
 cudaError_t launch_prep_x(const uint16_t* x, int R, int K, uint16_t* x16p, float* xsum,
                           long long sum_sm, long long sum_sg, cudaStream_t s);
