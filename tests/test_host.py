@@ -5,6 +5,7 @@ way engine/patches/moe-int8/patch.py:140-168 does."""
 import ctypes as C
 import os
 import re
+import weakref
 
 import pytest
 import torch
@@ -157,3 +158,30 @@ def test_env_configuration(monkeypatch):
         assert (o.int8_prefill, o.min_tokens, o.down_int8) == (1, 1024, 0)
     finally:
         patch.uninstall()
+
+
+def test_table_cache_never_serves_another_tensors_tables(monkeypatch):
+    """The per-weight table cache is keyed by id(); an id reused by a new
+    tensor (after the old one was freed) must not return the old tables."""
+    from titan_b200 import ops
+    built = []
+    monkeypatch.setattr(ops, "build_tables", lambda w, s, b: built.append(w) or ops.Int8Tables(s, b))
+    ops.clear_tables()
+    try:
+        w1 = torch.zeros(2, 128, 8, dtype=torch.int32)
+        s1 = torch.zeros(2, 128, 1, dtype=torch.bfloat16)
+        b1 = torch.zeros_like(s1)
+        t1 = ops.cached_tables(w1, s1, b1)
+        assert ops.cached_tables(w1, s1, b1) is t1 and len(built) == 1
+        s1.add_(1)                                   # in-place update of the scales
+        assert ops.cached_tables(w1, s1, b1) is not t1 and len(built) == 2
+        # forge the id collision: a stale entry under the new tensor's key
+        w2 = torch.zeros(2, 128, 8, dtype=torch.int32)
+        s2 = torch.zeros(2, 128, 1, dtype=torch.bfloat16)
+        b2 = torch.zeros_like(s2)
+        key = (id(w2), tuple(w2.shape), s2.data_ptr())
+        ops._TABLES[key] = ((s2._version, b2._version), t1, weakref.ref(w1), weakref.ref(s1))
+        t2 = ops.cached_tables(w2, s2, b2)
+        assert t2 is not t1 and built[-1] is w2
+    finally:
+        ops.clear_tables()

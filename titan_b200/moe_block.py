@@ -76,12 +76,13 @@ class SparseMoeBlock(nn.Module):
     # ------------------------------------------------------------ weights
     def prepare(self) -> int:
         """Build the transposed scale/bias tables of every projection (the
-        reference's warmup(), patch.py:179-198).  Returns their bytes."""
+        reference's warmup(), patch.py:179-198).  Returns their bytes.  The
+        block owns its tables: they live and die with it."""
         self._layer = None
         mods = [self.switch_mlp.gate_up_proj, self.switch_mlp.down_proj]
         if self.shared_expert is not None:
             mods += [self.shared_expert.gate_up_proj, self.shared_expert.down_proj]
-        self._tables = [ops.cached_tables(m.weight, m.scales, m.biases) for m in mods]
+        self._tables = [ops.build_tables(m.weight, m.scales, m.biases) for m in mods]
         return sum(t.nbytes for t in self._tables)
 
     def layer_struct(self) -> _lib.Layer:

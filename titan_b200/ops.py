@@ -22,6 +22,7 @@ uint32 words; bf16 tensors are torch.bfloat16.
 from __future__ import annotations
 
 import math
+import weakref
 from dataclasses import dataclass
 
 import torch
@@ -158,14 +159,16 @@ _TABLES: dict = {}
 
 def cached_tables(wq, scales, biases) -> Int8Tables:
     """Tables memoised per weight tensor (engine/patches/moe-int8/kernel.py:
-    449-459 keys its cache on the weight's identity the same way).  The entry
-    holds the scale tensor's storage pointer and version so an in-place
-    update of the scales rebuilds it."""
+    449-459 keys its cache on the weight's identity the same way).  A Python
+    id is reused once its object is freed, so each entry also holds weak
+    references to the weight and scale tensors it was built from and is
+    rebuilt unless both are still the very objects passed in; the scale and
+    bias versions make an in-place update rebuild it too."""
     key = (id(wq), tuple(wq.shape), scales.data_ptr())
     hit = _TABLES.get(key)
     ver = (scales._version, biases._version)
-    if hit is None or hit[0] != ver:
-        hit = (ver, build_tables(wq, scales, biases))
+    if hit is None or hit[0] != ver or hit[2]() is not wq or hit[3]() is not scales:
+        hit = (ver, build_tables(wq, scales, biases), weakref.ref(wq), weakref.ref(scales))
         _TABLES[key] = hit
     return hit[1]
 
@@ -175,7 +178,7 @@ def clear_tables() -> None:
 
 
 def tables_nbytes() -> int:
-    return sum(t.nbytes for _, t in _TABLES.values())
+    return sum(h[1].nbytes for h in _TABLES.values())
 
 
 # --------------------------------------------------------------- activations
