@@ -119,6 +119,24 @@ int tmoe_gather_qmm_int8(const uint16_t* x, const uint32_t* w, const uint16_t* s
                          const uint16_t* biases_t, const int32_t* rhs, int R, int E, int N, int K,
                          void* ws, size_t ws_bytes, uint16_t* y, void* stream);
 
+/* tmoe_gather_qmm_int8 without a workspace argument; it allocates nothing.
+ * No counterpart in the reference (MLX allocates its own temporaries).
+ * For callers that cannot allocate device memory at the call site: a host
+ * binding with no device allocator of its own (a ctypes / cgo stub holding
+ * only the input and output pointers), or code running while a serving engine
+ * has reserved the whole device memory pool.  Scratch is one fixed array of
+ * tmoe_static_scratch_bytes() (16 MiB) per device inside this library's
+ * device image; a call whose tmoe_gather_qmm_int8_workspace_size() exceeds it
+ * returns TMOE_ERR_WORKSPACE before any launch.  The first call on a device
+ * looks the array up (this may load the library's device module): make it
+ * before any stream capture.  All calls on a device share the array, so calls
+ * in flight at the same time on different streams or host threads race:
+ * serialise them on one stream. */
+size_t tmoe_static_scratch_bytes(void);
+int tmoe_gather_qmm_int8_static(const uint16_t* x, const uint32_t* w, const uint16_t* scales_t,
+                                const uint16_t* biases_t, const int32_t* rhs, int R, int E, int N,
+                                int K, uint16_t* y, void* stream);
+
 /* bf16-activation gather with exact dequantisation and fp32 accumulation —
  * the stock mx.gather_qmm of switch_layers.py:86-98 (sorted or unsorted rhs).
  * x [R, K] bf16, rhs [R] int32 (any order); scales_t / biases_t may be NULL

@@ -96,6 +96,8 @@ _SIGS = {
     "tmoe_route_sort": ([P, I32, I32, P, SZ, P, P, P, P, P, P, I32, P], I32),
     "tmoe_gather_qmm_int8_workspace_size": ([I32, I32, I32, I32], SZ),
     "tmoe_gather_qmm_int8": ([P, P, P, P, P, I32, I32, I32, I32, P, SZ, P, P], I32),
+    "tmoe_static_scratch_bytes": ([], SZ),
+    "tmoe_gather_qmm_int8_static": ([P, P, P, P, P, I32, I32, I32, I32, P, P], I32),
     "tmoe_gather_qmm_bf16_workspace_size": ([I32, I32, I32, I32], SZ),
     "tmoe_gather_qmm_bf16": ([P, P, P, P, P, P, P, I32, I32, I32, I32, P, SZ, P, P], I32),
     "tmoe_decode_workspace_size": ([I32, I32, I32, I32, I32], SZ),

@@ -67,6 +67,8 @@ bool bad_k(int K) { return K <= 0 || K % 64 != 0; }
 
 }  // namespace
 
+int tmoe::record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 extern "C" {
 
 int tmoe_abi_version(void) { return TMOE_ABI_VERSION; }

@@ -123,4 +123,7 @@ cudaError_t launch_qsum(const uint32_t* w, int E, int N, int K, uint16_t* qsum, 
 cudaError_t launch_dense_tiles(int R, int tile_m, int32_t* tile_row, int32_t* tile_exp,
                                int32_t* ntiles, int32_t* offsets, cudaStream_t s);
 
+// Records `msg` as this thread's tmoe_last_error() text and returns `code`.
+int record_error(int code, const char* msg);
+
 }  // namespace tmoe
