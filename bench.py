@@ -55,6 +55,10 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--traffic-file", default=os.path.join(ROOT, "profiles", "traffic.txt"))
+    ap.add_argument("--profile", choices=("decode", "prefill"), default=None,
+                    help="run a small untimed case for an ncu capture and exit")
+    ap.add_argument("--gemm-kernel", type=int, default=0,
+                    help="prefill grouped GEMMs: 0 tcgen05 (default), 1 mma.sync baseline")
     return ap.parse_args()
 
 
@@ -342,10 +346,11 @@ def bench_prefill(args, world, device):
     torch.manual_seed(99)
     blk = SparseMoeBlock(c["H"], c["E"], c["k"], c["I"], c["Is"], device=device, weight_std=0.02)
     blk.prepare()
-    o = _lib.Options()
-    o.min_tokens, o.int8_prefill, o.down_int8, o.wsum_mode = 512, 1, 1, 0
     out = {}
-    for T in Ts:
+    for T, kernel in [(T, kk) for T in Ts for kk in (0, 1)]:
+        o = _lib.Options()
+        o.min_tokens, o.int8_prefill, o.down_int8, o.wsum_mode = 512, 1, 1, 0
+        o.gemm_kernel = kernel
         x = torch.randn(T, c["H"], device=device).to(torch.bfloat16)
         for _ in range(max(args.warmup, 3)):
             blk(x, options=o)
@@ -362,7 +367,9 @@ def bench_prefill(args, world, device):
         ms = max_over_ranks(a.elapsed_time(b) / steps, world)
         ops = prefill_ops_per_token(c) * T
         stages, launches = stage_profile([lambda: blk(x, options=o)], reps=2)
-        out[str(T)] = {"ms": round(ms, 4), "tok_per_s": round(T / (ms * 1e-3), 1),
+        out[str(T) if kernel == 0 else f"{T}_mma_sync"] = {
+                       "gemm": "tcgen05" if kernel == 0 else "mma.sync",
+                       "ms": round(ms, 4), "tok_per_s": round(T / (ms * 1e-3), 1),
                        "TOPs": round(ops / (ms * 1e-3) / 1e12, 2),
                        "frac_int8_nominal_4500": round(ops / (ms * 1e-3) / 4.5e15, 4),
                        "gpu_launches": launches,
@@ -508,8 +515,43 @@ def run_titan(args, world, rank, local):
     return 0
 
 
+def run_profile_case(args):
+    """A small untimed case of one path, for ncu captures (bench numbers are
+    never taken from it): decode = 2 config-2 layers at T=1, 3 steps;
+    prefill = one config-3 block at the first --prefill-T, 2 calls."""
+    import torch
+    from titan_b200 import SparseMoeBlock, _lib
+    device = torch.device("cuda", 0)
+    if args.profile == "decode":
+        blocks = build_decode_layers(2, device, seed=1234)
+        x = torch.randn(HEADLINE_T, CFG2["H"], device=device).to(torch.bfloat16)
+        opts = decode_opts()
+        for _ in range(3):
+            for b in blocks:
+                b(x, options=opts)
+    else:
+        c = CFG3
+        T = int(args.prefill_T.split(",")[0])
+        torch.manual_seed(99)
+        blk = SparseMoeBlock(c["H"], c["E"], c["k"], c["I"], c["Is"], device=device,
+                             weight_std=0.02)
+        blk.prepare()
+        o = _lib.Options()
+        o.min_tokens, o.int8_prefill, o.down_int8, o.wsum_mode = 512, 1, 1, 0
+        o.gemm_kernel = args.gemm_kernel
+        x = torch.randn(T, c["H"], device=device).to(torch.bfloat16)
+        for _ in range(2):
+            blk(x, options=o)
+    torch.cuda.synchronize()
+    rc = _lib.load().tmoe_device_status()
+    print(json.dumps({"profile": args.profile, "device_status": rc}))
+    return 0 if rc == 0 else 1
+
+
 def main():
     args = parse()
+    if args.profile:
+        return run_profile_case(args)
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
