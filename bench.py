@@ -473,6 +473,7 @@ def run_titan(args, world, rank, local):
         "gemv_gate_up": (uniq + 1) * 2 * c["I"] * (c["H"] // 2 + c["H"] // 64 * 4),
         "gemv_down": (uniq + 1) * c["H"] * (c["I"] // 2 + c["I"] // 64 * 4),
         "router_logits": (c["E"] + 1) * c["H"] * 2,
+        "decode_route": (c["E"] + 1) * c["H"] * 2,     # router rows; routing is on-chip
     }
     name = dom[0]
     alg = per_launch.get(name)

@@ -224,11 +224,31 @@ int tmoe_device_status(void);
 /* Qwen3_5MoeSparseMoeBlock.__call__ —
  * titan/adapters/mlx/vendor/mlx_vlm/models/qwen3_5_moe/language.py:60-91 with
  * the int8 overlay installed.  x [T, H] bf16 -> y [T, H] bf16; idx_out [T, k]
- * int32 and scores_out [T, k] bf16 may be NULL. */
+ * int32 and scores_out [T, k] bf16 may be NULL.
+ * The workspace must be zero-filled once, when it is allocated (its head holds
+ * counters that every call leaves at zero again); reusing it across calls,
+ * token counts and both paths needs no further clearing.  Calls sharing one
+ * workspace must be ordered (one stream). */
 size_t tmoe_moe_workspace_size(const tmoe_layer* layer, int T, const tmoe_options* opt);
 int tmoe_moe_forward(const tmoe_layer* layer, const uint16_t* x, int T, const tmoe_options* opt,
                      void* ws, size_t ws_bytes, uint16_t* y, int32_t* idx_out,
                      uint16_t* scores_out, void* stream);
+
+/* Expert parallelism, owner side: the routed experts of this rank applied to
+ * rows received from other ranks — the expert half of
+ * Qwen3_5MoeSparseMoeBlock.__call__ (language.py:74-84) once the routing is
+ * known, for experts sharded e // (E / W) over W ranks.  `layer` describes
+ * this rank's E_local experts (router and shared-expert fields unused).
+ * x [R, H] bf16; pairs in row-major order: pair_row [P] (row of each pair),
+ * pair_exp [P] (local expert id), pair_score [P] bf16, row_start [R+1] (CSR
+ * over pair_row).  y [R, H] bf16: y[r] = bf16(sum over the row's pairs, in
+ * order, of score * bf16(expert(x[r]))), fp32 accumulation. */
+size_t tmoe_moe_experts_workspace_size(const tmoe_layer* layer, int R, int npairs,
+                                       const tmoe_options* opt);
+int tmoe_moe_experts(const tmoe_layer* layer, const uint16_t* x, int R, const int32_t* pair_row,
+                     const int32_t* pair_exp, const uint16_t* pair_score,
+                     const int32_t* row_start, int npairs, const tmoe_options* opt, void* ws,
+                     size_t ws_bytes, uint16_t* y, void* stream);
 
 #ifdef __cplusplus
 }

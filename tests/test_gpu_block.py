@@ -92,6 +92,22 @@ def test_prefill_int8_routed_bitexact(cuda, oracle, T, H, E, k, I, kernel):
 
 
 @KERNELS
+def test_prefill_int8_bitexact_tiny_scales(cuda, oracle, kernel):
+    """Weights so small that their scales fall below fp16's normal range: the
+    tcgen05 kernel then keeps B unscaled and rescales in fp32 (the other of
+    its two INT8 epilogues); both must give the same bits."""
+    from titan_b200 import SparseMoeBlock
+    L = oracle.make_layer(H=512, E=16, k=4, I=128, Is=0, seed=21, w_std=2e-5)
+    blk = SparseMoeBlock(512, 16, 4, 128, 0, device=cuda, init=False)
+    load_block(blk, L)
+    x = oracle.make_x(160, 512, seed=21)
+    y, idx, sc = blk(bf(x), options=_opts(min_tokens=1, kernel=kernel), return_routing=True)
+    ry4, ridx, _ = oracle.moe_prefill(L, x, int8_mode=3 | 4)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    assert np.array_equal(nbf(y), ry4)
+
+
+@KERNELS
 @pytest.mark.parametrize("mode", [3, 1, 0])
 def test_prefill_modes_with_shared_expert(cuda, oracle, mode, kernel):
     """int8 both (overlay default), int8 gate_up only (SKIP_DOWN), stock bf16.

@@ -338,11 +338,9 @@ int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* s
   }
   TMOE_TRY(launch_route_plan(rhs, R, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
   const int G = K / 64;
-  TMOE_TRY(launch_prep_x(x, R, K, b.x16p, b.xsum, G, 1, s), "prep_x");
   if (gemv) {
     StreamParams q{};
-    q.x16p = b.x16p;
-    q.xsum = b.xsum;
+    q.x = x;
     q.K = K;
     q.W = w;
     q.S = scales;
@@ -355,8 +353,9 @@ int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* s
     q.umax = U;
     q.col_div = 1;
     q.outb = y;
-    TMOE_TRY(launch_gemv_stream(2, q, s), "gemv");
+    TMOE_TRY(launch_gemv_stream(2, q, R, s), "gemv");
   } else {
+    TMOE_TRY(launch_prep_x(x, R, K, b.x16p, b.xsum, G, 1, s), "prep_x");
     GemmParams g{};
     g.A = b.x16p;
     g.ars = b.xsum;
@@ -402,7 +401,7 @@ size_t carve_decode_op(Carve& c, int T, int k, int E, int K, int I, int D, Decod
   t.uexp = c.take<int32_t>(U > 0 ? U : 1);
   t.ustart = c.take<int32_t>(U + 1);
   t.nuniq = c.take<int32_t>(1);
-  t.counters = c.take<int32_t>((D > 0 ? D : 64) / 64 + 1);
+  t.counters = c.take<int32_t>((D > 0 ? D : 32) / 32 + 1);
   t.a16 = c.take<uint16_t>((size_t)T * K);
   t.asum = c.take<float>((size_t)T * (K / 64));
   t.part = c.take<float>((size_t)R * (D > 0 ? D : 1));
@@ -445,10 +444,8 @@ int tmoe_gate_up_silu(const uint16_t* x, const uint32_t* w, const uint16_t* scal
   p.ustart = b.ustart;
   p.nuniq = b.nuniq;
   TMOE_TRY(launch_route_plan(idx, R, E, kTileM, 1, p, b.route_scratch, s), "route_plan");
-  TMOE_TRY(launch_prep_x(x, T, K, b.a16, b.asum, K / 64, 1, s), "prep_x");
   StreamParams q{};
-  q.x16p = b.a16;
-  q.xsum = b.asum;
+  q.x = x;
   q.K = K;
   q.W = w;
   q.S = scales;
@@ -461,7 +458,7 @@ int tmoe_gate_up_silu(const uint16_t* x, const uint32_t* w, const uint16_t* scal
   q.umax = U;
   q.col_div = k;
   q.out = h;
-  TMOE_TRY(launch_gemv_stream(0, q, s), "gemv_gate_up");
+  TMOE_TRY(launch_gemv_stream(0, q, T, s), "gemv_gate_up");
   return TMOE_OK;
 }
 
@@ -491,7 +488,7 @@ int tmoe_down_wsum(const float* h, const uint32_t* w, const uint16_t* scales,
   p.ustart = b.ustart;
   p.nuniq = b.nuniq;
   TMOE_TRY(launch_route_plan(idx, R, E, kTileM, 1, p, b.route_scratch, s), "route_plan");
-  TMOE_TRY(launch_zero_i32(b.counters, D / 64, s), "zero_counters");
+  TMOE_TRY(launch_zero_i32(b.counters, D / 32, s), "zero_counters");
   StreamParams q{};
   q.h = h;
   q.K = I;
@@ -511,7 +508,7 @@ int tmoe_down_wsum(const float* h, const uint32_t* w, const uint16_t* scales,
   q.T = T;
   q.k = k;
   q.y = y;
-  TMOE_TRY(launch_gemv_stream(1, q, s), "gemv_down");
+  TMOE_TRY(launch_gemv_stream(1, q, T, s), "gemv_down");
   return TMOE_OK;
 }
 
@@ -572,6 +569,9 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
   const bool prefill = T >= opt_min_tokens(opt);
   const int maxt = max_tiles(R, E);
   BlockWs b{};
+  // Self-resetting counters first, at the same offset on every path: the
+  // decode router's ticket and one combine counter per 32-row output slab.
+  b.counters = c.take<int32_t>(H / 32 + 1);
   b.logits = c.take<uint16_t>((size_t)T * E);
   b.gate_logit = c.take<float>(T > 0 ? T : 1);
   b.idx = c.take<int32_t>(R);
@@ -584,9 +584,6 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
     b.uexp = c.take<int32_t>(U > 0 ? U : 1);
     b.ustart = c.take<int32_t>(U + 1);
     b.nuniq = c.take<int32_t>(1);
-    b.counters = c.take<int32_t>(H / 64);
-    b.x16p = c.take<uint16_t>((size_t)T * H);
-    b.xsum = c.take<float>((size_t)T * G);
     b.h = c.take<float>((size_t)R * I);
     b.part = c.take<float>((size_t)R * H);
     if (Is > 0) {
@@ -691,9 +688,11 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   uint16_t* scores = scores_out ? scores_out : b.scores;
   cudaStream_t s = S(stream);
 
-  TMOE_TRY(launch_router_logits(x, L->router_w, Is > 0 ? L->shared_gate_w : nullptr, T, H, E,
-                                b.logits, b.gate_logit, s),
-           "router_logits");
+  const uint16_t* wg = Is > 0 ? L->shared_gate_w : nullptr;
+  const bool fused_route = !prefill && T <= kDecodeRouteMaxT;
+  if (!fused_route)
+    TMOE_TRY(launch_router_logits(x, L->router_w, wg, T, H, E, b.logits, b.gate_logit, s),
+             "router_logits");
   RoutePlan p{};
   p.order = b.order;
   p.inv = b.inv;
@@ -703,20 +702,18 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     p.uexp = b.uexp;
     p.ustart = b.ustart;
     p.nuniq = b.nuniq;
-    if (T <= 32) {
-      // one CTA: top-k + routing plan + fp16 copy of x, counters zeroed
-      TMOE_TRY(launch_route_decode(b.logits, T, E, k, idx, scores, x, H, b.x16p, b.xsum, p,
-                                   b.counters, H / 64, s),
-               "route_decode");
+    if (fused_route) {
+      // logits, top-k and plan in one launch; combine counters zeroed
+      TMOE_TRY(launch_decode_route(x, L->router_w, wg, T, H, E, k, b.logits, b.gate_logit, idx,
+                                   scores, p, b.counters, H / 32, s),
+               "decode_route");
     } else {
       TMOE_TRY(launch_router_topk(b.logits, T, E, k, idx, scores, nullptr, s), "router_topk");
       TMOE_TRY(launch_route_plan(idx, R, E, kTileM, 1, p, b.route_scratch, s), "route_plan");
-      TMOE_TRY(launch_prep_x(x, T, H, b.x16p, b.xsum, G, 1, s), "prep_x");
-      TMOE_TRY(launch_zero_i32(b.counters, H / 64, s), "zero_counters");
+      TMOE_TRY(launch_zero_i32(b.counters + 1, H / 32, s), "zero_counters");
     }
     StreamParams q{};
-    q.x16p = b.x16p;
-    q.xsum = b.xsum;
+    q.x = x;
     q.K = H;
     q.K_sh = H;
     q.W = L->gate_up_w;
@@ -738,7 +735,7 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     q.col_div = k;
     q.nsh = T;
     q.out = b.h;
-    TMOE_TRY(launch_gemv_stream(0, q, s), "gemv_gate_up");
+    TMOE_TRY(launch_gemv_stream(0, q, T, s), "gemv_gate_up");
     StreamParams d{};
     d.h = b.h;
     d.h_sh = b.hs;
@@ -764,12 +761,12 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     d.col_div = 1;
     d.nsh = T;
     d.out = b.part;
-    d.counters = b.counters;
+    d.counters = b.counters + 1;
     d.scores = scores;
     d.T = T;
     d.k = k;
     d.y = y;
-    TMOE_TRY(launch_gemv_stream(1, d, s), "gemv_down");
+    TMOE_TRY(launch_gemv_stream(1, d, T, s), "gemv_down");
     return TMOE_OK;
   }
   TMOE_TRY(launch_router_topk(b.logits, T, E, k, idx, scores, nullptr, s), "router_topk");
@@ -878,6 +875,165 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   TMOE_TRY(launch_wsum(b.ys, b.inv, scores, T, k, H, opt_wsum(opt), Is > 0 ? b.ys_sh : nullptr,
                        b.gate_logit, y, s),
            "weighted_sum");
+  return TMOE_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------- routed experts on pairs
+// The owner side of expert parallelism: rows x [R, H] received from other
+// ranks and the (row, local expert, score) pairs this rank serves, in
+// row-major order with CSR row_start [R+1].  Same grouped GEMMs as the
+// prefill path; each row's output is the fp32 sum over its pairs of
+// score * bf16(expert(x_row)), in pair order, rounded to bf16 once.
+
+namespace {
+
+struct ExpertsWs {
+  int32_t *order, *inv, *offsets, *tile_row, *tile_exp, *ntiles;
+  void* route_scratch;
+  int8_t *xq, *hq;
+  float *xsc, *xrs, *hsc, *hrs;
+  uint16_t *x16p, *h16p, *ys;
+  float* xsum;
+};
+
+size_t carve_experts(Carve& c, const tmoe_layer* L, int R, int P, const tmoe_options* opt,
+                     ExpertsWs* out) {
+  const int H = L->hidden, E = L->num_experts, I = L->moe_inter, G = H / 64;
+  const int maxt = max_tiles(P, E);
+  const bool i8 = opt_int8(opt), d8 = i8 && opt_down_int8(opt), tc = opt_tc05(opt);
+  ExpertsWs b{};
+  b.order = c.take<int32_t>(P);
+  b.inv = c.take<int32_t>(P);
+  b.offsets = c.take<int32_t>(E + 1);
+  b.tile_row = c.take<int32_t>(maxt);
+  b.tile_exp = c.take<int32_t>(maxt);
+  b.ntiles = c.take<int32_t>(1);
+  b.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(P, E));
+  if (i8) {
+    b.xq = c.take<int8_t>((size_t)R * H * (tc ? 2 : 1));
+    b.xsc = c.take<float>((size_t)R * G);
+    b.xrs = c.take<float>((size_t)R * G);
+  } else {
+    b.x16p = c.take<uint16_t>((size_t)R * H);
+    b.xsum = c.take<float>((size_t)R * G);
+  }
+  if (d8 && !tc)
+    b.hq = c.take<int8_t>((size_t)P * I);
+  else
+    b.h16p = c.take<uint16_t>((size_t)P * I);
+  if (d8) b.hsc = c.take<float>((size_t)P * (I / 64));
+  b.hrs = c.take<float>((size_t)P * (I / 64));
+  b.ys = c.take<uint16_t>((size_t)P * H);
+  if (out) *out = b;
+  return c.off;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t tmoe_moe_experts_workspace_size(const tmoe_layer* L, int R, int npairs,
+                                       const tmoe_options* opt) {
+  if (!L || R < 0 || npairs < 0) return 0;
+  Carve c(nullptr);
+  return carve_experts(c, L, R, npairs, opt, nullptr);
+}
+
+int tmoe_moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pair_row,
+                     const int32_t* pair_exp, const uint16_t* pair_score,
+                     const int32_t* row_start, int npairs, const tmoe_options* opt, void* ws,
+                     size_t ws_bytes, uint16_t* y, void* stream) {
+  if (!L || R < 0 || npairs < 0) return fail(TMOE_ERR_INVALID, "tmoe_moe_experts: bad arguments");
+  const int H = L->hidden, E = L->num_experts, I = L->moe_inter, G = H / 64;
+  if (!L->gate_up_w || !L->gate_up_st || !L->gate_up_bt || !L->down_w || !L->down_st ||
+      !L->down_bt)
+    return fail(TMOE_ERR_INVALID, "tmoe_moe_experts: missing routed weights or prepared tables");
+  if (H <= 0 || H % 128 || I <= 0 || I % 64 || E <= 0 || E > 1024)
+    return fail(TMOE_ERR_UNSUPPORTED, "tmoe_moe_experts: need H %% 128 == 0, I %% 64 == 0, E <= 1024");
+  if (R == 0) return TMOE_OK;
+  if (!x || !y || !row_start || (npairs > 0 && (!pair_row || !pair_exp || !pair_score)))
+    return fail(TMOE_ERR_INVALID, "tmoe_moe_experts: null pointer");
+  const size_t need = tmoe_moe_experts_workspace_size(L, R, npairs, opt);
+  if (!ws || ws_bytes < need)
+    return fail(TMOE_ERR_WORKSPACE, "tmoe_moe_experts: workspace %zu < %zu bytes", ws_bytes, need);
+  cudaStream_t s = S(stream);
+  if (npairs == 0) {
+    // rows with no pair here contribute zero
+    TMOE_TRY(cudaMemsetAsync(y, 0, (size_t)R * H * 2, s), "zero_rows");
+    return TMOE_OK;
+  }
+  Carve c(ws);
+  ExpertsWs b;
+  carve_experts(c, L, R, npairs, opt, &b);
+  const int P = npairs, maxt = max_tiles(P, E);
+  RoutePlan p{};
+  p.order = b.order;
+  p.inv = b.inv;
+  p.offsets = b.offsets;
+  p.tile_row = b.tile_row;
+  p.tile_exp = b.tile_exp;
+  p.ntiles = b.ntiles;
+  TMOE_TRY(launch_route_plan(pair_exp, P, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
+  const bool i8 = opt_int8(opt), d8 = i8 && opt_down_int8(opt), tc = opt_tc05(opt);
+  auto gemm = [&](bool int8, int epi, const GemmParams& Pm) {
+    return tc ? launch_gemm_tc05(int8, epi, Pm, maxt, s) : launch_gemm_grouped(int8, epi, Pm, maxt, s);
+  };
+  if (tc) {
+    if (i8)
+      TMOE_TRY(launch_prep_a16(x, R, H, true, reinterpret_cast<uint16_t*>(b.xq), b.xsc, b.xrs, s),
+               "quantize_rows");
+    else
+      TMOE_TRY(launch_prep_a16(x, R, H, false, b.x16p, nullptr, b.xsum, s), "prep_x");
+  } else {
+    if (i8)
+      TMOE_TRY(launch_quantize_rows(x, R, H, b.xq, b.xsc, b.xrs, s), "quantize_rows");
+    else
+      TMOE_TRY(launch_prep_x(x, R, H, b.x16p, b.xsum, G, 1, s), "prep_x");
+  }
+  GemmParams g{};
+  g.A = i8 ? static_cast<const void*>(b.xq) : static_cast<const void*>(b.x16p);
+  g.asc = b.xsc;
+  g.ars = i8 ? b.xrs : b.xsum;
+  g.s_r = G;
+  g.s_g = 1;
+  g.a_rows = b.order;          // sorted position -> pair
+  g.a_map = pair_row;          // pair -> received row
+  g.a_div = 1;
+  g.W = L->gate_up_w;
+  g.st = L->gate_up_st;
+  g.bt = L->gate_up_bt;
+  g.tile_row = b.tile_row;
+  g.tile_exp = b.tile_exp;
+  g.ntiles = b.ntiles;
+  g.offsets = b.offsets;
+  g.K = H;
+  g.N = 2 * I;
+  g.hq = b.hq;
+  g.hsc = b.hsc;
+  g.hrs = b.hrs;
+  g.Rpad_h = P;
+  g.h16p = b.h16p;
+  TMOE_TRY(gemm(i8, d8 ? kEpiSwigluQ8 : kEpiSwigluH16, g), "gemm_gate_up");
+  GemmParams dn{};
+  dn.A = (d8 && !tc) ? static_cast<const void*>(b.hq) : static_cast<const void*>(b.h16p);
+  dn.asc = b.hsc;
+  dn.ars = b.hrs;
+  dn.s_r = 1;
+  dn.s_g = P;
+  dn.W = L->down_w;
+  dn.st = L->down_st;
+  dn.bt = L->down_bt;
+  dn.tile_row = b.tile_row;
+  dn.tile_exp = b.tile_exp;
+  dn.ntiles = b.ntiles;
+  dn.offsets = b.offsets;
+  dn.K = I;
+  dn.N = H;
+  dn.Y = b.ys;
+  TMOE_TRY(gemm(d8, kEpiStore, dn), "gemm_down");
+  TMOE_TRY(launch_segment_wsum(b.ys, b.inv, pair_score, row_start, R, H, y, s), "segment_wsum");
   return TMOE_OK;
 }
 

@@ -20,6 +20,7 @@
 #include <stdint.h>
 
 #define TMOE_DEV __device__ __forceinline__
+#define TMOE_HD __host__ __device__ __forceinline__
 
 namespace tmoe {
 
@@ -121,6 +122,13 @@ TMOE_DEV void cp_async16(void* smem, const void* gmem) {
   uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem));
 }
+// Same copy, asking L2 to fetch the whole 256-byte span around the source:
+// for rows read 16-32 bytes at a time in ascending order (packed weights one
+// 64-group per step), the following steps then hit L2 instead of DRAM.
+TMOE_DEV void cp_async16_l2pf(void* smem, const void* gmem) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(s), "l"(gmem));
+}
 TMOE_DEV void cp_async16_zfill(void* smem, const void* gmem, bool valid) {
   uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
   int src_bytes = valid ? 16 : 0;
@@ -134,6 +142,32 @@ TMOE_DEV void cp_async4(void* smem, const void* gmem) {
   uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem));
 }
+// Programmatic dependent launch.  pdl_trigger() lets the next kernel on the
+// stream start launching; pdl_wait() blocks until the previous kernel has
+// completed and its memory is visible.  A kernel launched with launch_pdl()
+// must call pdl_wait() before it reads anything a predecessor wrote and
+// before it writes anything a predecessor may still read.  Both are no-ops
+// for a kernel launched without the attribute.
+TMOE_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+TMOE_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+TMOE_DEV void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 TMOE_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
 template <int N>
 TMOE_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }

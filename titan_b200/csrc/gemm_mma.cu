@@ -135,7 +135,8 @@ __global__ void __launch_bounds__(256) gemm_grouped_kernel(GemmParams P) {
   auto src_row = [&](int r) -> int {
     int rr = row0 + r;
     if (rr >= rowend) rr = row0;
-    return P.a_rows ? P.a_rows[rr] / P.a_div : rr;
+    if (!P.a_rows) return rr;
+    return P.a_map ? P.a_map[P.a_rows[rr]] : P.a_rows[rr] / P.a_div;
   };
   int arow_src[AROWS];
 #pragma unroll

@@ -3,14 +3,15 @@
 //
 // One CTA computes a 128-row x 128-column tile of one expert over the K
 // dimension, one 64-wide quantisation group per pipeline stage.  Roles
-// (384 threads):
+// (512 threads):
 //   warp 0      allocates TMEM, issues tcgen05.mma (one elected lane) and
 //               commits stage / accumulator barriers;
-//   warps 1-3   producers: copy the A rows (gathered through a_rows) with
-//               cp.async and widen the packed int4 B rows into fp16 in
-//               registers, both into the 128B-swizzled K-major layout that the
-//               MMA descriptors address; plus the per-group scalars;
-//   warps 4-11  epilogue: two warps per TMEM lane quadrant, 64 columns each.
+//   warps 1-7   producers: cp.async copies of the A rows (gathered through
+//               a_rows), the packed int4 B rows and the scalars, LAG groups
+//               ahead; then widen the current group's B rows into fp16, both
+//               operands in the 128B-swizzled K-major layout that the MMA
+//               descriptors address;
+//   warps 8-15  epilogue: two warps per TMEM lane quadrant, 64 columns each.
 //
 // Two arithmetic modes, both on kind::f16 with fp32 accumulation:
 //   INT8  — the reference's int8 x int4 algebra: A holds the activation codes
@@ -20,7 +21,10 @@
 //           double-buffered in TMEM per group and rescaled by the epilogue:
 //           acc = fma(D*s, xsc, acc); acc = fma(xrs, bf16(b + 8s), acc) — the
 //           arithmetic of the mma.sync kernel and the oracle's re-centred
-//           order, bit for bit.  (kind::i8 would halve the MMA time but its
+//           order, bit for bit.  When every scale of the CTA's columns lies in
+//           fp16's normal range, B carries (q-8)*s instead (still exact) and
+//           the MMA returns D*s itself, saving one multiply per element per
+//           group with identical bits.  (kind::i8 would halve the MMA time but its
 //           s32 accumulator needs an int->float conversion per element per
 //           group; the per-group rescale then costs more issue slots than the
 //           MMA saves.)
@@ -41,18 +45,26 @@ __device__ int g_tc05_error = 0;
 namespace tc {
 
 constexpr int BM = 128, BN = 128;
-constexpr int NST = 4;
+constexpr int NST = 5;                            // pipeline stages
+constexpr int LAG = 3;                            // groups in flight ahead of the widening
 constexpr int A_BYTES = BM * 128;                 // 64 fp16 per row per group
 constexpr int B_BYTES = BN * 128;
 constexpr int SC_BYTES = (2 * BM + 2 * BN) * 4;   // xsc, xrs, s, bv (fp32)
-constexpr int STAGE = 35840;                      // A + B + SC rounded to 1 KB
-static_assert(A_BYTES + B_BYTES + SC_BYTES <= STAGE && STAGE % 1024 == 0, "stage layout");
+constexpr int RAWB_BYTES = BN * 32;               // packed int4 rows of the group
+constexpr int RAWT_BYTES = 2 * BN * 2;            // bf16 scales and biases of the group
+constexpr int STAGE = 39936;                      // A + B + SC + RAWB + RAWT rounded to 1 KB
+static_assert(A_BYTES + B_BYTES + SC_BYTES + RAWB_BYTES + RAWT_BYTES <= STAGE &&
+                  STAGE % 1024 == 0, "stage layout");
+static_assert(LAG < NST, "the producer refills a stage the MMA finished two groups ago");
 constexpr int BAR_OFF = NST * STAGE;
-constexpr int XCH_OFF = BAR_OFF + 256;
+constexpr int AROW_OFF = BAR_OFF + 256;           // source row of each tile row
+constexpr int XCH_OFF = AROW_OFF + BM * 4;
 constexpr int SMEM = XCH_OFF + BM * 36 * 4 + 1024;
-constexpr int NTHREADS = 384;
-constexpr int NPROD = 96;
-constexpr uint32_t kSpinLimit = 1u << 22;
+static_assert(SMEM <= 232448, "shared memory per CTA");
+constexpr int NTHREADS = 512;
+constexpr int NPROD = 224;                       // warps 1-7
+constexpr uint32_t kSpinLimit = 1u << 22;   // bound of every wait (polls)
+constexpr uint32_t kFastPolls = 1u << 12;   // polls before backing off
 
 TMOE_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -76,11 +88,22 @@ TMOE_DEV bool mbar_wait(uint32_t a, uint32_t parity, volatile int* abort_flag) {
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try(a, parity)) return true;
     if (*abort_flag) return false;
-    if (i > 32) __nanosleep(128);
+    if (i >= kFastPolls) __nanosleep(64);
   }
   *abort_flag = 1;
   atomicExch(&g_tc05_error, 1);
   return false;
+}
+
+// Named barrier over the producer warps that also ANDs a predicate.
+TMOE_DEV bool producers_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, 2, %2, p; selp.u32 %0, 1, 0, q; }"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(NPROD)
+      : "memory");
+  return r != 0;
 }
 
 TMOE_DEV uint64_t sw128_desc(uint32_t saddr) {
@@ -122,15 +145,25 @@ TMOE_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" :::
 
 // 8 nibbles (elements 0..7 of a chunk) -> 4 half2 in the pair order
 // (0,4),(1,5),(2,6),(3,7): the fp16 operand layout of every A and B chunk.
+// 0x6400|q is 1024 + q; pairs 1 and 3 are taken 4 bits up (1024 + 16q) and
+// re-centred by one HFMA2 (x/16 - 72); every step is exact.
 TMOE_DEV uint4 widen8(uint32_t w, bool scale, __half2 s2) {
   const __half2 off = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
+  const __half2 sixteenth = __halves2half2(__ushort_as_half(0x2c00), __ushort_as_half(0x2c00));
+  const __half2 m72 = __halves2half2(__ushort_as_half(0xd480), __ushort_as_half(0xd480));
+  const uint32_t w8 = w >> 8;
+  uint32_t v[4] = {(w & 0x000f000fu) | 0x64006400u, (w & 0x00f000f0u) | 0x64006400u,
+                   (w8 & 0x000f000fu) | 0x64006400u, (w8 & 0x00f000f0u) | 0x64006400u};
+  __half2 h[4];
+  h[0] = __hsub2(*reinterpret_cast<__half2*>(&v[0]), off);
+  h[1] = __hfma2(*reinterpret_cast<__half2*>(&v[1]), sixteenth, m72);
+  h[2] = __hsub2(*reinterpret_cast<__half2*>(&v[2]), off);
+  h[3] = __hfma2(*reinterpret_cast<__half2*>(&v[3]), sixteenth, m72);
   uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    uint32_t v = ((w >> (4 * i)) & 0x000f000fu) | 0x64006400u;
-    __half2 h = __hsub2(*reinterpret_cast<__half2*>(&v), off);
-    if (scale) h = __hmul2(h, s2);
-    o[i] = *reinterpret_cast<uint32_t*>(&h);
+    if (scale) h[i] = __hmul2(h[i], s2);
+    o[i] = *reinterpret_cast<uint32_t*>(&h[i]);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
@@ -156,18 +189,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
   const int n0 = blockIdx.x * (SW ? 64 : BN);
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NST), sempty0 = smem_u32(bars + 2 * NST);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NST);
   const uint32_t tfull0 = smem_u32(bars + 3 * NST), tempty0 = smem_u32(bars + 3 * NST + 2);
   const uint32_t drain = smem_u32(bars + 3 * NST + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * NST + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * NST + 6);
+  int* prescale_flag = reinterpret_cast<int*>(bars + 3 * NST + 7);
   float* xch = reinterpret_cast<float*>(smem + XCH_OFF);           // [128][36]
 
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
       mbar_init(full0 + 8 * s, NPROD);
-      mbar_init(empty0 + 8 * s, 1);
-      mbar_init(sempty0 + 8 * s, 8);
+      mbar_init(empty0 + 8 * s, 9);         // the MMA commit + the 8 epilogue warps
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
@@ -218,72 +251,135 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
       if (!I8) mma_commit(tfull0);
     }
     __syncwarp();
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // --------------------------------------------------------------- producers
+    // Copies for group g + LAG are issued (cp.async: A rows, packed B rows,
+    // row scalars, column tables) before group g is widened, so LAG groups of
+    // loads are in flight behind the one being converted.
     const int pt = tid - 32;
     const size_t KW = (size_t)(P.K / 8);
     const uint32_t* We = P.W + (size_t)e * P.N * KW;
     const uint16_t* ste = P.st + (size_t)e * G * P.N;
     const uint16_t* bte = P.bt + (size_t)e * G * P.N;
     const uint16_t* A = static_cast<const uint16_t*>(P.A);
-    for (int g = 0; g < G; ++g) {
+    int* arow_s = reinterpret_cast<int*>(smem + AROW_OFF);
+    for (int r = pt; r < BM; r += NPROD) {
+      int rr = row0 + r;
+      if (rr >= rowend) rr = row0;           // rows past the expert's end: any valid row
+      arow_s[r] = !P.a_rows ? rr : (P.a_map ? P.a_map[P.a_rows[rr]] : P.a_rows[rr] / P.a_div);
+    }
+    // INT8: B can carry the scale, (q - 8) * s exact in fp16, when every scale
+    // of the tile is 0 or inside [2^-14, 2^12): then the MMA returns D * s
+    // exactly (|D| <= 2^16, so D * s needs at most 24 bits).  One flag per CTA.
+    bool safe = true;
+    if (I8) {
+      for (int i = pt; i < G * 16; i += NPROD) {
+        const int g = i >> 4, cc = i & 15;
+        const uint4 v = *reinterpret_cast<const uint4*>(ste + (size_t)g * P.N + wrow(cc * 8));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t b = (w[j >> 1] >> (16 * (j & 1))) & 0xffffu;
+          const uint32_t ex = (b >> 7) & 0xffu;
+          safe = safe && (((b & 0x7fffu) == 0u) || (ex >= 113u && ex <= 138u));
+        }
+      }
+    }
+    const bool prescale = I8 ? producers_and(safe) : producers_and(true);
+    if (pt == 0) *prescale_flag = prescale ? 1 : 0;
+    const bool scale_b = !I8 || prescale;
+
+    // Per-thread copy plan, fixed across groups (addresses advance per group).
+    constexpr int NA = (BM * 8 + NPROD - 1) / NPROD;
+    constexpr int NB = (BN * 2 + NPROD - 1) / NPROD;
+    constexpr int NS = (2 * BM + NPROD - 1) / NPROD;
+    const uint16_t* a_src[NA];
+    uint32_t a_dst[NA];
+#pragma unroll
+    for (int j = 0; j < NA; ++j) {
+      const int i = min(pt + j * NPROD, BM * 8 - 1);
+      const int r = i >> 3, c = i & 7;
+      a_src[j] = A + (size_t)arow_s[r] * P.K + c * 8;
+      a_dst[j] = r * 128 + ((c ^ (r & 7)) << 4);
+    }
+    const uint32_t* b_src[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      const int i = min(pt + j * NPROD, BN * 2 - 1);
+      b_src[j] = We + (size_t)wrow(i >> 1) * KW + (i & 1) * 4;
+    }
+    const float* s_src[NS];
+#pragma unroll
+    for (int j = 0; j < NS; ++j) {
+      const int i = min(pt + j * NPROD, 2 * BM - 1);
+      const float* arr = (i < BM) ? P.asc : P.ars;
+      s_src[j] = (arr ? arr : P.ars) + (size_t)arow_s[i & (BM - 1)] * P.s_r;
+    }
+    const uint16_t* t_src = (pt < 32) ? ((pt >> 4) ? bte : ste) + wrow((pt & 15) * 8) : ste;
+
+    auto issue = [&](int g) {
+      uint8_t* sA = smem + (g % NST) * STAGE;
+      float* sc = reinterpret_cast<float*>(sA + A_BYTES + B_BYTES);
+      uint8_t* raw = reinterpret_cast<uint8_t*>(sc) + SC_BYTES;
+      uint8_t* rawt = raw + RAWB_BYTES;
+#pragma unroll
+      for (int j = 0; j < NA; ++j)
+        if (pt + j * NPROD < BM * 8) cp_async16(sA + a_dst[j], a_src[j] + g * 64);
+#pragma unroll
+      for (int j = 0; j < NB; ++j)
+        if (pt + j * NPROD < BN * 2) cp_async16_l2pf(raw + (pt + j * NPROD) * 16, b_src[j] + g * 8);
+#pragma unroll
+      for (int j = 0; j < NS; ++j) {
+        const int i = pt + j * NPROD;
+        if (i < 2 * BM && (I8 || i >= BM)) cp_async4(sc + i, s_src[j] + (size_t)g * P.s_g);
+      }
+      if (pt < 32) cp_async16(rawt + pt * 16, t_src + (size_t)g * P.N);
+    };
+    auto stage_free = [&](int g) -> bool {
       const int s = g % NST;
       const uint32_t ph = ((g / NST) & 1) ^ 1;
-      if (!mbar_wait(empty0 + 8 * s, ph, abort_flag)) break;
-      if (!mbar_wait(sempty0 + 8 * s, ph, abort_flag)) break;
-      uint8_t* sA = smem + s * STAGE;
-      uint8_t* sB = sA + A_BYTES;
-      float* sc = reinterpret_cast<float*>(sB + B_BYTES);   // xsc[128] xrs[128] s[128] bv[128]
-      // A: 128 rows x 8 chunks of 16 B, swizzled
-      for (int i = pt; i < BM * 8; i += NPROD) {
-        const int r = i >> 3, c = i & 7;
-        int rr = row0 + r;
-        if (rr >= rowend) rr = row0;
-        const int arow = P.a_rows ? P.a_rows[rr] / P.a_div : rr;
-        cp_async16(sA + r * 128 + ((c ^ (r & 7)) << 4), A + (size_t)arow * P.K + g * 64 + c * 8);
+      return mbar_wait(empty0 + 8 * s, ph, abort_flag);
+    };
+
+    for (int g = 0; g < LAG; ++g) {   // the first NST stages start free; one
+      if (g < G) issue(g);             // commit group per group index keeps the
+      cp_async_commit();               // wait_group<LAG> count exact when G < LAG
+    }
+    for (int g = 0; g < G; ++g) {
+      const int gi = g + LAG;
+      bool ok = true;
+      if (gi < G) {
+        ok = stage_free(gi);
+        if (ok) issue(gi);
       }
       cp_async_commit();
+      cp_async_wait<LAG>();                    // this thread's copies of group g landed
+      if (!producers_and(ok && !*abort_flag)) break;   // ... and every producer's
+      const int s = g % NST;
+      uint8_t* sB = smem + s * STAGE + A_BYTES;
+      float* sc = reinterpret_cast<float*>(sB + B_BYTES);
+      const uint8_t* raw = reinterpret_cast<const uint8_t*>(sc) + SC_BYTES;
+      const uint16_t* rawt = reinterpret_cast<const uint16_t*>(raw + RAWB_BYTES);
       // B: 128 rows x 2 half-rows (4 packed words each) -> 8 fp16 chunks
       for (int i = pt; i < BN * 2; i += NPROD) {
         const int r = i >> 1, hh = i & 1;
-        const int wr = wrow(r);
-        const uint4 w4 = ldg_nc_v4(We + (size_t)wr * KW + g * 8 + hh * 4);
-        __half2 s2 = __halves2half2(__ushort_as_half(0), __ushort_as_half(0));
-        if (!I8) {
-          const __half sh = __float2half_rn(bf2f(ste[(size_t)g * P.N + wr]));
-          s2 = __halves2half2(sh, sh);
-        }
+        const uint4 w4 = *reinterpret_cast<const uint4*>(raw + r * 32 + hh * 16);
+        const __half sh = __float2half_rn(bf2f(rawt[r]));
+        const __half2 s2 = __halves2half2(sh, sh);
         const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int c = hh * 4 + j;
-          *reinterpret_cast<uint4*>(sB + r * 128 + ((c ^ (r & 7)) << 4)) = widen8(ws[j], !I8, s2);
+          *reinterpret_cast<uint4*>(sB + r * 128 + ((c ^ (r & 7)) << 4)) = widen8(ws[j], scale_b, s2);
         }
       }
-      // per-group scalars
-      for (int i = pt; i < 2 * BM + 2 * BN; i += NPROD) {
-        float v = 0.0f;
-        if (i < 2 * BM) {
-          const int r = i & (BM - 1);
-          int rr = row0 + r;
-          if (rr >= rowend) rr = row0;
-          const int arow = P.a_rows ? P.a_rows[rr] / P.a_div : rr;
-          const float* arr = (i < BM) ? P.asc : P.ars;
-          if (I8 || i >= BM) v = arr[(size_t)arow * P.s_r + (size_t)g * P.s_g];
-        } else {
-          const int c = (i - 2 * BM) & (BN - 1);
-          const int wr = wrow(c);
-          const float sv = bf2f(ste[(size_t)g * P.N + wr]);
-          if (i < 2 * BM + BN) {
-            v = __fmul_rn(sv, 1.0f);
-          } else {
-            const float bb = __fadd_rn(bf2f(bte[(size_t)g * P.N + wr]), __fmul_rn(8.0f, sv));
-            v = I8 ? bfround(bb) : bb;
-          }
-        }
-        sc[i] = v;
+      // column scalars: s and the folded bias b + 8s
+      for (int c = pt; c < BN; c += NPROD) {
+        const float sv = bf2f(rawt[c]);
+        const float bb = __fadd_rn(bf2f(rawt[BN + c]), __fmul_rn(8.0f, sv));
+        sc[2 * BM + c] = sv;
+        sc[2 * BM + BN + c] = I8 ? bfround(bb) : bb;
       }
-      cp_async_wait<0>();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(full0 + 8 * s);
     }
@@ -291,17 +387,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
   } else {
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;                      // TMEM lane quadrant
-    const int half = (warp - 4) >> 2;            // column half
+    const int half = (warp - 8) >> 2;            // column half
     const int lr = q * 32 + lane;                // tile row of this thread
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     float acc[64];
 #pragma unroll
     for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
     bool ok = true;
+    bool prescaled = false;
     for (int g = 0; g < G && ok; ++g) {
       const int s = g % NST;
       const uint32_t ph = (g / NST) & 1;
       if (!mbar_wait(full0 + 8 * s, ph, abort_flag)) { ok = false; break; }
+      if (g == 0) prescaled = *reinterpret_cast<volatile int*>(prescale_flag) != 0;
       const float* sc = reinterpret_cast<const float*>(smem + s * STAGE + A_BYTES + B_BYTES);
       const float xs = sc[lr], xr = sc[BM + lr];
       const float* cs = sc + 2 * BM + 64 * half;
@@ -310,42 +408,54 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
         const int b = g & 1;
         if (!mbar_wait(tfull0 + 8 * b, (g >> 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        float d[64];
         const uint32_t ta = tmem + lane_addr + (uint32_t)(b * BN + 64 * half);
-        tmem_ld16(ta, d);
-        tmem_ld16(ta + 16, d + 16);
-        tmem_ld16(ta + 32, d + 32);
-        tmem_ld16(ta + 48, d + 48);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(tempty0 + 8 * b);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float t1 = __fmul_rn(d[c], cs[c]);
-          acc[c] = __fmaf_rn(t1, xs, acc[c]);
-          acc[c] = __fmaf_rn(xr, cb[c], acc[c]);
+        for (int hh = 0; hh < 2; ++hh) {       // two 32-column halves: fewer registers
+          float d[32];
+          tmem_ld16(ta + 32 * hh, d);
+          tmem_ld16(ta + 32 * hh + 16, d + 16);
+          tmem_wait_ld();
+          if (hh == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty0 + 8 * b);
+          }
+          if (prescaled) {                     // d = D * s already (exact)
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              acc[32 * hh + c] = __fmaf_rn(d[c], xs, acc[32 * hh + c]);
+              acc[32 * hh + c] = __fmaf_rn(xr, cb[32 * hh + c], acc[32 * hh + c]);
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const float t1 = __fmul_rn(d[c], cs[32 * hh + c]);
+              acc[32 * hh + c] = __fmaf_rn(t1, xs, acc[32 * hh + c]);
+              acc[32 * hh + c] = __fmaf_rn(xr, cb[32 * hh + c], acc[32 * hh + c]);
+            }
+          }
         }
       } else {
 #pragma unroll
         for (int c = 0; c < 64; ++c) acc[c] = __fmaf_rn(xr, cb[c], acc[c]);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(sempty0 + 8 * s);
+      if (lane == 0) mbar_arrive(empty0 + 8 * s);
     }
     if (!I8 && ok) {
       if (mbar_wait(tfull0, 0, abort_flag)) {
         tc_fence_after();
-        float d[64];
         const uint32_t ta = tmem + lane_addr + (uint32_t)(64 * half);
-        tmem_ld16(ta, d);
-        tmem_ld16(ta + 16, d + 16);
-        tmem_ld16(ta + 32, d + 32);
-        tmem_ld16(ta + 48, d + 48);
-        tmem_wait_ld();
-        tc_fence_before();
 #pragma unroll
-        for (int c = 0; c < 64; ++c) acc[c] = __fadd_rn(d[c], acc[c]);
+        for (int hh = 0; hh < 2; ++hh) {
+          float d[32];
+          tmem_ld16(ta + 32 * hh, d);
+          tmem_ld16(ta + 32 * hh + 16, d + 16);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) acc[32 * hh + c] = __fadd_rn(d[c], acc[32 * hh + c]);
+        }
+        tc_fence_before();
       } else {
         ok = false;
       }

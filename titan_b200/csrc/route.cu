@@ -11,8 +11,8 @@
 // per-expert offsets, tile starts and distinct-expert slots come from one
 // block-wide exclusive scan of a packed (count, tiles, present) word.
 //
-// route_decode fuses, for decode batches (T <= 32), the router's top-k, the
-// plan and the activation prep into a single CTA.
+// decode_route fuses, for small decode batches, the router logits, the
+// top-k and the plan into one launch (the last CTA to finish routes).
 //
 // Also here: the per-(token, 64-group) int8 activation quantiser
 // (moe_gather_int8.py:132-165).  It runs once per token; the grouped GEMM
@@ -261,51 +261,116 @@ cudaError_t launch_route_plan(const int32_t* idx, int R, int E, int tile_m, int 
 }
 
 // ------------------------------------------------------------ decode routing
-// One CTA of 1024 threads for T <= 32 tokens: (a) warp t computes token t's
-// softmax + top-k from the router logits (the canonical order of
-// router_topk_kernel), (b) the routing plan over the T*k pairs, (c) the fp16
-// operand copy and exact group sums of x for the decode GEMVs.
+// Decode router (T <= kDecodeRouteMaxT tokens) in one launch.  Each CTA of 4
+// warps computes the logits of 16 rows (experts, plus the shared-expert gate as
+// row E) for every token: 8 lanes per row, one per canonical partial, the rows
+// and the token vectors staged in shared memory by cp.async.  The last CTA to
+// finish (a device-wide ticket; nobody waits) then does, for every token, the
+// softmax + top-k of router_topk_kernel's canonical order, builds the routing
+// plan over the T*k pairs, zeroes the decode combine counters and resets the
+// ticket.
+//
+// counters[0] is the ticket; counters[1 .. ncounters] are the combine
+// counters.  counters[0] must be zero when the kernel starts; it is zero again
+// when the kernel ends.
+constexpr int kDrRows = 16;        // rows per CTA (4 per warp)
+constexpr int kDrTok = 8;          // tokens per pass
+
+TMOE_DEV float tree8(float v) {
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return v;
+}
+
 template <int PER>
-__global__ void __launch_bounds__(1024) route_decode_kernel(
-    const uint16_t* __restrict__ logits, int T, int E, int k, int32_t* __restrict__ idx,
-    uint16_t* __restrict__ scores, const uint16_t* __restrict__ x, int H,
-    uint16_t* __restrict__ x16p, float* __restrict__ xsum, RoutePlan plan,
-    int32_t* __restrict__ counters, int ncounters) {
+__global__ void __launch_bounds__(128) decode_route_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
+    const uint16_t* __restrict__ wg, int T, int H, int E, int k, uint16_t* __restrict__ logits,
+    float* __restrict__ gate_logit, int32_t* __restrict__ idx, uint16_t* __restrict__ scores,
+    RoutePlan plan, int32_t* __restrict__ counters, int ncounters) {
+  extern __shared__ __align__(16) uint8_t smem_dr[];
   __shared__ int32_t sidx[1024];
   __shared__ int32_t cnt[1024];
   __shared__ int32_t off[1025];
   __shared__ uint64_t ws[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int R = T * k;
-  for (int i = threadIdx.x; i < ncounters; i += blockDim.x) counters[i] = 0;
-  // (c) activation prep, one warp per (token, group)
-  {
-    const int G = H / kGroup;
-    for (int task = warp; task < T * G; task += 32) {
-      const int m = task / G, g = task % G;
-      const uint16_t* src = x + (size_t)m * H + g * kGroup;
-      const uint32_t pr = *reinterpret_cast<const uint32_t*>(src + 2 * lane);
-      const float a = bf2f((uint16_t)(pr & 0xffffu)), b = bf2f((uint16_t)(pr >> 16));
-      const float s = warp_butterfly_sum(__fadd_rn(a, b));
-      uint16_t* dst = x16p + (size_t)m * H + g * kGroup;
-      const int k0 = 2 * lane;
-      const int hi = k0 & 8, r0 = k0 & 7, r1 = (k0 + 1) & 7;
-      dst[(k0 & ~15) + hi + ((r0 & 3) << 1) + (r0 >> 2)] = __half_as_ushort(__float2half_rn(a));
-      dst[((k0 + 1) & ~15) + ((k0 + 1) & 8) + ((r1 & 3) << 1) + (r1 >> 2)] =
-          __half_as_ushort(__float2half_rn(b));
-      if (lane == 0) xsum[(size_t)m * G + g] = s;
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nch = H >> 3;                              // 16-byte chunks per row
+  const int nrows = E + (wg ? 1 : 0);
+  const int r0 = blockIdx.x * kDrRows;
+  uint4* wsm = reinterpret_cast<uint4*>(smem_dr);      // [16][nch]
+  uint4* xsm = wsm + kDrRows * nch;                    // [8][nch]
+
+  pdl_trigger();
+  // ---- logits of rows r0 .. r0+15 (warp w copies rows 4w .. 4w+3); the rows
+  // are constant, so they are requested before waiting for the previous kernel
+  for (int r = 4 * warp; r < 4 * warp + 4; ++r) {
+    const int er = r0 + r;
+    const bool ok = er < nrows;
+    const uint16_t* row = ok ? ((er < E) ? wr + (size_t)er * H : wg) : wr;
+    for (int c = lane; c < nch; c += 32) cp_async16_zfill(&wsm[r * nch + c], row + (size_t)c * 8, ok);
+  }
+  pdl_wait();                                          // x and the workspace are ours now
+  const int p = lane & 7, sub = lane >> 3;
+  const int rl = warp * 4 + sub, e = r0 + rl;
+  const uint4* wrow_s = wsm + rl * nch;
+  for (int t0 = 0; t0 < T; t0 += kDrTok) {
+    const int nt = min(kDrTok, T - t0);
+    __syncthreads();                                   // previous pass done with xsm
+    for (int tt = 0; tt < nt; ++tt)
+      for (int c = tid; c < nch; c += 128)
+        cp_async16(&xsm[tt * nch + c], x + (size_t)(t0 + tt) * H + (size_t)c * 8);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    float acc[kDrTok];
+#pragma unroll
+    for (int i = 0; i < kDrTok; ++i) acc[i] = 0.0f;
+#pragma unroll 4
+    for (int c = p; c < nch; c += 8) {
+      float wf[8];
+      unpack8_bf16(wrow_s[c], wf);
+#pragma unroll
+      for (int tt = 0; tt < kDrTok; ++tt) {
+        if (tt < nt) {
+          float xf[8];
+          unpack8_bf16(xsm[tt * nch + c], xf);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[tt] = __fmaf_rn(xf[q], wf[q], acc[tt]);
+        }
+      }
+    }
+#pragma unroll
+    for (int tt = 0; tt < kDrTok; ++tt) {
+      const float s8 = tree8(acc[tt]);
+      if (e < nrows && p == tt && tt < nt) {
+        if (e < E)
+          logits[(size_t)(t0 + tt) * E + e] = f2bf(s8);
+        else
+          gate_logit[t0 + tt] = s8;
+      }
     }
   }
-  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
-  // (a) top-k, warp t -> token t
-  if (warp < T) {
-    const int t = warp;
+
+  // ---- the last CTA to finish routes every token
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = (atomicAdd(&counters[0], 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int R = T * k;
+  for (int i = tid; i < ncounters; i += 128) counters[1 + i] = 0;
+  if (R > 32)
+    for (int i = tid; i < E; i += 128) cnt[i] = 0;
+  for (int t = warp; t < T; t += 4) {
     float lv[PER];
     float m = -__int_as_float(0x7f800000);
 #pragma unroll
     for (int c = 0; c < PER; ++c) {
-      const int e = 32 * c + lane;
-      lv[c] = (e < E) ? bf2f(logits[(size_t)t * E + e]) : -__int_as_float(0x7f800000);
+      const int ee = 32 * c + lane;
+      lv[c] = (ee < E) ? bf2f(__ldcg(logits + (size_t)t * E + ee)) : -__int_as_float(0x7f800000);
       m = fmaxf(m, lv[c]);
     }
     m = warp_max(m);
@@ -313,8 +378,8 @@ __global__ void __launch_bounds__(1024) route_decode_kernel(
     float part = 0.0f;
 #pragma unroll
     for (int c = 0; c < PER; ++c) {
-      const int e = 32 * c + lane;
-      if (e < E) {
+      const int ee = 32 * c + lane;
+      if (ee < E) {
         ex[c] = cexp(__fsub_rn(lv[c], m));
         part = __fadd_rn(part, ex[c]);
       } else {
@@ -332,9 +397,9 @@ __global__ void __launch_bounds__(1024) route_decode_kernel(
       uint32_t best = 0;
 #pragma unroll
       for (int c = 0; c < PER; ++c) {
-        const int e = 32 * c + lane;
-        if (e < E && !((taken >> c) & 1u)) {
-          const uint32_t key = (pb[c] << 16) | (uint32_t)(0xffff - e);
+        const int ee = 32 * c + lane;
+        if (ee < E && !((taken >> c) & 1u)) {
+          const uint32_t key = (pb[c] << 16) | (uint32_t)(0xffff - ee);
           best = key > best ? key : best;
         }
       }
@@ -356,35 +421,82 @@ __global__ void __launch_bounds__(1024) route_decode_kernel(
     }
   }
   __syncthreads();
-  // (b) plan
-  for (int i = threadIdx.x; i < R; i += blockDim.x) atomicAdd(&cnt[sidx[i]], 1);
-  __syncthreads();
-  plan_from_counts(cnt, off, E, R, 1, 0, plan, ws);
-  plan_totals(cnt, E, R, 1, 0, plan);
-  __syncthreads();
-  for (int i = threadIdx.x; i < R; i += blockDim.x) {
-    const int e = sidx[i];
-    int rank = 0;
-    for (int j = 0; j < i; ++j) rank += (sidx[j] == e);
-    const int pos = off[e] + rank;
-    plan.order[pos] = i;
-    plan.inv[i] = pos;
+  if (R <= 32) {
+    // One warp: bitonic sort of (expert, pair) keys; the pair index makes the
+    // order stable.  Sorted position j holds pair order[j]; the first position
+    // of each expert starts a distinct-expert segment.
+    if (warp == 0) {
+      int key = lane < R ? (sidx[lane] << 6) | lane : 0x7fffffff;
+#pragma unroll
+      for (int kk = 2; kk <= 32; kk <<= 1) {
+#pragma unroll
+        for (int j = kk >> 1; j > 0; j >>= 1) {
+          const int other = __shfl_xor_sync(0xffffffffu, key, j);
+          const bool up = (lane & kk) == 0, lower = (lane & j) == 0;
+          key = (lower == up) ? min(key, other) : max(key, other);
+        }
+      }
+      const int ee = key >> 6, flat = key & 63;
+      const int prev = __shfl_up_sync(0xffffffffu, ee, 1);
+      const bool first = lane < R && (lane == 0 || prev != ee);
+      const uint32_t mask = __ballot_sync(0xffffffffu, first);
+      if (lane < R) {
+        plan.order[lane] = flat;
+        plan.inv[flat] = lane;
+      }
+      if (first) {
+        const int u = __popc(mask & ((1u << lane) - 1u));
+        plan.uexp[u] = ee;
+        plan.ustart[u] = lane;
+      }
+      if (lane == 0) {
+        plan.nuniq[0] = __popc(mask);
+        plan.ustart[__popc(mask)] = R;
+      }
+    }
+  } else {
+    for (int i = tid; i < R; i += 128) atomicAdd(&cnt[sidx[i]], 1);
+    __syncthreads();
+    plan_from_counts(cnt, off, E, R, 1, 0, plan, ws);
+    plan_totals(cnt, E, R, 1, 0, plan);
+    __syncthreads();
+    for (int i = tid; i < R; i += 128) {
+      const int ee = sidx[i];
+      int rank = 0;
+      for (int j = 0; j < i; ++j) rank += (sidx[j] == ee);
+      const int pos = off[ee] + rank;
+      plan.order[pos] = i;
+      plan.inv[i] = pos;
+    }
   }
+  if (tid == 0) counters[0] = 0;
 }
 
-cudaError_t launch_route_decode(const uint16_t* logits, int T, int E, int k, int32_t* idx,
-                                uint16_t* scores, const uint16_t* x, int H, uint16_t* x16p,
-                                float* xsum, const RoutePlan& plan, int32_t* counters,
-                                int ncounters, cudaStream_t s) {
+size_t decode_route_smem(int H) { return (size_t)(kDrRows + kDrTok) * H * 2; }
+
+cudaError_t launch_decode_route(const uint16_t* x, const uint16_t* wr, const uint16_t* wg, int T,
+                                int H, int E, int k, uint16_t* logits, float* gate_logit,
+                                int32_t* idx, uint16_t* scores, const RoutePlan& plan,
+                                int32_t* counters, int ncounters, cudaStream_t s) {
   const int per = (E + 31) / 32;
-#define TMOE_RD(P)                                                                          \
-  route_decode_kernel<P><<<1, 1024, 0, s>>>(logits, T, E, k, idx, scores, x, H, x16p, xsum, \
-                                            plan, counters, ncounters)
-  if (per <= 4) TMOE_RD(4);
-  else if (per <= 8) TMOE_RD(8);
-  else if (per <= 16) TMOE_RD(16);
-  else TMOE_RD(32);
-#undef TMOE_RD
+  const int nrows = E + (wg ? 1 : 0);
+  const int grid = (nrows + kDrRows - 1) / kDrRows;
+  const size_t smem = decode_route_smem(H);
+  cudaError_t err = cudaSuccess;
+#define TMOE_DR(P)                                                                              \
+  do {                                                                                          \
+    err = cudaFuncSetAttribute(decode_route_kernel<P>,                                          \
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);         \
+    if (err == cudaSuccess)                                                                     \
+      err = launch_pdl(decode_route_kernel<P>, dim3(grid), dim3(128), smem, s, x, wr, wg, T, H, \
+                       E, k, logits, gate_logit, idx, scores, plan, counters, ncounters);       \
+  } while (0)
+  if (per <= 4) TMOE_DR(4);
+  else if (per <= 8) TMOE_DR(8);
+  else if (per <= 16) TMOE_DR(16);
+  else TMOE_DR(32);
+#undef TMOE_DR
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 

@@ -30,8 +30,9 @@ struct GemmParams {
   const float* asc;     // row scale (I8 only), element (row, g) at row*s_r + g*s_g
   const float* ars;     // exact group sum of the unquantised row, same strides
   long long s_r, s_g;
-  const int32_t* a_rows;  // optional: sorted row r reads A row a_rows[r] / a_div
-  int a_div;
+  const int32_t* a_rows;  // optional: sorted row r reads A row a_rows[r] / a_div,
+  int a_div;              // or a_map[a_rows[r]] when a_map is set
+  const int32_t* a_map;
   const uint32_t* W;    // [E][N][K/8] packed int4
   const uint16_t* st;   // [E][G][N] bf16 scales
   const uint16_t* bt;   // [E][G][N] bf16 biases
@@ -53,8 +54,8 @@ struct GemmParams {
 
 // Streaming decode GEMV over the distinct experts (decode.cu).
 struct StreamParams {
-  const uint16_t* x16p;   // modes 0/2: activation rows, fp16 operand layout [rows][K]
-  const float* xsum;      // [rows][K/64]
+  const uint16_t* x;      // modes 0/2: bf16 activation rows [rows][K]; the row of sorted
+                          // column p is order[p] / col_div (shared expert: column = token)
   const float* h;         // mode 1: routed fp32 h [R][K]
   const float* h_sh;      // mode 1: shared fp32 h [T][K_sh]
   int K, K_sh;
@@ -71,12 +72,12 @@ struct StreamParams {
   const int32_t* nuniq;
   const int32_t* order;
   int umax;
-  int col_div;            // activation row of sorted column p: order[p] / col_div
+  int col_div;
   int nsh;                // shared-expert columns (tokens)
   float* out;             // modes 0/1: routed fp32 output rows order[p]
   float* out_sh;          // modes 0/1: shared fp32 output rows t
   uint16_t* outb;         // mode 2: bf16 output rows order[p]
-  int32_t* counters;      // mode 1: [N/64] slab counters, zero on entry, left zero
+  int32_t* counters;      // mode 1: [N/32] slab counters, zero on entry, left zero
   const uint16_t* scores; // mode 1: bf16 [T][k] (or scores_f32)
   const float* scores_f32;
   const float* gate_logit;  // mode 1 with a shared expert: fp32 [T]
@@ -84,13 +85,19 @@ struct StreamParams {
   uint16_t* y;            // mode 1: bf16 [T][N]
 };
 
-size_t gemv_stream_smem(int K, bool lo);
-cudaError_t launch_gemv_stream(int mode, const StreamParams& P, cudaStream_t s);
+size_t gemv_stream_smem(int K, int ncol, bool lo);
+int gemv_slab_rows();
+// max_cols: an upper bound of the columns (activation rows) of any one expert
+cudaError_t launch_gemv_stream(int mode, const StreamParams& P, int max_cols, cudaStream_t s);
 cudaError_t launch_zero_i32(int32_t* p, int n, cudaStream_t s);
-cudaError_t launch_route_decode(const uint16_t* logits, int T, int E, int k, int32_t* idx,
-                                uint16_t* scores, const uint16_t* x, int H, uint16_t* x16p,
-                                float* xsum, const RoutePlan& plan, int32_t* counters,
-                                int ncounters, cudaStream_t s);
+// Router logits + top-k + plan for T <= kDecodeRouteMaxT in one launch.
+// counters[0] (a ticket) must be zero on entry and is zero on exit;
+// counters[1..ncounters] are zeroed for the decode combine.
+cudaError_t launch_decode_route(const uint16_t* x, const uint16_t* wr, const uint16_t* wg, int T,
+                                int H, int E, int k, uint16_t* logits, float* gate_logit,
+                                int32_t* idx, uint16_t* scores, const RoutePlan& plan,
+                                int32_t* counters, int ncounters, cudaStream_t s);
+constexpr int kDecodeRouteMaxT = 8;
 
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* wg, int T,
                                  int H, int E, uint16_t* logits, float* gate_logit, cudaStream_t s);
@@ -115,6 +122,9 @@ cudaError_t launch_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* 
                         int D, int mode, const uint16_t* sh, const float* gate_logit, uint16_t* out,
                         cudaStream_t s);
 cudaError_t launch_swiglu(const uint16_t* gu, int R, int I, uint16_t* h, cudaStream_t s);
+cudaError_t launch_segment_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* score,
+                                const int32_t* row_start, int R, int D, uint16_t* y,
+                                cudaStream_t s);
 cudaError_t launch_affine_quantize(const float* w, long long rows, int K, uint32_t* wq,
                                    uint16_t* scales, uint16_t* biases, cudaStream_t s);
 cudaError_t launch_prepare_tables(const uint16_t* scales, const uint16_t* biases, int E, int N, int G,

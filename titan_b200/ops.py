@@ -55,12 +55,14 @@ _WS: dict = {}
 def workspace(nbytes: int, device, tag: str = "") -> torch.Tensor:
     """A grow-only device byte buffer per (device, stream, tag).  The C ABI
     never allocates; the host owns this memory.  Calls on one stream are
-    ordered, so reusing the buffer across calls is safe."""
+    ordered, so reusing the buffer across calls is safe.  New buffers start
+    zero-filled: tmoe_moe_forward keeps self-resetting counters at the head of
+    its workspace."""
     device = torch.device(device)
     key = (device.index, torch.cuda.current_stream(device).cuda_stream, tag)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+        buf = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
         _WS[key] = buf
     return buf
 
