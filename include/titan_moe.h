@@ -234,21 +234,30 @@ int tmoe_moe_forward(const tmoe_layer* layer, const uint16_t* x, int T, const tm
                      void* ws, size_t ws_bytes, uint16_t* y, int32_t* idx_out,
                      uint16_t* scores_out, void* stream);
 
-/* Expert parallelism, owner side: the routed experts of this rank applied to
- * rows received from other ranks — the expert half of
- * Qwen3_5MoeSparseMoeBlock.__call__ (language.py:74-84) once the routing is
- * known, for experts sharded e // (E / W) over W ranks.  `layer` describes
- * this rank's E_local experts (router and shared-expert fields unused).
- * x [R, H] bf16; pairs in row-major order: pair_row [P] (row of each pair),
- * pair_exp [P] (local expert id), pair_score [P] bf16, row_start [R+1] (CSR
- * over pair_row).  y [R, H] bf16: y[r] = bf16(sum over the row's pairs, in
- * order, of score * bf16(expert(x[r]))), fp32 accumulation. */
+/* Expert parallelism (no reference counterpart: the reference runs one
+ * device).  Experts are sharded e // (E / W) over W ranks; these two calls are
+ * the two halves of Qwen3_5MoeSparseMoeBlock.__call__ (language.py:74-91)
+ * around the exchanges.
+ *
+ * Owner side: this rank's routed experts on rows received from other ranks.
+ * `layer` describes the rank's E_local experts (router and shared-expert
+ * fields unused).  x [R, H] bf16; pairs in row-major order: pair_row [P]
+ * (received row), pair_exp [P] (local expert id).  y_pairs [P, H] bf16 gets
+ * every pair's expert output, the same bits the single-device block computes
+ * for that (token, slot). */
 size_t tmoe_moe_experts_workspace_size(const tmoe_layer* layer, int R, int npairs,
                                        const tmoe_options* opt);
 int tmoe_moe_experts(const tmoe_layer* layer, const uint16_t* x, int R, const int32_t* pair_row,
-                     const int32_t* pair_exp, const uint16_t* pair_score,
-                     const int32_t* row_start, int npairs, const tmoe_options* opt, void* ws,
-                     size_t ws_bytes, uint16_t* y, void* stream);
+                     const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
+                     size_t ws_bytes, uint16_t* y_pairs, void* stream);
+
+/* Source side: the block's top-k weighted sum (moe_weighted_sum.py:142-195;
+ * mode 0 clone, 1 fast) of every token's k expert outputs ys[inv[t*k+j]] plus
+ * the sigmoid-gated shared expert (language.py:85-91; shared_out [T, D] bf16
+ * and gate_logit [T] fp32, both NULL when there is none).  y [T, D] bf16. */
+int tmoe_moe_combine(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
+                     int D, int mode, const uint16_t* shared_out, const float* gate_logit,
+                     uint16_t* y, void* stream);
 
 #ifdef __cplusplus
 }

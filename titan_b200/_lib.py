@@ -108,8 +108,9 @@ _SIGS = {
     "tmoe_moe_workspace_size": ([C.POINTER(Layer), I32, C.POINTER(Options)], SZ),
     "tmoe_moe_forward": ([C.POINTER(Layer), P, I32, C.POINTER(Options), P, SZ, P, P, P, P], I32),
     "tmoe_moe_experts_workspace_size": ([C.POINTER(Layer), I32, I32, C.POINTER(Options)], SZ),
-    "tmoe_moe_experts": ([C.POINTER(Layer), P, I32, P, P, P, P, I32, C.POINTER(Options), P, SZ,
-                          P, P], I32),
+    "tmoe_moe_experts": ([C.POINTER(Layer), P, I32, P, P, I32, C.POINTER(Options), P, SZ, P, P],
+                         I32),
+    "tmoe_moe_combine": ([P, P, P, I32, I32, I32, I32, P, P, P, P], I32),
 }
 
 EXPORTED = tuple(_SIGS)

@@ -882,10 +882,9 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
 
 // ------------------------------------------------- routed experts on pairs
 // The owner side of expert parallelism: rows x [R, H] received from other
-// ranks and the (row, local expert, score) pairs this rank serves, in
-// row-major order with CSR row_start [R+1].  Same grouped GEMMs as the
-// prefill path; each row's output is the fp32 sum over its pairs of
-// score * bf16(expert(x_row)), in pair order, rounded to bf16 once.
+// ranks and the (row, local expert) pairs this rank serves.  Same grouped
+// GEMMs as the prefill path; y_pairs [P, H] gets each pair's bf16 expert
+// output in pair order, exactly the values the single-device block weighs.
 
 namespace {
 
@@ -894,7 +893,7 @@ struct ExpertsWs {
   void* route_scratch;
   int8_t *xq, *hq;
   float *xsc, *xrs, *hsc, *hrs;
-  uint16_t *x16p, *h16p, *ys;
+  uint16_t *x16p, *h16p;
   float* xsum;
 };
 
@@ -925,7 +924,6 @@ size_t carve_experts(Carve& c, const tmoe_layer* L, int R, int P, const tmoe_opt
     b.h16p = c.take<uint16_t>((size_t)P * I);
   if (d8) b.hsc = c.take<float>((size_t)P * (I / 64));
   b.hrs = c.take<float>((size_t)P * (I / 64));
-  b.ys = c.take<uint16_t>((size_t)P * H);
   if (out) *out = b;
   return c.off;
 }
@@ -942,9 +940,8 @@ size_t tmoe_moe_experts_workspace_size(const tmoe_layer* L, int R, int npairs,
 }
 
 int tmoe_moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pair_row,
-                     const int32_t* pair_exp, const uint16_t* pair_score,
-                     const int32_t* row_start, int npairs, const tmoe_options* opt, void* ws,
-                     size_t ws_bytes, uint16_t* y, void* stream) {
+                     const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
+                     size_t ws_bytes, uint16_t* y_pairs, void* stream) {
   if (!L || R < 0 || npairs < 0) return fail(TMOE_ERR_INVALID, "tmoe_moe_experts: bad arguments");
   const int H = L->hidden, E = L->num_experts, I = L->moe_inter, G = H / 64;
   if (!L->gate_up_w || !L->gate_up_st || !L->gate_up_bt || !L->down_w || !L->down_st ||
@@ -952,18 +949,13 @@ int tmoe_moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_
     return fail(TMOE_ERR_INVALID, "tmoe_moe_experts: missing routed weights or prepared tables");
   if (H <= 0 || H % 128 || I <= 0 || I % 64 || E <= 0 || E > 1024)
     return fail(TMOE_ERR_UNSUPPORTED, "tmoe_moe_experts: need H %% 128 == 0, I %% 64 == 0, E <= 1024");
-  if (R == 0) return TMOE_OK;
-  if (!x || !y || !row_start || (npairs > 0 && (!pair_row || !pair_exp || !pair_score)))
+  if (R == 0 || npairs == 0) return TMOE_OK;
+  if (!x || !y_pairs || !pair_row || !pair_exp)
     return fail(TMOE_ERR_INVALID, "tmoe_moe_experts: null pointer");
   const size_t need = tmoe_moe_experts_workspace_size(L, R, npairs, opt);
   if (!ws || ws_bytes < need)
     return fail(TMOE_ERR_WORKSPACE, "tmoe_moe_experts: workspace %zu < %zu bytes", ws_bytes, need);
   cudaStream_t s = S(stream);
-  if (npairs == 0) {
-    // rows with no pair here contribute zero
-    TMOE_TRY(cudaMemsetAsync(y, 0, (size_t)R * H * 2, s), "zero_rows");
-    return TMOE_OK;
-  }
   Carve c(ws);
   ExpertsWs b;
   carve_experts(c, L, R, npairs, opt, &b);
@@ -1031,9 +1023,24 @@ int tmoe_moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_
   dn.offsets = b.offsets;
   dn.K = I;
   dn.N = H;
-  dn.Y = b.ys;
+  dn.Y = y_pairs;
+  dn.y_rows = b.order;         // stored back in pair order
   TMOE_TRY(gemm(d8, kEpiStore, dn), "gemm_down");
-  TMOE_TRY(launch_segment_wsum(b.ys, b.inv, pair_score, row_start, R, H, y, s), "segment_wsum");
+  return TMOE_OK;
+}
+
+// The source side: the block's weighted sum (clone or fast mode) over every
+// token's k expert outputs, wherever they were computed, plus the gated
+// shared expert — the last step of tmoe_moe_forward.
+int tmoe_moe_combine(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
+                     int D, int mode, const uint16_t* shared_out, const float* gate_logit,
+                     uint16_t* y, void* stream) {
+  if (!ys || !inv || !scores || !y || T < 0 || k <= 0 || (mode != 0 && mode != 1) ||
+      (!shared_out) != (!gate_logit))
+    return fail(TMOE_ERR_INVALID, "tmoe_moe_combine: bad arguments");
+  if (D <= 0 || D % 8) return fail(TMOE_ERR_UNSUPPORTED, "tmoe_moe_combine: need D %% 8 == 0");
+  TMOE_TRY(launch_wsum(ys, inv, scores, T, k, D, mode, shared_out, gate_logit, y, S(stream)),
+           "weighted_sum");
   return TMOE_OK;
 }
 

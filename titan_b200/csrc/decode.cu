@@ -227,8 +227,12 @@ __global__ void __launch_bounds__(kThreads, 5) gemv_stream_kernel(StreamParams P
       }
     }
   }
-  pdl_wait();                                    // routing and activations are ready
-  const int nuniq = P.nuniq[0];
+  // The shared expert's gate_up reads only the layer input, which the router
+  // kernel released before triggering this launch; everything else waits for
+  // the routing.
+  const bool independent = MODE == 0 && shared;
+  if (!independent) pdl_wait();
+  const int nuniq = independent ? 0 : P.nuniq[0];
   if (!shared && u >= nuniq) return;
   const int e = shared ? 0 : P.uexp[u];
   const int p0 = shared ? 0 : P.ustart[u];

@@ -262,18 +262,23 @@ cudaError_t launch_route_plan(const int32_t* idx, int R, int E, int tile_m, int 
 
 // ------------------------------------------------------------ decode routing
 // Decode router (T <= kDecodeRouteMaxT tokens) in one launch.  Each CTA of 4
-// warps computes the logits of 16 rows (experts, plus the shared-expert gate as
-// row E) for every token: 8 lanes per row, one per canonical partial, the rows
-// and the token vectors staged in shared memory by cp.async.  The last CTA to
-// finish (a device-wide ticket; nobody waits) then does, for every token, the
-// softmax + top-k of router_topk_kernel's canonical order, builds the routing
-// plan over the T*k pairs, zeroes the decode combine counters and resets the
-// ticket.
+// warps computes the logits of 8 rows (experts, plus the shared-expert gate as
+// row E) for every token: warps 0 and 1 hold 4 rows each, 8 lanes per row, one
+// per canonical partial, with the rows and the token vectors staged in shared
+// memory by cp.async.  The last CTA to finish (a device-wide ticket; nobody
+// waits) then routes every token with all 4 warps: the exponentials of a
+// quarter of the experts per warp, the canonical sequential lane sums by one
+// warp, a top-k per warp over its quarter and the final top-k over the 4k
+// candidates (the same selection and tie order as router_topk_kernel), the
+// routing plan over the T*k pairs, and it zeroes the decode combine counters
+// and resets the ticket.
 //
 // counters[0] is the ticket; counters[1 .. ncounters] are the combine
 // counters.  counters[0] must be zero when the kernel starts; it is zero again
-// when the kernel ends.
-constexpr int kDrRows = 16;        // rows per CTA (4 per warp)
+// when the kernel ends.  The rows are requested before the wait for the
+// previous kernel (they are constant); the next kernel is released only after
+// that wait, so it may read this layer's input without waiting for us.
+constexpr int kDrRows = 8;         // rows per CTA (4 per warp, warps 0-1)
 constexpr int kDrTok = 8;          // tokens per pass
 
 TMOE_DEV float tree8(float v) {
@@ -281,6 +286,23 @@ TMOE_DEV float tree8(float v) {
   v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
   v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
   return v;
+}
+
+// One canonical partial (chunks p, p+8, ...) of one row for NT tokens.
+template <int NT>
+TMOE_DEV void router_dots(const uint4* wrow_s, const uint4* xsm, int nch, int p, float* acc) {
+#pragma unroll 4
+  for (int c = p; c < nch; c += 8) {
+    float wf[8];
+    unpack8_bf16(wrow_s[c], wf);
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt) {
+      float xf[8];
+      unpack8_bf16(xsm[tt * nch + c], xf);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[tt] = __fmaf_rn(xf[q], wf[q], acc[tt]);
+    }
+  }
 }
 
 template <int PER>
@@ -294,27 +316,29 @@ __global__ void __launch_bounds__(128) decode_route_kernel(
   __shared__ int32_t cnt[1024];
   __shared__ int32_t off[1025];
   __shared__ uint64_t ws[32];
+  __shared__ float ex_s[1024];                         // exponentials of one token
+  __shared__ uint32_t cand[4][32];                     // per-warp top-k keys
+  __shared__ float red_s[4];
   __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nch = H >> 3;                              // 16-byte chunks per row
   const int nrows = E + (wg ? 1 : 0);
   const int r0 = blockIdx.x * kDrRows;
-  uint4* wsm = reinterpret_cast<uint4*>(smem_dr);      // [16][nch]
+  uint4* wsm = reinterpret_cast<uint4*>(smem_dr);      // [8][nch]
   uint4* xsm = wsm + kDrRows * nch;                    // [8][nch]
 
-  pdl_trigger();
-  // ---- logits of rows r0 .. r0+15 (warp w copies rows 4w .. 4w+3); the rows
-  // are constant, so they are requested before waiting for the previous kernel
-  for (int r = 4 * warp; r < 4 * warp + 4; ++r) {
+  // ---- logits of rows r0 .. r0+7: constant rows requested before the wait
+  for (int r = 2 * warp; r < 2 * warp + 2; ++r) {
     const int er = r0 + r;
     const bool ok = er < nrows;
     const uint16_t* row = ok ? ((er < E) ? wr + (size_t)er * H : wg) : wr;
     for (int c = lane; c < nch; c += 32) cp_async16_zfill(&wsm[r * nch + c], row + (size_t)c * 8, ok);
   }
   pdl_wait();                                          // x and the workspace are ours now
+  pdl_trigger();
   const int p = lane & 7, sub = lane >> 3;
-  const int rl = warp * 4 + sub, e = r0 + rl;
-  const uint4* wrow_s = wsm + rl * nch;
+  const int rl = warp * 4 + sub, e = r0 + rl;          // warps 0-1
+  const uint4* wrow_s = wsm + (rl & 7) * nch;
   for (int t0 = 0; t0 < T; t0 += kDrTok) {
     const int nt = min(kDrTok, T - t0);
     __syncthreads();                                   // previous pass done with xsm
@@ -324,31 +348,29 @@ __global__ void __launch_bounds__(128) decode_route_kernel(
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    float acc[kDrTok];
+    if (warp < 2) {
+      float acc[kDrTok];
 #pragma unroll
-    for (int i = 0; i < kDrTok; ++i) acc[i] = 0.0f;
-#pragma unroll 4
-    for (int c = p; c < nch; c += 8) {
-      float wf[8];
-      unpack8_bf16(wrow_s[c], wf);
+      for (int i = 0; i < kDrTok; ++i) acc[i] = 0.0f;
+      // token count rounded up to 1, 2, 4 or 8: straight-line inner loops
+      // (the extra accumulators read stale rows and are dropped)
+      if (nt == 1)
+        router_dots<1>(wrow_s, xsm, nch, p, acc);
+      else if (nt == 2)
+        router_dots<2>(wrow_s, xsm, nch, p, acc);
+      else if (nt <= 4)
+        router_dots<4>(wrow_s, xsm, nch, p, acc);
+      else
+        router_dots<8>(wrow_s, xsm, nch, p, acc);
 #pragma unroll
       for (int tt = 0; tt < kDrTok; ++tt) {
-        if (tt < nt) {
-          float xf[8];
-          unpack8_bf16(xsm[tt * nch + c], xf);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) acc[tt] = __fmaf_rn(xf[q], wf[q], acc[tt]);
+        const float s8 = tree8(acc[tt]);
+        if (e < nrows && p == tt && tt < nt) {
+          if (e < E)
+            logits[(size_t)(t0 + tt) * E + e] = f2bf(s8);
+          else
+            gate_logit[t0 + tt] = s8;
         }
-      }
-    }
-#pragma unroll
-    for (int tt = 0; tt < kDrTok; ++tt) {
-      const float s8 = tree8(acc[tt]);
-      if (e < nrows && p == tt && tt < nt) {
-        if (e < E)
-          logits[(size_t)(t0 + tt) * E + e] = f2bf(s8);
-        else
-          gate_logit[t0 + tt] = s8;
       }
     }
   }
@@ -364,63 +386,89 @@ __global__ void __launch_bounds__(128) decode_route_kernel(
   for (int i = tid; i < ncounters; i += 128) counters[1 + i] = 0;
   if (R > 32)
     for (int i = tid; i < E; i += 128) cnt[i] = 0;
-  for (int t = warp; t < T; t += 4) {
-    float lv[PER];
+  constexpr int QPER = (PER + 3) / 4;                  // columns c of each warp's quarter
+  for (int t = 0; t < T; ++t) {
+    // (1) max: each warp over c in [warp*QPER, ...), then across warps
+    const uint16_t* lrow = logits + (size_t)t * E;
+    float lv[QPER];
     float m = -__int_as_float(0x7f800000);
 #pragma unroll
-    for (int c = 0; c < PER; ++c) {
-      const int ee = 32 * c + lane;
-      lv[c] = (ee < E) ? bf2f(__ldcg(logits + (size_t)t * E + ee)) : -__int_as_float(0x7f800000);
-      m = fmaxf(m, lv[c]);
+    for (int q = 0; q < QPER; ++q) {
+      const int c = warp * QPER + q, ee = 32 * c + lane;
+      lv[q] = (c < PER && ee < E) ? bf2f(__ldcg(lrow + ee)) : -__int_as_float(0x7f800000);
+      m = fmaxf(m, lv[q]);
     }
     m = warp_max(m);
-    float ex[PER];
-    float part = 0.0f;
+    if (lane == 0) red_s[warp] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(red_s[0], red_s[1]), fmaxf(red_s[2], red_s[3]));
+    // (2) exponentials in parallel
 #pragma unroll
-    for (int c = 0; c < PER; ++c) {
-      const int ee = 32 * c + lane;
-      if (ee < E) {
-        ex[c] = cexp(__fsub_rn(lv[c], m));
-        part = __fadd_rn(part, ex[c]);
-      } else {
-        ex[c] = 0.0f;
-      }
+    for (int q = 0; q < QPER; ++q) {
+      const int c = warp * QPER + q, ee = 32 * c + lane;
+      if (c < PER) ex_s[32 * c + lane] = (ee < E) ? cexp(__fsub_rn(lv[q], m)) : 0.0f;
     }
-    const float inv = __fdiv_rn(1.0f, warp_butterfly_sum(part));
-    uint32_t pb[PER];
+    __syncthreads();
+    // (3) the canonical denominator: lane partial over e = 32c + l in order,
+    // then the butterfly (one warp)
+    if (warp == 0) {
+      float part = 0.0f;
 #pragma unroll
-    for (int c = 0; c < PER; ++c) pb[c] = f2bf(__fmul_rn(ex[c], inv));
-    uint32_t taken = 0, my_p = 0;
-    int my_e = 0;
-    float ssum = 0.0f;
+      for (int c = 0; c < PER; ++c)
+        if (32 * c + lane < E) part = __fadd_rn(part, ex_s[32 * c + lane]);
+      const float inv = __fdiv_rn(1.0f, warp_butterfly_sum(part));
+      if (lane == 0) red_s[0] = inv;
+    }
+    __syncthreads();
+    const float inv = red_s[0];
+    // (4) top-k of each warp's quarter by bf16 probability, lowest index on ties
+    uint32_t key[QPER];
+#pragma unroll
+    for (int q = 0; q < QPER; ++q) {
+      const int c = warp * QPER + q, ee = 32 * c + lane;
+      key[q] = (c < PER && ee < E)
+                   ? (((uint32_t)f2bf(__fmul_rn(ex_s[32 * c + lane], inv)) << 16) | (uint32_t)(0xffff - ee))
+                   : 0u;
+    }
     for (int j = 0; j < k; ++j) {
       uint32_t best = 0;
 #pragma unroll
-      for (int c = 0; c < PER; ++c) {
-        const int ee = 32 * c + lane;
-        if (ee < E && !((taken >> c) & 1u)) {
-          const uint32_t key = (pb[c] << 16) | (uint32_t)(0xffff - ee);
-          best = key > best ? key : best;
-        }
-      }
+      for (int q = 0; q < QPER; ++q) best = key[q] > best ? key[q] : best;
       const uint32_t win = __reduce_max_sync(0xffffffffu, best);
-      const int e_sel = 0xffff - (int)(win & 0xffffu);
-      const uint32_t p_sel = win >> 16;
-      if ((e_sel & 31) == lane) taken |= 1u << (e_sel >> 5);
-      ssum = __fadd_rn(ssum, bf2f((uint16_t)p_sel));
-      if (lane == j) {
-        my_p = p_sel;
-        my_e = e_sel;
+#pragma unroll
+      for (int q = 0; q < QPER; ++q)
+        if (key[q] == win) key[q] = 0;
+      if (lane == j) cand[warp][j] = win;
+    }
+    __syncthreads();
+    // (5) the final top-k over the 4k candidates, in selection order
+    if (warp == 0) {
+      uint32_t ck[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) ck[w] = lane < k ? cand[w][lane] : 0u;
+      uint32_t my_key = 0;
+      float ssum = 0.0f;
+      for (int j = 0; j < k; ++j) {
+        uint32_t best = 0;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) best = ck[w] > best ? ck[w] : best;
+        const uint32_t win = __reduce_max_sync(0xffffffffu, best);
+#pragma unroll
+        for (int w = 0; w < 4; ++w)
+          if (ck[w] == win) ck[w] = 0;
+        ssum = __fadd_rn(ssum, bf2f((uint16_t)(win >> 16)));
+        if (lane == j) my_key = win;
+      }
+      const float sb = bfround(ssum);
+      if (lane < k) {
+        const int my_e = 0xffff - (int)(my_key & 0xffffu);
+        idx[(size_t)t * k + lane] = my_e;
+        sidx[t * k + lane] = my_e;
+        scores[(size_t)t * k + lane] = f2bf(__fdiv_rn(bf2f((uint16_t)(my_key >> 16)), sb));
       }
     }
-    const float sb = bfround(ssum);
-    if (lane < k) {
-      idx[(size_t)t * k + lane] = my_e;
-      sidx[t * k + lane] = my_e;
-      scores[(size_t)t * k + lane] = f2bf(__fdiv_rn(bf2f((uint16_t)my_p), sb));
-    }
+    __syncthreads();
   }
-  __syncthreads();
   if (R <= 32) {
     // One warp: bitonic sort of (expert, pair) keys; the pair index makes the
     // order stable.  Sorted position j holds pair order[j]; the first position

@@ -122,9 +122,6 @@ cudaError_t launch_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* 
                         int D, int mode, const uint16_t* sh, const float* gate_logit, uint16_t* out,
                         cudaStream_t s);
 cudaError_t launch_swiglu(const uint16_t* gu, int R, int I, uint16_t* h, cudaStream_t s);
-cudaError_t launch_segment_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* score,
-                                const int32_t* row_start, int R, int D, uint16_t* y,
-                                cudaStream_t s);
 cudaError_t launch_affine_quantize(const float* w, long long rows, int K, uint32_t* wq,
                                    uint16_t* scales, uint16_t* biases, cudaStream_t s);
 cudaError_t launch_prepare_tables(const uint16_t* scales, const uint16_t* biases, int E, int N, int G,

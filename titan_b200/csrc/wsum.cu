@@ -83,45 +83,6 @@ cudaError_t launch_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* 
   return cudaGetLastError();
 }
 
-// Expert-parallel partial sum: for each received row r, the weighted sum of
-// the expert outputs of its pairs q in [row_start[r], row_start[r+1]) (the
-// experts of this rank that the row's token selected), fp32 in pair order,
-// rounded to bf16 once: y[r] = bf16(sum_q score[q] * ys[inv[q]]).
-__global__ void __launch_bounds__(256) segment_wsum_kernel(
-    const uint16_t* __restrict__ ys, const int32_t* __restrict__ inv,
-    const uint16_t* __restrict__ score, const int32_t* __restrict__ row_start, int R, int D,
-    uint16_t* __restrict__ y) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int dv = D / 8;
-  if (i >= (long long)R * dv) return;
-  const int r = (int)(i / dv), d0 = (int)(i % dv) * 8;
-  float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int q = row_start[r]; q < row_start[r + 1]; ++q) {
-    const float sc = bf2f(score[q]);
-    const uint4 v = *reinterpret_cast<const uint4*>(ys + (size_t)inv[q] * D + d0);
-    float f[8];
-    unpack8_bf16(v, f);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) a[c] = __fmaf_rn(sc, f[c], a[c]);
-  }
-  uint4 o;
-  o.x = (uint32_t)f2bf(a[0]) | ((uint32_t)f2bf(a[1]) << 16);
-  o.y = (uint32_t)f2bf(a[2]) | ((uint32_t)f2bf(a[3]) << 16);
-  o.z = (uint32_t)f2bf(a[4]) | ((uint32_t)f2bf(a[5]) << 16);
-  o.w = (uint32_t)f2bf(a[6]) | ((uint32_t)f2bf(a[7]) << 16);
-  *reinterpret_cast<uint4*>(y + (size_t)r * D + d0) = o;
-}
-
-cudaError_t launch_segment_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* score,
-                                const int32_t* row_start, int R, int D, uint16_t* y,
-                                cudaStream_t s) {
-  const long long n = (long long)R * (D / 8);
-  if (n > 0)
-    segment_wsum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ys, inv, score, row_start, R,
-                                                                    D, y);
-  return cudaGetLastError();
-}
-
 // SwiGLU over a [R, 2I] gate|up tensor, bf16 rounding after each op.
 __global__ void __launch_bounds__(256) swiglu_kernel(const uint16_t* __restrict__ gu, long long R,
                                                      int I, uint16_t* __restrict__ h) {

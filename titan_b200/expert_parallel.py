@@ -1,0 +1,211 @@
+"""Expert parallelism for the quantised MoE block.
+
+Experts are sharded over W ranks, expert e on rank e // (E / W); the router
+and the shared expert stay data-parallel (each rank serves its own tokens).
+A layer takes two all-to-all exchanges (the reference runs one device and has
+no counterpart; the partitioning follows its block,
+titan/adapters/mlx/vendor/mlx_vlm/models/qwen3_5_moe/language.py:60-91):
+
+  dispatch  each token row goes once to every rank that owns at least one of
+            its k experts (deduplicated per destination rank, not per
+            expert), with the k-wide local expert ids of the slots served
+            there (-1 elsewhere);
+  combine   each owner returns one bf16 row per (token, slot) it served: the
+            expert output itself, the same bits the single-device block
+            computes for that slot.
+
+The source then runs the block's own weighted sum (clone mode, with the
+sigmoid-gated shared expert) over the k outputs of every token, so the
+expert-parallel layer reproduces the single-device layer bit for bit wherever
+the experts' arithmetic is fixed-order (the int8 path).
+
+Plumbing is ``torch.distributed`` (NCCL on GPUs, gloo in the CPU tests); the
+expert arithmetic is ``tmoe_moe_experts`` and the final sum
+``tmoe_moe_combine`` from libtitan_moe.so.  The dispatch plan is computed on
+the device with tensor ops; the host reads only the exchanged counts, which
+the variable-size all-to-all needs.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from . import _lib, ops
+
+__all__ = ["DispatchPlan", "plan_dispatch", "pairs_from_meta", "return_slots",
+           "ExpertParallelMoE", "ep_forward"]
+
+
+@dataclass
+class DispatchPlan:
+    send_token: torch.Tensor    # [S] local token of each sent row (destination-major)
+    send_counts: torch.Tensor   # [W] rows per destination rank (int64)
+    local_ids: torch.Tensor     # [S, k] int32 local expert id per slot, -1 if not on that rank
+
+
+def plan_dispatch(idx: torch.Tensor, experts_per_rank: int, world: int) -> DispatchPlan:
+    """Deduplicated dispatch plan of one rank's tokens; idx [T, k] global
+    expert ids.  Rows are ordered by destination rank, then by token."""
+    T, k = idx.shape
+    dest = idx.long() // experts_per_rank                          # [T, k]
+    member = torch.zeros(T, world, dtype=torch.bool, device=idx.device)
+    if T:
+        member.scatter_(1, dest, True)
+    d_idx, t_idx = member.t().nonzero(as_tuple=True)              # destination-major
+    send_counts = member.sum(0).to(torch.int64)
+    on_d = dest[t_idx] == d_idx[:, None]                           # [S, k]
+    local = torch.where(on_d, idx[t_idx].long() - d_idx[:, None] * experts_per_rank,
+                        torch.full_like(dest[t_idx], -1)).to(torch.int32)
+    return DispatchPlan(t_idx, send_counts, local.contiguous())
+
+
+def pairs_from_meta(local_ids: torch.Tensor):
+    """Received k-wide metadata -> the (row, local expert) pairs this rank
+    serves, row-major (row, then slot)."""
+    pair_row, slot = (local_ids >= 0).nonzero(as_tuple=True)
+    pair_exp = local_ids[pair_row, slot]
+    return pair_row.to(torch.int32).contiguous(), pair_exp.to(torch.int32).contiguous()
+
+
+def return_slots(plan: DispatchPlan, T: int, k: int) -> torch.Tensor:
+    """Where each (token, slot) lands in the combine buffer: the owners send
+    their pair outputs back in the order of the sent rows (destination, then
+    token) and, inside a row, of the slots; inv [T*k] int32."""
+    valid = plan.local_ids >= 0
+    r, j = valid.nonzero(as_tuple=True)
+    inv = torch.empty(T * k, dtype=torch.int32, device=plan.local_ids.device)
+    inv[plan.send_token[r] * k + j] = torch.arange(r.numel(), dtype=torch.int32,
+                                                     device=inv.device)
+    return inv
+
+
+def _exchange(t: torch.Tensor, send_counts: list[int], recv_counts: list[int], group) -> torch.Tensor:
+    out = torch.empty((sum(recv_counts),) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.all_to_all_single(out, t.contiguous(), recv_counts, send_counts, group=group)
+    return out
+
+
+def _wire(t: torch.Tensor) -> torch.Tensor:
+    """bf16 rows travel as int32 words (every backend moves those; gloo has
+    no 16-bit types)."""
+    return t.view(torch.int32) if t.dtype == torch.bfloat16 else t
+
+
+def _unwire(t: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+    return t.view(torch.bfloat16) if like.dtype == torch.bfloat16 else t
+
+
+def ep_forward(x: torch.Tensor, idx: torch.Tensor, experts_per_rank: int, expert_fn: Callable,
+               combine_fn: Callable, group=None):
+    """One expert-parallel MoE layer on this rank's tokens x [T, H] with their
+    expert ids idx [T, k].  expert_fn(rows, pair_row, pair_exp) -> [P, H]
+    bf16 applies this rank's experts to the pairs it serves;
+    combine_fn(ys, inv) -> [T, H] bf16 forms the output from every token's k
+    expert outputs ys[inv[t*k + j]]."""
+    world = dist.get_world_size(group)
+    T, k = idx.shape
+    plan = plan_dispatch(idx, experts_per_rank, world)
+    counts = torch.stack([plan.send_counts,
+                          torch.zeros_like(plan.send_counts)], 1)   # rows, slots (filled below)
+    slots_per_row = (plan.local_ids >= 0).sum(1)
+    bounds = torch.cumsum(plan.send_counts, 0)
+    csum = torch.cat([slots_per_row.new_zeros(1), torch.cumsum(slots_per_row, 0)])
+    counts[:, 1] = csum[bounds] - csum[bounds - plan.send_counts]
+    recv = torch.empty_like(counts)
+    dist.all_to_all_single(recv, counts, group=group)
+    c = counts.cpu()
+    rc = recv.cpu()
+    rows_out, rows_in = c[:, 0].tolist(), rc[:, 0].tolist()
+    pairs_back, pairs_recv = c[:, 1].tolist(), rc[:, 1].tolist()
+    rows = _unwire(_exchange(_wire(x[plan.send_token]), rows_out, rows_in, group), x)
+    ids = _exchange(plan.local_ids, rows_out, rows_in, group)
+    pair_row, pair_exp = pairs_from_meta(ids)
+    y_pairs = expert_fn(rows, pair_row, pair_exp)
+    back = _unwire(_exchange(_wire(y_pairs), pairs_recv, pairs_back, group), y_pairs)
+    return combine_fn(back, return_slots(plan, T, k))
+
+
+class ExpertParallelMoE(torch.nn.Module):
+    """A SparseMoeBlock sharded over the ranks of ``group``: this rank holds
+    experts [rank * E/W, (rank+1) * E/W) and a full copy of the router and the
+    shared expert; the constructor slices them out of a full block."""
+
+    def __init__(self, block, group=None):
+        super().__init__()
+        self.group = group
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        E = block.num_experts
+        if E % world:
+            raise _lib.InvalidArgument(f"{E} experts do not split over {world} ranks")
+        self.world, self.rank, self.epr = world, rank, E // world
+        self.hidden, self.top_k = block.hidden, block.top_k
+        self.moe_inter = block.moe_inter
+        lo, hi = rank * self.epr, (rank + 1) * self.epr
+        sm = block.switch_mlp
+        self.gate_weight = block.gate_weight
+        self.gu = (sm.gate_up_proj.weight[lo:hi].contiguous(), sm.gate_up_proj.scales[lo:hi].contiguous(),
+                   sm.gate_up_proj.biases[lo:hi].contiguous())
+        self.dn = (sm.down_proj.weight[lo:hi].contiguous(), sm.down_proj.scales[lo:hi].contiguous(),
+                   sm.down_proj.biases[lo:hi].contiguous())
+        self.tables = (ops.build_tables(*self.gu), ops.build_tables(*self.dn))
+        self.shared_expert = block.shared_expert
+        self.shared_gate = block.shared_expert_gate_weight
+        self._layer = None
+
+    def _layer_struct(self) -> _lib.Layer:
+        if self._layer is None:
+            L = _lib.Layer()
+            L.hidden, L.num_experts, L.top_k = self.hidden, self.epr, self.top_k
+            L.moe_inter, L.shared_inter = self.moe_inter, 0
+            L.gate_up_w, L.gate_up_s, L.gate_up_b = (t.data_ptr() for t in self.gu)
+            L.down_w, L.down_s, L.down_b = (t.data_ptr() for t in self.dn)
+            L.gate_up_st, L.gate_up_bt = self.tables[0].scales_t.data_ptr(), self.tables[0].biases_t.data_ptr()
+            L.down_st, L.down_bt = self.tables[1].scales_t.data_ptr(), self.tables[1].biases_t.data_ptr()
+            self._layer = L
+        return self._layer
+
+    def experts(self, rows, pair_row, pair_exp, options: _lib.Options | None = None):
+        """This rank's routed experts on received rows (tmoe_moe_experts)."""
+        R, P = rows.shape[0], pair_row.numel()
+        y = torch.empty(P, self.hidden, dtype=torch.bfloat16, device=rows.device)
+        if P == 0:
+            return y
+        L = self._layer_struct()
+        opt = options if options is not None else _lib.Options(512, 1, 0, 1, 0)
+        lib = _lib.load()
+        nb = lib.tmoe_moe_experts_workspace_size(L, R, P, opt)
+        ws = ops.workspace(nb, rows.device, "ep")
+        _lib.check(lib.tmoe_moe_experts(L, rows.data_ptr(), R, pair_row.data_ptr(),
+                                        pair_exp.data_ptr(), P, opt, ws.data_ptr(), ws.numel(),
+                                        y.data_ptr(), ops.stream_ptr(rows.device)),
+                   "tmoe_moe_experts")
+        return y
+
+    def combine(self, ys, inv, scores, shared_out, gate_logit, mode: int = 0):
+        """The block's weighted sum plus gated shared expert (tmoe_moe_combine)."""
+        T, k = scores.shape
+        y = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=scores.device)
+        if T == 0:
+            return y
+        _lib.call("tmoe_moe_combine", ys.data_ptr(), inv.data_ptr(), scores.data_ptr(), T, k,
+                  self.hidden, mode, None if shared_out is None else shared_out.data_ptr(),
+                  None if gate_logit is None else gate_logit.data_ptr(), y.data_ptr(),
+                  ops.stream_ptr(scores.device))
+        return y
+
+    def forward(self, x: torch.Tensor, options: _lib.Options | None = None) -> torch.Tensor:
+        xf = x.reshape(-1, self.hidden).contiguous()
+        idx, scores = ops.router_topk(xf, self.gate_weight, self.top_k)
+        shared_out = gate_logit = None
+        if self.shared_expert is not None:
+            gate_logit = (xf.float() @ self.shared_gate.float().t()).reshape(-1).contiguous()
+            shared_out = self.shared_expert(xf).contiguous()
+        mode = options.wsum_mode if options is not None else 0
+        y = ep_forward(xf, idx, self.epr, lambda *a: self.experts(*a, options=options),
+                       lambda ys, inv: self.combine(ys, inv, scores, shared_out, gate_logit, mode),
+                       self.group)
+        return y.reshape(x.shape)
