@@ -762,6 +762,7 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     d.nsh = T;
     d.out = b.part;
     d.counters = b.counters + 1;
+    d.plan_ready = 1;          // the gate_up kernel releases this one after the routing
     d.scores = scores;
     d.T = T;
     d.k = k;

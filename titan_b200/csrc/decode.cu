@@ -211,7 +211,16 @@ __global__ void __launch_bounds__(kThreads, 5) gemv_stream_kernel(StreamParams P
   const int g = lane >> 2, t = lane & 3;
   const int u = blockIdx.x;
   const bool shared = P.Wsh != nullptr && u == P.umax;
-  pdl_trigger();
+  // Dependencies.  The shared expert's gate_up reads only the layer input,
+  // which the router kernel released before triggering this launch.  With
+  // plan_ready the routing was complete when this kernel was released (the
+  // previous kernel triggers only after its own wait), so the expert's rows
+  // can be requested before waiting for the activations.  Everything else
+  // waits first.  This kernel releases the next one only once it is past
+  // that wait, so the next one may read the routing early in turn.
+  const bool independent = MODE == 0 && shared;
+  const bool early_plan = MODE == 1 && P.plan_ready;
+  if (independent) pdl_trigger();
   if (shared) {
     // the shared expert's rows do not depend on the routing: pull this slab
     // into L2 while the previous kernel finishes
@@ -227,11 +236,10 @@ __global__ void __launch_bounds__(kThreads, 5) gemv_stream_kernel(StreamParams P
       }
     }
   }
-  // The shared expert's gate_up reads only the layer input, which the router
-  // kernel released before triggering this launch; everything else waits for
-  // the routing.
-  const bool independent = MODE == 0 && shared;
-  if (!independent) pdl_wait();
+  if (!independent && !early_plan) {
+    pdl_wait();
+    pdl_trigger();
+  }
   const int nuniq = independent ? 0 : P.nuniq[0];
   if (!shared && u >= nuniq) return;
   const int e = shared ? 0 : P.uexp[u];
@@ -257,32 +265,38 @@ __global__ void __launch_bounds__(kThreads, 5) gemv_stream_kernel(StreamParams P
   uint8_t* wsm = sm + warp * L.warp_bytes;
 
   // ---- copies, in the order they are needed: the first pass's activation
-  // columns (commit group 0), then the weight rows of the first half of the
-  // quarter's groups (group 1) and of the second half (group 2)
+  // columns (one commit group), then the weight rows of the first half of the
+  // quarter's groups and of the second half (two groups).  With early_plan the
+  // weights go first and the columns follow the wait.
   const int ncol_first = min(ncol, ncol_all);
-  issue_columns<MODE>(P, L, wsm, shared, p0, 0, ncol_first, g0 * kGroup, ng * kGroup, lane);
-  cp_async_commit();
   const int nh = (ng + 1) / 2;                   // groups in the first weight half
-  for (int part = 0; part < 2; ++part) {
-    // all lanes busy: (row, chunk) of copy i = lane + 32 j, stepped without division
-    const int j0 = part ? nh : 0;
-    const int chunks = ((part ? ng : nh) - j0) * 2;   // 16-byte chunks per row slice
-    if (chunks > 0) {
-      const int dr = 32 / chunks, dc = 32 % chunks;
-      int r = lane / chunks, c = lane % chunks;
-      for (; r < kSlabRows;) {
-        cp_async16(wsm + L.w_off + r * L.wstride + j0 * 32 + c * 16,
-                   We + (size_t)wrow_of(r) * KW + (g0 + j0) * 8 + c * 4);
-        r += dr;
-        c += dc;
-        if (c >= chunks) {
-          c -= chunks;
-          ++r;
+  auto issue_weights = [&]() {
+    for (int part = 0; part < 2; ++part) {
+      // all lanes busy: (row, chunk) of copy i = lane + 32 j, stepped without division
+      const int j0 = part ? nh : 0;
+      const int chunks = ((part ? ng : nh) - j0) * 2;   // 16-byte chunks per row slice
+      if (chunks > 0) {
+        const int dr = 32 / chunks, dc = 32 % chunks;
+        int r = lane / chunks, c = lane % chunks;
+        for (; r < kSlabRows;) {
+          cp_async16(wsm + L.w_off + r * L.wstride + j0 * 32 + c * 16,
+                     We + (size_t)wrow_of(r) * KW + (g0 + j0) * 8 + c * 4);
+          r += dr;
+          c += dc;
+          if (c >= chunks) {
+            c -= chunks;
+            ++r;
+          }
         }
       }
+      cp_async_commit();
     }
+  };
+  if (!early_plan) {
+    issue_columns<MODE>(P, L, wsm, shared, p0, 0, ncol_first, g0 * kGroup, ng * kGroup, lane);
     cp_async_commit();
   }
+  issue_weights();
   // ---- scales of row `lane`: loads issued now, converted after the first
   // activation columns are staged so both latencies overlap
   const size_t ro = (size_t)wrow_of(lane) * G + g0;
@@ -305,6 +319,13 @@ __global__ void __launch_bounds__(kThreads, 5) gemv_stream_kernel(StreamParams P
     }
   };
 
+  if (early_plan) {
+    pdl_wait();                                  // the activations are ready now
+    pdl_trigger();
+    issue_columns<MODE>(P, L, wsm, shared, p0, 0, ncol_first, g0 * kGroup, ng * kGroup, lane);
+    cp_async_commit();
+  }
+
   const uint8_t* w0p = wsm + L.w_off + g * L.wstride + t * 8;
   const float2* sbp = reinterpret_cast<const float2*>(wsm + L.sb_off);
   const uint8_t* xhp = wsm + L.xh_off;
@@ -319,6 +340,8 @@ __global__ void __launch_bounds__(kThreads, 5) gemv_stream_kernel(StreamParams P
       issue_columns<MODE>(P, L, wsm, shared, p0, cb, nc, g0 * kGroup, ng * kGroup, lane);
       cp_async_commit();
       cp_async_wait<0>();
+    } else if (early_plan) {
+      cp_async_wait<0>();                        // weights and activation columns
     } else {
       cp_async_wait<2>();                        // the activation columns
     }
@@ -381,11 +404,11 @@ __global__ void __launch_bounds__(kThreads, 5) gemv_stream_kernel(StreamParams P
         acc[m][3] = __fmaf_rn(hi.x, d[m][3], __fmaf_rn(hi.y, xs1, acc[m][3]));
       }
     };
-    if (cb == 0) cp_async_wait<1>();             // the first weight half
+    if (cb == 0 && !early_plan) cp_async_wait<1>();   // the first weight half
     __syncwarp();
 #pragma unroll 1
     for (int j = 0; j < nh; ++j) group(j);
-    if (cb == 0) cp_async_wait<0>();             // the second half
+    if (cb == 0 && !early_plan) cp_async_wait<0>();   // the second half
     __syncwarp();
 #pragma unroll 1
     for (int j = nh; j < ng; ++j) group(j);

@@ -83,6 +83,8 @@ struct StreamParams {
   const float* gate_logit;  // mode 1 with a shared expert: fp32 [T]
   int T, k;
   uint16_t* y;            // mode 1: bf16 [T][N]
+  int plan_ready;         // mode 1: the routing was complete when the previous kernel
+                          // released this launch (it reads it before its wait)
 };
 
 size_t gemv_stream_smem(int K, int ncol, bool lo);
