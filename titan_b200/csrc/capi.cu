@@ -714,6 +714,7 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     }
     StreamParams q{};
     q.x = x;
+    q.tokens = T == 1 ? 1 : 0;
     q.K = H;
     q.K_sh = H;
     q.W = L->gate_up_w;

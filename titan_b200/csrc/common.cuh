@@ -168,6 +168,16 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// Ticket for "the last CTA to arrive does the rest": called by one thread
+// after a CTA barrier, it publishes the CTA's prior writes (release, made
+// cumulative by the barrier) and, for the last arrival, makes every other
+// CTA's published writes visible (acquire).  Returns the previous count.
+TMOE_DEV int ticket_acq_rel(int* counter) {
+  int prev;
+  asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(counter) : "memory");
+  return prev;
+}
+
 TMOE_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
 template <int N>
 TMOE_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }

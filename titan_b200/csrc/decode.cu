@@ -123,9 +123,10 @@ TMOE_DEV void issue_columns(const StreamParams& P, const GemvPlan& L, uint8_t* w
     if (MODE == 1)
       src = reinterpret_cast<const uint8_t*>(shared ? P.h_sh + (size_t)col * K
                                                     : P.h + (size_t)P.order[p0 + col] * K);
-    else
+    else  // one token: every column is row 0, no lookup of the plan's order
       src = reinterpret_cast<const uint8_t*>(
-          P.x + (size_t)(shared ? col : P.order[p0 + col] / P.col_div) * K);
+          P.x + (size_t)(shared || P.tokens == 1 ? (shared ? col : 0)
+                                                  : P.order[p0 + col] / P.col_div) * K);
     src += (size_t)k0 * esz;
     for (int i = lane; i < chunks; i += 32)
       cp_async16(wsm + L.raw_off + c * L.rstride + i * 16, src + i * 16);
@@ -452,15 +453,13 @@ __global__ void __launch_bounds__(kThreads, 5) gemv_stream_kernel(StreamParams P
     // weighted sum over the k slots plus the gated shared expert.  Nobody
     // waits: every CTA counts itself in and only the last one does the sum.
     __shared__ int last;
-    __threadfence();
     __syncthreads();
     if (tid == 0) {
       const int contributors = nuniq + (P.Wsh ? 1 : 0);
-      last = (atomicAdd(&P.counters[slab], 1) == contributors - 1);
+      last = (ticket_acq_rel(&P.counters[slab]) == contributors - 1);
     }
     __syncthreads();
     if (!last) return;
-    __threadfence();
     const int D = P.N;
     for (int i = tid; i < P.T * kSlabRows; i += kThreads) {
       const int tt = i / kSlabRows, d = slab * kSlabRows + (i % kSlabRows);

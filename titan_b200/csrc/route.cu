@@ -376,12 +376,10 @@ __global__ void __launch_bounds__(128) decode_route_kernel(
   }
 
   // ---- the last CTA to finish routes every token
-  __threadfence();
   __syncthreads();
-  if (tid == 0) s_last = (atomicAdd(&counters[0], 1) == (int)gridDim.x - 1);
+  if (tid == 0) s_last = (ticket_acq_rel(&counters[0]) == (int)gridDim.x - 1);
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   const int R = T * k;
   for (int i = tid; i < ncounters; i += 128) counters[1 + i] = 0;
   if (R > 32)

@@ -83,6 +83,8 @@ struct StreamParams {
   const float* gate_logit;  // mode 1 with a shared expert: fp32 [T]
   int T, k;
   uint16_t* y;            // mode 1: bf16 [T][N]
+  int tokens;             // modes 0/2: number of activation rows when known to be 1
+                          // (then every column is row 0), else 0
   int plan_ready;         // mode 1: the routing was complete when the previous kernel
                           // released this launch (it reads it before its wait)
 };
