@@ -59,6 +59,11 @@ def parse():
                     help="run a small untimed case for an ncu capture and exit")
     ap.add_argument("--gemm-kernel", type=int, default=0,
                     help="prefill grouped GEMMs: 0 tcgen05 (default), 1 mma.sync baseline")
+    ap.add_argument("--workload", choices=("decode", "ep"), default="decode",
+                    help="decode: the headline (replicas at N>1); ep: config 4, expert "
+                         "parallelism over the N ranks (strong scaling)")
+    ap.add_argument("--ep-tokens", type=int, default=8192, help="ep: global tokens per step")
+    ap.add_argument("--ep-layers", type=int, default=36, help="ep: layers per step")
     return ap.parse_args()
 
 
@@ -380,6 +385,127 @@ def bench_prefill(args, world, device):
     return out
 
 
+def zipf_router_(blk, gen, s=1.1):
+    """Expert popularity ~ Zipf(s): column 0 of the router carries
+    -s*log(rank) for a seeded random ranking of the experts (the tokens'
+    x[:, 0] is 1), the other columns N(0, 1.28/sqrt(H)) so that every
+    logit gets noise of the Gumbel's spread and top-k approximates sampling
+    k experts without replacement from the Zipf law."""
+    import torch
+    E, H = blk.gate_weight.shape
+    perm = torch.randperm(E, generator=gen).to(blk.gate_weight.device)
+    bias = torch.empty(E, device=blk.gate_weight.device)
+    bias[perm] = -s * torch.log(torch.arange(1, E + 1, device=bias.device, dtype=torch.float32))
+    w = torch.randn(E, H, generator=gen).to(blk.gate_weight.device) * (1.28 / math.sqrt(H - 1))
+    w[:, 0] = bias
+    with torch.no_grad():
+        blk.gate_weight.copy_(w.to(torch.bfloat16))
+
+
+def run_ep(args, world, rank, local):
+    """Config 4: expert parallelism over the N ranks, strong scaling.  Every
+    rank builds the same layers (same seeds) and keeps experts
+    [rank*E/N, (rank+1)*E/N); it serves ep_tokens/N tokens per layer: router,
+    shared expert and weighted sum on its own tokens, the routed experts of
+    the tokens of every rank that chose one of its experts (two NCCL
+    all-to-alls per layer).  value = global tokens per second."""
+    import torch
+    from titan_b200 import SparseMoeBlock, _lib
+    from titan_b200.expert_parallel import ExpertParallelMoE
+    import torch.distributed as dist
+    _lib.load()
+    device = torch.device("cuda", torch.cuda.current_device())
+    own_group = not dist.is_initialized()
+    if own_group:                     # N=1: a one-rank group, so the same code path runs
+        import socket
+        so = socket.socket()
+        so.bind(("127.0.0.1", 0))
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(so.getsockname()[1]))
+        so.close()
+        dist.init_process_group("nccl", rank=0, world_size=1,
+                                timeout=datetime.timedelta(seconds=300))
+    try:
+        return _run_ep(args, world, rank, local, device)
+    finally:
+        if own_group:
+            dist.destroy_process_group()
+
+
+def _run_ep(args, world, rank, local, device):
+    import torch
+    from titan_b200 import SparseMoeBlock, _lib
+    from titan_b200.expert_parallel import ExpertParallelMoE
+    c = CFG2
+    if args.ep_tokens % world:
+        raise SystemExit(f"--ep-tokens {args.ep_tokens} does not split over {world} ranks")
+    T = args.ep_tokens // world
+    layers = []
+    for l in range(args.ep_layers):
+        torch.manual_seed(4321 + l)
+        blk = SparseMoeBlock(c["H"], c["E"], c["k"], c["I"], c["Is"], device=device,
+                             weight_std=0.02)
+        zipf_router_(blk, torch.Generator().manual_seed(777 + l))
+        layers.append(ExpertParallelMoE(blk))
+        del blk
+    torch.cuda.empty_cache()
+    gen = torch.Generator(device=device).manual_seed(9000 + rank)
+    x = torch.randn(T, c["H"], generator=gen, device=device)
+    x[:, 0] = 1.0
+    x = x.to(torch.bfloat16)
+    opts = _lib.Options()
+    opts.min_tokens, opts.int8_prefill, opts.down_int8, opts.wsum_mode = 1, 1, 1, 0
+    # routing statistics of layer 0 over this rank's tokens
+    from titan_b200 import ops
+    idx, _ = ops.router_topk(x, layers[0].gate_weight, c["k"])
+    dest = (idx.long() // (c["E"] // world))
+    member = torch.zeros(T, world, dtype=torch.bool, device=device)
+    member.scatter_(1, dest, True)
+    ranks_per_token = float(member.sum(1).float().mean())
+    counts = torch.bincount(idx.reshape(-1).long(), minlength=c["E"]).float()
+    top_share = float(counts.sort(descending=True).values[:10].sum() / counts.sum())
+
+    def step():
+        for ep in layers:
+            ep(x, options=opts)
+
+    clk = Clocks(local).__enter__()
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk.__exit__(None, None, None)
+    ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
+    if rank != 0:
+        return 0
+    line = {
+        "metric": "moe_ep_tokens_per_s", "value": round(args.ep_tokens / (ms * 1e-3), 1),
+        "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "us_per_layer": round(1000 * ms / args.ep_layers, 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8 x int4 (tcgen05 f16 exact), f32 acc", "data": "synthetic",
+        "config": {"workload": f"config4 EP: {args.ep_layers} config-2 layers (H=2048, 512+1 "
+                               f"experts, I=512, top-10), {args.ep_tokens} tokens per step, "
+                               "Zipf(1.1) expert popularity",
+                   "tokens_per_rank": T, "experts_per_rank": c["E"] // world,
+                   "parallelism": f"ep{world}", "collective": "2 NCCL all-to-alls per layer",
+                   "l2": f"inputs larger than L2: {args.ep_layers} layers of weights cycled",
+                   "timing": "CUDA events around the step, max over ranks"},
+        "routing": {"ranks_per_token": round(ranks_per_token, 2),
+                    "top10_expert_share": round(top_share, 4)},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # -------------------------------------------------------------- CPU baseline
 
 def host_layer(rng, c):
@@ -474,6 +600,8 @@ def run_titan(args, world, rank, local):
         "gemv_down": (uniq + 1) * c["H"] * (c["I"] // 2 + c["I"] // 64 * 4),
         "router_logits": (c["E"] + 1) * c["H"] * 2,
         "decode_route": (c["E"] + 1) * c["H"] * 2,     # router rows; routing is on-chip
+        # the whole layer: selected + shared experts, router rows, x and y
+        "decode_layer": sweep[str(HEADLINE_T)]["bytes_per_layer"],
     }
     name = dom[0]
     alg = per_launch.get(name)
@@ -485,6 +613,12 @@ def run_titan(args, world, rank, local):
                 "algorithmic_bytes_per_launch": int(alg),
                 "us_per_launch": round(dom[1]["us_per_launch"], 3),
                 "traffic": traffic.get(name)}
+    # per-kernel profile at other batch sizes (one pass over the layers)
+    stages_by_T = {}
+    for Tp in (2, 8):
+        xp = torch.randn(Tp, CFG2["H"], device=device).to(torch.bfloat16)
+        st, _ = stage_profile([lambda b=b: b(xp, options=opts) for b in blocks], reps=1)
+        stages_by_T[str(Tp)] = {k: round(v["us_per_launch"], 3) for k, v in st.items()}
     e2e = bench_e2e(blocks, opts, HEADLINE_T, max(3, args.steps // 2), args.warmup, world)
     del blocks
     torch.cuda.empty_cache()
@@ -510,6 +644,7 @@ def run_titan(args, world, rank, local):
         "roofline": roof, "cpu_baseline": cb, "e2e": e2e, "gpu_launches": launches * args.steps,
         "clocks": clocks, "decode_sweep": sweep, "prefill_config3": prefill,
         "decode_stages_us": {k: round(v["us_per_launch"], 3) for k, v in stages.items()},
+        "decode_stages_us_by_T": stages_by_T,
         "bytes_per_layer": int(nbytes / args.layers),
     }
     print(json.dumps(line), flush=True)
@@ -559,6 +694,8 @@ def main():
         return run_reference(args, world, rank)
     world, rank, local = dist_setup(args)
     try:
+        if args.workload == "ep":
+            return run_ep(args, world, rank, local)
         return run_titan(args, world, rank, local)
     finally:
         if world > 1:

@@ -37,7 +37,7 @@ enum {
   TMOE_ERR_WORKSPACE = 6    /* workspace missing or smaller than required    */
 };
 
-#define TMOE_ABI_VERSION 2
+#define TMOE_ABI_VERSION 3
 
 int tmoe_abi_version(void);
 const char* tmoe_last_error(void);
@@ -214,7 +214,11 @@ typedef struct tmoe_options {
                        bf16-activation grouped GEMMs for the prefill path */
   int gemm_kernel;  /* prefill GEMMs: 0 = tcgen05 / TMEM (default),
                        1 = mma.sync (the comparison baseline) */
-} tmoe_options;     /* NULL options = {512, 1, 0, 1, 0} */
+  int decode_kernel; /* decode path (T < min_tokens): 0 = the whole layer in
+                        one launch where the shape allows it (T <= 4, H, I
+                        and Is multiples of 512), else 1 = router, gate_up
+                        and down as three launches (always available) */
+} tmoe_options;     /* NULL options = {512, 1, 0, 1, 0, 0} */
 
 /* Device-side error record of the bounded waits inside the tcgen05 kernels
  * (no reference counterpart).  Synchronises the device; returns 0 when no

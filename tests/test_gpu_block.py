@@ -36,13 +36,26 @@ def _block(oracle, H, E, k, I, Is, seed, cuda):
     return blk, L
 
 
-def _opts(min_tokens, int8=1, down_int8=1, wsum=0, kernel=0):
-    """kernel 0 = tcgen05 grouped GEMMs (default), 1 = mma.sync baseline."""
+def _opts(min_tokens, int8=1, down_int8=1, wsum=0, kernel=0, decode_kernel=0):
+    """kernel 0 = tcgen05 grouped GEMMs (default), 1 = mma.sync baseline;
+    decode_kernel 0 = the layer in one launch where it applies, 1 = three."""
     from titan_b200 import _lib
     o = _lib.Options()
     o.min_tokens, o.int8_prefill, o.down_int8, o.wsum_mode = min_tokens, int8, down_int8, wsum
     o.gemm_kernel = kernel
+    o.decode_kernel = decode_kernel
     return o
+
+
+def _launches(fn):
+    from titan_b200 import _lib
+    names = []
+    _lib.set_stage_hook(names.append)
+    try:
+        out = fn()
+    finally:
+        _lib.set_stage_hook(None)
+    return out, names
 
 
 KERNELS = pytest.mark.parametrize("kernel", [0, 1], ids=["tcgen05", "mma_sync"])
@@ -57,6 +70,68 @@ def test_decode_block_vs_golden(cuda, oracle, T):
     assert np.array_equal(idx.cpu().numpy(), ridx)
     assert np.array_equal(nbf(sc), rsc)
     assert_bf16_close(nbf(y), ry, what=f"decode T={T}")
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 4])
+def test_decode_single_launch_vs_three_launches(cuda, oracle, T):
+    """The one-launch decode layer (grid barriers, routing in every CTA) and
+    the three-launch pipeline on BASELINE config-2 shapes: identical routing,
+    both within tolerance of the oracle, and the one-launch path really is a
+    single launch."""
+    from titan_b200 import SparseMoeBlock, _lib
+    torch.manual_seed(40 + T)
+    blk = SparseMoeBlock(2048, 512, 10, 512, 512, device=cuda)
+    blk.prepare()                      # weight tables built outside the recorded call
+    L = layer_from_block(oracle, blk)
+    x = oracle.make_x(T, 2048, seed=300 + T)
+    (y0, i0, s0), names = _launches(
+        lambda: blk(bf(x), options=_opts(512), return_routing=True))
+    assert names == ["decode_layer"], names
+    (y1, i1, s1), names1 = _launches(
+        lambda: blk(bf(x), options=_opts(512, decode_kernel=1), return_routing=True))
+    assert "decode_layer" not in names1
+    ry, ridx, rsc = oracle.moe_decode(L, x)
+    assert np.array_equal(i0.cpu().numpy(), ridx)
+    assert np.array_equal(i1.cpu().numpy(), ridx)
+    assert np.array_equal(nbf(s0), rsc)
+    assert np.array_equal(nbf(s1), rsc)
+    assert_bf16_close(nbf(y0), ry, what=f"one-launch decode T={T}")
+    assert_bf16_close(nbf(y1), ry, what=f"three-launch decode T={T}")
+    assert _lib.load().tmoe_device_status() == 0
+
+
+def test_decode_single_launch_repeats_and_graph(cuda, oracle):
+    """Many launches in a row reuse the self-resetting grid barriers: the
+    same input gives the same bits every time, eagerly and replayed from a
+    CUDA graph, with layers of different expert counts interleaved."""
+    from titan_b200 import SparseMoeBlock, _lib
+    torch.manual_seed(7)
+    blocks = [SparseMoeBlock(2048, E, 10, 512, 512, device=cuda) for E in (512, 128, 512)]
+    x = bf(oracle.make_x(1, 2048, seed=9))
+    ref = [b(x, options=_opts(512)) for b in blocks]
+    for _ in range(20):
+        for b, r in zip(blocks, ref):
+            assert torch.equal(b(x, options=_opts(512)).view(torch.int16), r.view(torch.int16))
+    opts = _opts(512)
+    outs = []
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for b in blocks:
+            b(x, options=opts)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for b in blocks:
+            outs.append(b(x, options=opts))
+    for _ in range(10):
+        g.replay()
+    torch.cuda.synchronize()
+    for o, r in zip(outs, ref):
+        assert torch.equal(o.view(torch.int16), r.view(torch.int16))
+    del g
+    assert _lib.load().tmoe_device_status() == 0
 
 
 def test_decode_block_full_expert_count(cuda, oracle):

@@ -13,7 +13,7 @@ import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libtitan_moe.so")
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class TmoeError(RuntimeError):
@@ -77,7 +77,7 @@ class Options(C.Structure):
     """struct tmoe_options."""
 
     _fields_ = [("min_tokens", I32), ("down_int8", I32), ("wsum_mode", I32), ("int8_prefill", I32),
-                ("gemm_kernel", I32)]
+                ("gemm_kernel", I32), ("decode_kernel", I32)]
 
 
 STAGE_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_char_p)

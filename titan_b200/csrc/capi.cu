@@ -81,6 +81,8 @@ void tmoe_set_stage_hook(tmoe_stage_fn fn, void* ctx) {
 int tmoe_device_status(void) {
   cudaDeviceSynchronize();
   if (tc05_error_flag()) return fail(TMOE_ERR_TIMEOUT, "a tcgen05 kernel's bounded wait timed out");
+  if (layer_error_flag())
+    return fail(TMOE_ERR_TIMEOUT, "a grid barrier of the single-launch decode layer timed out");
   return TMOE_OK;
 }
 
@@ -561,6 +563,7 @@ int opt_down_int8(const tmoe_options* o) { return o ? (o->down_int8 != 0) : 1; }
 int opt_wsum(const tmoe_options* o) { return o ? o->wsum_mode : 0; }
 int opt_int8(const tmoe_options* o) { return o ? (o->int8_prefill != 0) : 1; }
 int opt_tc05(const tmoe_options* o) { return o ? (o->gemm_kernel == 0) : 1; }
+int opt_layer(const tmoe_options* o) { return o ? (o->decode_kernel == 0) : 1; }
 
 size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt, BlockWs* out) {
   const int H = L->hidden, E = L->num_experts, k = L->top_k, I = L->moe_inter,
@@ -698,6 +701,46 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   p.inv = b.inv;
   p.offsets = b.offsets;
 
+  if (!prefill && opt_layer(opt)) {
+    const int ns = decode_layer_stages(T, H, E, k, I, Is, decode_layer_ctas());
+    if (ns > 0) {
+      // the whole layer in one launch
+      LayerArgs a{};
+      a.x = x;
+      a.wr = L->router_w;
+      a.wg = wg;
+      a.guw = L->gate_up_w;
+      a.gus = L->gate_up_s;
+      a.gub = L->gate_up_b;
+      a.dnw = L->down_w;
+      a.dns = L->down_s;
+      a.dnb = L->down_b;
+      if (Is > 0) {
+        a.sguw = L->shared_gate_up_w;
+        a.sgus = L->shared_gate_up_s;
+        a.sgub = L->shared_gate_up_b;
+        a.sdnw = L->shared_down_w;
+        a.sdns = L->shared_down_s;
+        a.sdnb = L->shared_down_b;
+      }
+      a.logits = b.logits;
+      a.gate_logit = b.gate_logit;
+      a.h = b.h;
+      a.hs = b.hs;
+      a.bar = b.counters + 1;
+      a.idx = idx;
+      a.scores = scores;
+      a.y = y;
+      a.T = T;
+      a.H = H;
+      a.E = E;
+      a.k = k;
+      a.I = I;
+      a.Is = Is;
+      TMOE_TRY(launch_decode_layer(a, ns, s), "decode_layer");
+      return TMOE_OK;
+    }
+  }
   if (!prefill) {
     p.uexp = b.uexp;
     p.ustart = b.ustart;

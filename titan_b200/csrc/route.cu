@@ -18,6 +18,7 @@
 // (moe_gather_int8.py:132-165).  It runs once per token; the grouped GEMM
 // gathers the quantised token rows of each expert tile itself.
 #include "common.cuh"
+#include "fragments.cuh"
 #include "tmoe_internal.h"
 
 namespace tmoe {
@@ -280,30 +281,6 @@ cudaError_t launch_route_plan(const int32_t* idx, int R, int E, int tile_m, int 
 // that wait, so it may read this layer's input without waiting for us.
 constexpr int kDrRows = 8;         // rows per CTA (4 per warp, warps 0-1)
 constexpr int kDrTok = 8;          // tokens per pass
-
-TMOE_DEV float tree8(float v) {
-  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
-  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
-  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
-  return v;
-}
-
-// One canonical partial (chunks p, p+8, ...) of one row for NT tokens.
-template <int NT>
-TMOE_DEV void router_dots(const uint4* wrow_s, const uint4* xsm, int nch, int p, float* acc) {
-#pragma unroll 4
-  for (int c = p; c < nch; c += 8) {
-    float wf[8];
-    unpack8_bf16(wrow_s[c], wf);
-#pragma unroll
-    for (int tt = 0; tt < NT; ++tt) {
-      float xf[8];
-      unpack8_bf16(xsm[tt * nch + c], xf);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) acc[tt] = __fmaf_rn(xf[q], wf[q], acc[tt]);
-    }
-  }
-}
 
 template <int PER>
 __global__ void __launch_bounds__(128) decode_route_kernel(

@@ -119,6 +119,33 @@ cudaError_t launch_gemm_tc05(bool int8, int epi, const GemmParams& P, int maxt, 
 cudaError_t launch_prep_a16(const uint16_t* x, int R, int K, bool quant, uint16_t* a16, float* xsc,
                             float* xrs, cudaStream_t s);
 int tc05_error_flag();
+
+// Single-launch decode layer (decode_layer.cu), T <= kLayerMaxT tokens.
+struct LayerArgs {
+  const uint16_t* x;                                   // [T][H] bf16
+  const uint16_t* wr;                                  // router [E][H] bf16
+  const uint16_t* wg;                                  // shared-expert gate [H] or null
+  const uint32_t* guw; const uint16_t* gus; const uint16_t* gub;     // gate_up [E][2I][..]
+  const uint32_t* dnw; const uint16_t* dns; const uint16_t* dnb;     // down [E][H][..]
+  const uint32_t* sguw; const uint16_t* sgus; const uint16_t* sgub;  // shared gate_up [2Is][..]
+  const uint32_t* sdnw; const uint16_t* sdns; const uint16_t* sdnb;  // shared down [H][..]
+  uint16_t* logits;      // [T][E] workspace
+  float* gate_logit;     // [T]
+  float* h;              // [T*k][I] fp32
+  float* hs;             // [T][Is] fp32
+  int32_t* bar;          // 4 words: barrier counts and generations (counts zero between launches)
+  int32_t* idx;          // [T][k] out
+  uint16_t* scores;      // [T][k] out
+  uint16_t* y;           // [T][H] out
+  int T, H, E, k, I, Is;
+};
+constexpr int kLayerMaxT = 4;
+// Ring stages for the plan (2..4), or 0 when the shape cannot take this path.
+int decode_layer_stages(int T, int H, int E, int k, int I, int Is, int nct);
+int decode_layer_ctas();
+size_t decode_layer_smem(int T, int H, int E, int k, int I, int Is, int nct, int ns);
+cudaError_t launch_decode_layer(const LayerArgs& a, int ns, cudaStream_t s);
+int layer_error_flag();
 cudaError_t launch_to_f16p(const uint16_t* x, long long n, uint16_t* y, cudaStream_t s);
 cudaError_t launch_prep_x(const uint16_t* x, int R, int K, uint16_t* x16p, float* xsum,
                           long long sum_sm, long long sum_sg, cudaStream_t s);
