@@ -483,6 +483,18 @@ def _run_ep(args, world, rank, local, device):
     barrier(world)
     clk.__exit__(None, None, None)
     ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
+    # phase breakdown of one more step (events between phases, summed over layers)
+    marks_all = []
+    for ep in layers:
+        marks = []
+        ep(x, options=opts, marks=marks)
+        marks_all.append(marks)
+    torch.cuda.synchronize()
+    phases = {}
+    for marks in marks_all:
+        for (_, a0), (name, b0) in zip(marks, marks[1:]):
+            phases[name] = phases.get(name, 0.0) + a0.elapsed_time(b0)
+    phases = {k: round(1000 * v / len(layers), 1) for k, v in phases.items()}
     if rank != 0:
         return 0
     line = {
@@ -498,6 +510,7 @@ def _run_ep(args, world, rank, local, device):
                    "parallelism": f"ep{world}", "collective": "2 NCCL all-to-alls per layer",
                    "l2": f"inputs larger than L2: {args.ep_layers} layers of weights cycled",
                    "timing": "CUDA events around the step, max over ranks"},
+        "phases_us_per_layer_rank0": phases,
         "routing": {"ranks_per_token": round(ranks_per_token, 2),
                     "top10_expert_share": round(top_share, 4)},
         "clocks": clk.summary(),

@@ -546,6 +546,13 @@ struct BlockWs {
   int32_t *order, *inv, *offsets, *tile_row, *tile_exp, *ntiles, *uexp, *ustart, *nuniq;
   void* route_scratch;
   // decode
+  int32_t* epoch;              // single-launch decode layer: launch epoch (offset 0, every path)
+  unsigned long long* gucnt;   // ... its gate_up-tiles-done counter (offset 256)
+  // ... and its exchanges: epoch-tagged logits and gate logits, CTA start
+  // marks, h of the routed pairs and of the shared expert
+  unsigned long long *tlog, *tgate;
+  int32_t* tseen;
+  uint32_t *th, *ths;
   int32_t* counters;
   uint16_t* x16p;
   float *xsum, *h, *hs, *part, *part_sh;
@@ -572,8 +579,12 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
   const bool prefill = T >= opt_min_tokens(opt);
   const int maxt = max_tiles(R, E);
   BlockWs b{};
-  // Self-resetting counters first, at the same offset on every path: the
-  // decode router's ticket and one combine counter per 32-row output slab.
+  // The single-launch decode layer's epoch word and gate_up counter first, at
+  // the same offsets for every path and shape (only that kernel writes them),
+  // then the self-resetting counters: the decode router's ticket and one
+  // combine counter per 32-row output slab.
+  b.epoch = c.take<int32_t>(1);
+  b.gucnt = c.take<unsigned long long>(1);
   b.counters = c.take<int32_t>(H / 32 + 1);
   b.logits = c.take<uint16_t>((size_t)T * E);
   b.gate_logit = c.take<float>(T > 0 ? T : 1);
@@ -584,6 +595,13 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
   b.offsets = c.take<int32_t>(E + 1);
   b.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(R, E));
   if (!prefill) {
+    if (T <= kLayerMaxT) {
+      b.tlog = c.take<unsigned long long>((size_t)T * E);
+      b.tgate = c.take<unsigned long long>(T);
+      b.tseen = c.take<int32_t>(kLayerMaxCtas);
+      b.th = c.take<uint32_t>((size_t)R * I);
+      if (Is > 0) b.ths = c.take<uint32_t>((size_t)T * Is);
+    }
     b.uexp = c.take<int32_t>(U > 0 ? U : 1);
     b.ustart = c.take<int32_t>(U + 1);
     b.nuniq = c.take<int32_t>(1);
@@ -723,11 +741,13 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
         a.sdns = L->shared_down_s;
         a.sdnb = L->shared_down_b;
       }
-      a.logits = b.logits;
-      a.gate_logit = b.gate_logit;
-      a.h = b.h;
-      a.hs = b.hs;
-      a.bar = b.counters + 1;
+      a.epoch = b.epoch;
+      a.gucnt = b.gucnt;
+      a.tlog = b.tlog;
+      a.tgate = b.tgate;
+      a.tseen = b.tseen;
+      a.th = b.th;
+      a.ths = b.ths;
       a.idx = idx;
       a.scores = scores;
       a.y = y;

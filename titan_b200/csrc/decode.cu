@@ -36,6 +36,7 @@ namespace {
 
 constexpr int kSlabRows = 32;   // weight rows per CTA (two m16 tiles)
 constexpr int kCols = 8;        // activation columns per MMA pass (n = 8)
+constexpr int kColsPerPass = 2; // columns staged per pass (at most kCols)
 constexpr int kThreads = 128;   // 4 warps, one K quarter each
 constexpr int kWarps = 4;
 constexpr int kMaxGw = 12;      // groups per warp whose scales are held in registers
@@ -449,7 +450,9 @@ cudaError_t launch_gemv_stream(int mode, const StreamParams& P, int max_cols, cu
   const int kmax = (P.Wsh && P.K_sh > P.K) ? P.K_sh : P.K;
   const int nb_y = (mode == 0) ? (nmax / 2 + 15) / 16 : (nmax + kSlabRows - 1) / kSlabRows;
   if (nb_x <= 0 || nb_y <= 0 || max_cols <= 0) return cudaSuccess;
-  const int ncol = max_cols < kCols ? max_cols : kCols;
+  // columns staged per pass: two keep the plan at 3-6 CTAs per SM; an expert
+  // with more columns makes more passes over the rows already in shared memory
+  const int ncol = max_cols < kColsPerPass ? max_cols : kColsPerPass;
   const int smem = GemvPlan(kmax, ncol, mode == 1).total;
   dim3 grid(nb_x, nb_y);
   cudaError_t err = cudaSuccess;

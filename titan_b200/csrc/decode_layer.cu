@@ -9,30 +9,44 @@
 // (engine/patches/decode-fusion/fused_kernels.py:31-229).
 //
 // B200 mapping.  One CTA per SM, 8 warps, all CTAs resident at once, so CTAs
-// may wait for each other (two grid barriers, every wait bounded).
+// may wait for each other's data.  There is no grid barrier:
+//   * the logits carry the launch epoch in the same single-copy-atomic 64-bit
+//     store as the value, and a reader re-loads a word until its tag is
+//     current — one L2 round trip once the data is there (a barrier costs a
+//     fence, an atomic and a poll before the data read even starts);
+//   * h is published per gate_up tile by a release-increment of a 64-bit
+//     counter that only grows; one thread per CTA polls that one word, then
+//     the CTA reads h once (re-reading hot h lines from 148 SMs would crowd
+//     the L2 slices that hold them).
+// The epoch counter lives in the caller's workspace; CTA 0 advances it once
+// every CTA has marked that it read it.  Every wait is bounded.
 //   0. Before the dependency wait (programmatic dependent launch) each CTA
 //      requests its router rows and the packed rows of its shared-expert
 //      gate_up tiles: constant data, loaded while the previous layer ends.
 //   1. x (T rows) is read once per CTA and kept in shared memory as bf16 (for
 //      the router) and as the fp16 MMA operand with exact 64-group sums (for
-//      gate_up).  Warp 0 computes the CTA's router rows, publishes them and
-//      arrives at grid barrier 1; the other warps compute the shared expert's
-//      gate_up tiles in the meantime.
-//   2. After the barrier every CTA routes every token itself (one warp per
-//      token) and builds the plan (pairs sorted by expert, distinct experts):
-//      no second round trip through global memory.
+//      gate_up).  Warp 0 computes the CTA's router rows and publishes them;
+//      the other warps compute the shared expert's gate_up tiles meanwhile.
+//   2. Every CTA waits for all logits and routes every token itself, the
+//      8 warps split over the tokens (8 / T warps per token), and builds the
+//      plan (pairs sorted by expert, distinct experts): no second round trip.
 //   3. The routed gate_up tiles (16 weight rows = 8 gate + 8 up rows over the
 //      full K, one warp each) are spread over all CTAs, balanced against each
 //      CTA's down work.  Every warp streams its tiles through a private ring
-//      of 5 KB stages (16 rows x 512 K of packed int4 plus their bf16 scales
-//      and biases), cp.async issued NS-1 stages ahead, and writes fp32 h.
-//      The down rows of the warp follow in the same ring, so they are loading
-//      while gate_up computes.
-//   4. Grid barrier 2 (every h written).  Each CTA stages every pair's h as
-//      fp16 hi + lo operands with exact group sums, computes the down tiles
-//      of its 16-row output slabs for every selected expert and the shared
-//      expert, and folds them into y in slot order plus the gated shared
-//      expert, inside the CTA: no ticket, no partials in global memory.
+//      of 4.5 KB stages (16 rows x 512 K of packed int4 plus their bf16
+//      scales and biases), cp.async issued NS-1 stages ahead, and publishes h
+//      as the down projection's fp16 hi + lo operand.  The down rows of the
+//      warp follow in the same ring, so they load while gate_up computes.
+//   4. Each CTA waits for every gate_up tile, stages every pair's h with
+//      exact group sums, computes the down tiles of its 16-row output slabs
+//      for every selected expert and the shared expert, and folds them into y
+//      in slot order plus the gated shared expert, inside the CTA: no ticket,
+//      no partial sums in global memory.
+//
+// The phases run once per launch each, so the kernel's speed depends on how
+// much of its code the SM's instruction cache holds: the tile MMA routine is
+// out of line (one copy per variant) and loops that are not on a hot path
+// stay rolled.
 //
 // MMA mapping (both GEMVs): m16n8k16, weights as A in exact fp16 (q - 8)
 // (qpairs4), the token columns as B (n = 8, at most 8 columns per expert per
@@ -51,40 +65,50 @@ namespace {
 constexpr int kLWarps = 8;
 constexpr int kLThreads = kLWarps * 32;
 constexpr int kChunkK = 512;                       // K per ring stage
-constexpr int kRowStride = 288;                    // 256 B packed row slice + pad (32 mod 128)
+constexpr int kRowStride = 256;                    // packed row slice (512 K); 16-byte chunk c of
+                                                   // row r sits at chunk c ^ (r & 7): the
+                                                   // fragment loads take the minimum 2 wavefronts
 constexpr int kStageW = 16 * kRowStride;           // weights of one stage
 constexpr int kStageBytes = kStageW + 2 * 16 * 16; // + bf16 scales and biases (16 rows x 8 groups)
 constexpr int kMaxRowsPerCta = 8;                  // router rows per CTA
-constexpr uint32_t kSpin = 1u << 22;               // polls before a wait gives up
+constexpr uint32_t kSpin = 1u << 17;               // polls before a wait gives up (~0.1 s)
 constexpr uint32_t kFastPolls = 1u << 12;
 
-TMOE_DEV int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// Exchanges between CTAs: relaxed single-copy-atomic accesses at GPU scope.
+TMOE_DEV void st_tag32(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+TMOE_DEV void st_tag64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+TMOE_DEV uint32_t ld_tag32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-TMOE_DEV void st_release(int* p, int v) {
-  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+TMOE_DEV unsigned long long ld_tag64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
-TMOE_DEV void st_relaxed(int* p, int v) {
-  asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// h as the down projection's operand: fp16 hi = h, lo = h - hi
+TMOE_DEV uint32_t pack_h(float h) {
+  const __half hi = __float2half_rn(h);
+  const __half lo = __float2half_rn(__fsub_rn(h, __half2float(hi)));
+  return (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
 }
-
-// Grid barrier for one thread per CTA (after a CTA barrier).  count returns
-// to zero at every completion; gen advances by one.  gen0 = gen as read
-// (acquire) before this CTA arrived.  A wait that runs out records the error
-// and returns, so nothing hangs.
-TMOE_DEV void grid_sync(int* count, int* gen, int gen0, int n) {
-  __threadfence();
-  if (ticket_acq_rel(count) == n - 1) {
-    st_relaxed(count, 0);
-    st_release(gen, gen0 + 1);
-    return;
-  }
-  for (uint32_t i = 0; i < kSpin; ++i) {
-    if (ld_acquire(gen) != gen0) return;
-    if (i >= kFastPolls) __nanosleep(64);
-  }
+// n gate_up tiles' h are published: the warp's stores are ordered before the
+// increment (warp barrier, then a release add by lane 0).
+TMOE_DEV void publish_tiles(unsigned long long* cnt, unsigned long long n, int lane) {
+  __syncwarp();
+  if (lane == 0) asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(cnt), "l"(n) : "memory");
+}
+TMOE_DEV void spin_pause(uint32_t i) {
+  if (i >= kFastPolls) __nanosleep(32);
+}
+// A wait that ran out: record it for the host and stop this CTA's other waits.
+TMOE_DEV void wait_failed(volatile int* abort_flag) {
+  *abort_flag = 1;
   atomicExch(&g_layer_error, 1);
 }
 
@@ -99,7 +123,7 @@ TMOE_DEV void cp_async_wait_n() {
 struct LayerPlan {
   int ntp, rpc, R, spc, cs_r, cs_s, gi, gs;
   int off_xraw, off_x16, off_xs, off_rows, off_rt, off_bh, off_bl, off_bx, off_sh, off_sl, off_sx,
-      off_res, off_ring, total;
+      off_ex, off_res, off_ring, total;
   TMOE_HD LayerPlan(int T, int H, int E, int k, int I, int Is, int nct, int ns) {
     ntp = T <= 1 ? 1 : (T <= 2 ? 2 : 4);
     rpc = (E + 1 + nct - 1) / nct;
@@ -118,7 +142,8 @@ struct LayerPlan {
     off_rt = o;   o += (8 * R + 16) * 4;            // routing scratch (ints / floats)
     o = (o + 15) & ~15;
     // h operands: routed pairs, then the shared expert's T columns.  The
-    // routing exponentials (T x E floats) live here before the staging.
+    // routing phase uses the same space first: logits (T x E bf16), then the
+    // exponentials / keys (T x 32 ceil(E / 32) words).
     const int st0 = o;
     off_bh = o;   o += R * cs_r;
     off_bl = o;   o += R * cs_r;
@@ -126,7 +151,9 @@ struct LayerPlan {
     off_sh = o;   o += T * cs_s;
     off_sl = o;   o += T * cs_s;
     off_sx = o;   o += T * gs * 4;
-    if (o - st0 < T * E * 4) o = st0 + T * E * 4;
+    off_ex = st0 + ((T * E * 2 + 15) & ~15);
+    const int rt_end = off_ex + T * ((E + 31) / 32) * 32 * 4;
+    if (o < rt_end) o = rt_end;
     o = (o + 15) & ~15;
     off_res = o;  o += spc * (R + T) * 16 * 4;
     o = (o + 127) & ~127;
@@ -158,7 +185,7 @@ TMOE_DEV void issue_stage(uint8_t* st, const Job& jb, int ch, int lane) {
 #pragma unroll
   for (int m = 0; m < 8; ++m) {
     const int i = lane + 32 * m, r = i >> 4, c = i & 15;
-    cp_async16(st + r * kRowStride + c * 16,
+    cp_async16(st + r * kRowStride + ((c ^ (r & 7)) << 4),
                jb.w + (size_t)job_row(jb, r) * KW + ch * 64 + c * 4);
   }
   const int r = lane & 15;
@@ -168,16 +195,20 @@ TMOE_DEV void issue_stage(uint8_t* st, const Job& jb, int ch, int lane) {
 
 // One stage of MMAs: 8 groups; B columns from bgh (+ bgl for fp32 sources
 // split into hi + lo), column sums xs0 / xs1 for the thread's two D columns.
+// Out of line, one copy per variant, groups not unrolled (instruction cache).
 template <bool LO>
-TMOE_DEV void stage_mma(const uint8_t* st, int gbase, const uint8_t* bgh, const uint8_t* bgl,
-                        const float* xs0, const float* xs1, int g, int t, float* acc) {
-  const uint8_t* wp = st + g * kRowStride + t * 8;
+__device__ __noinline__ float4 stage_mma(const uint8_t* st, int gbase, const uint8_t* bgh,
+                                         const uint8_t* bgl, const float* xs0, const float* xs1,
+                                         int g, int t, float4 acc4) {
+  float acc[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
+  const uint8_t* wp = st + g * kRowStride + (t & 1) * 8;   // rows g and g + 8 share the swizzle
   const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + kStageW);
   const uint16_t* bp = sp + 128;
-#pragma unroll 2
+#pragma unroll 1
   for (int j = 0; j < 8; ++j) {
-    const uint2 wl = *reinterpret_cast<const uint2*>(wp + j * 32);
-    const uint2 wh = *reinterpret_cast<const uint2*>(wp + 8 * kRowStride + j * 32);
+    const int sw = ((2 * j + (t >> 1)) ^ g) << 4;            // chunk 2j + t/2 of rows g, g + 8
+    const uint2 wl = *reinterpret_cast<const uint2*>(wp + sw);
+    const uint2 wh = *reinterpret_cast<const uint2*>(wp + 8 * kRowStride + sw);
     const int gj = gbase + j;
     const uint4* hp = reinterpret_cast<const uint4*>(bgh + gj * 128 + t * 32);
     const uint4 h0 = hp[0], h1 = hp[1];
@@ -213,6 +244,7 @@ TMOE_DEV void stage_mma(const uint8_t* st, int gbase, const uint8_t* bgh, const 
     acc[2] = __fmaf_rn(sh, d[2], __fmaf_rn(bh, x0, acc[2]));
     acc[3] = __fmaf_rn(sh, d[3], __fmaf_rn(bh, x1, acc[3]));
   }
+  return make_float4(acc[0], acc[1], acc[2], acc[3]);
 }
 
 }  // namespace
@@ -276,6 +308,7 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
   int32_t* s_ustart = s_uexp + R + 1;     // [R + 2]
   float* s_score = reinterpret_cast<float*>(s_ustart + R + 2);   // [R] bf16 score as float
   int32_t* s_nuniq = reinterpret_cast<int32_t*>(s_score + R);
+  float* s_gate = reinterpret_cast<float*>(s_nuniq + 1);         // [T] sigmoid(gate logit)
   const int nch_h = H / 8;                // 16-byte chunks of a router row
 
   // ---- 0: constant data before the dependency wait
@@ -327,10 +360,19 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
 
   pdl_wait();
   pdl_trigger();
-  int gen1 = 0, gen2 = 0;
+  // this launch's epoch: one more than the counter (CTA 0 advances it once
+  // every CTA has read it); every CTA marks that it has seen it.  The gate_up
+  // counter as it stands: no CTA adds to it before every CTA has published its
+  // logits, which each does after this read.
+  __shared__ int s_epoch;
+  __shared__ int s_abort;
+  __shared__ unsigned long long s_gubase;
   if (tid == 0) {
-    gen1 = ld_acquire(A.bar + 1);
-    gen2 = ld_acquire(A.bar + 3);
+    s_abort = 0;
+    s_gubase = ld_tag64(A.gucnt);
+    const int ep = (int)ld_tag32(reinterpret_cast<const uint32_t*>(A.epoch)) + 1;
+    s_epoch = ep;
+    st_tag32(reinterpret_cast<uint32_t*>(A.tseen) + c, (uint32_t)ep);
   }
 
   // ---- 1: x -> bf16 copy (router) + fp16 operand with exact group sums
@@ -369,6 +411,7 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
     }
   }
   __syncthreads();
+  const int epoch = s_epoch;
 
   if (warp == 0) {
     // ---- router rows of this CTA: 4 rows per pass, 8 lanes (partials) each
@@ -392,86 +435,173 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
         const float s8 = tree8(acc[tt]);
         if (j < L.rpc && p == tt && tt < T) {
           if (er < E)
-            A.logits[(size_t)tt * E + er] = f2bf(s8);
+            st_tag64(A.tlog + (size_t)tt * E + er,
+                     (unsigned long long)f2bf(s8) | ((unsigned long long)(uint32_t)epoch << 32));
           else if (er == E && A.wg)
-            A.gate_logit[tt] = s8;
+            st_tag64(A.tgate + tt, (unsigned long long)__float_as_uint(s8) |
+                                       ((unsigned long long)(uint32_t)epoch << 32));
         }
       }
     }
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) grid_sync(A.bar, A.bar + 1, gen1, nct);
-    __syncwarp();
   } else {
     // ---- the shared expert's gate_up tiles (independent of the routing)
     int seq = 0;
     for (int m = 0; m < n_sh; ++m) {
       const Job jb = sh_job(m);
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       const int c0 = min(2 * t, T - 1), c1 = min(2 * t + 1, T - 1);
       const uint8_t* bgh = x16 + (size_t)min(g, T - 1) * H * 2;
       for (int ch = 0; ch < cgu; ++ch, ++seq) {
         sh_issue_next();
         cp_async_wait_n<NS - 1>();
         __syncwarp();
-        stage_mma<false>(ring + (seq % NS) * kStageBytes, ch * 8, bgh, bgh, xs + c0 * G,
-                         xs + c1 * G, g, t, acc);
+        acc = stage_mma<false>(ring + (seq % NS) * kStageBytes, ch * 8, bgh, bgh, xs + c0 * G,
+                               xs + c1 * G, g, t, acc);
         __syncwarp();
       }
       const int row = jb.row0 + g;
-      if (2 * t < T) A.hs[(size_t)(2 * t) * Is + row] = silu_mul_f32(acc[0], acc[2]);
-      if (2 * t + 1 < T) A.hs[(size_t)(2 * t + 1) * Is + row] = silu_mul_f32(acc[1], acc[3]);
+      if (2 * t < T) A.ths[(size_t)(2 * t) * Is + row] = pack_h(silu_mul_f32(acc.x, acc.z));
+      if (2 * t + 1 < T) A.ths[(size_t)(2 * t + 1) * Is + row] = pack_h(silu_mul_f32(acc.y, acc.w));
     }
     cp_async_wait_n<0>();
     __syncwarp();
   }
   __syncthreads();
 
-  // ---- 2: routing of every token (warp w routes token w)
-  float* ex_all = reinterpret_cast<float*>(sm + L.off_bh);
-  if (warp < T) {
-    const int tt = warp;
-    const uint16_t* lrow = A.logits + (size_t)tt * E;
-    float* ex = ex_all + (size_t)tt * E;
-    float m = -__int_as_float(0x7f800000);
-    for (int e = lane; e < E; e += 32) {
-      const float v = bf2f(__ldcg(lrow + e));
-      ex[e] = v;
-      m = fmaxf(m, v);
+  // ---- 2: every thread waits for its words of this launch's logits (CTA 0
+  // also for every CTA's start mark, after which it advances the epoch)
+  uint16_t* lg_s = reinterpret_cast<uint16_t*>(sm + L.off_bh);
+  {
+    const int n = T * E;
+    const int nseen = c == 0 ? nct : 0;
+    for (int i = tid; i < n + T + nseen; i += kLThreads) {
+      bool done = false;
+      for (uint32_t it = 0; it < kSpin && !(it >= kFastPolls && *(volatile int*)&s_abort);
+           ++it, spin_pause(it)) {
+        if (i < n) {
+          const unsigned long long w = ld_tag64(A.tlog + i);
+          if ((int)(w >> 32) == epoch) {
+            lg_s[i] = (uint16_t)(w & 0xffffu);
+            done = true;
+          }
+        } else if (i < n + T) {
+          if (!A.wg) {
+            done = true;
+          } else {
+            const unsigned long long w = ld_tag64(A.tgate + (i - n));
+            if ((int)(w >> 32) == epoch) {
+              s_gate[i - n] = csigmoid(__uint_as_float((uint32_t)w));
+              done = true;
+            }
+          }
+        } else {
+          done = (int)ld_tag32(reinterpret_cast<const uint32_t*>(A.tseen) + (i - n - T)) == epoch;
+        }
+        if (done) break;
+      }
+      if (!done) wait_failed(&s_abort);
     }
-    m = warp_max(m);
-    float part = 0.0f;
-    for (int e = lane; e < E; e += 32) {
-      const float v = cexp(__fsub_rn(ex[e], m));
-      ex[e] = v;
-      part = __fadd_rn(part, v);
-    }
-    const float inv = __fdiv_rn(1.0f, warp_butterfly_sum(part));
+  }
+  __syncthreads();
+  if (c == 0 && tid == 0) st_tag32(reinterpret_cast<uint32_t*>(A.epoch), (uint32_t)epoch);
+  // every CTA has read the gate_up counter by now: the shared-expert tiles of
+  // phase 1 are counted from here
+  if (n_sh > 0) publish_tiles(A.gucnt, (unsigned long long)n_sh, lane);
+  // Routing: token tt gets W = 8 / T warps; warp wi of the token owns the
+  // columns c in [wi C / W, (wi + 1) C / W) of the lane-major layout
+  // e = 32 c + lane (C = ceil(E / 32)).  The arithmetic of route_token (max,
+  // cexp(l - max), the canonical denominator by one warp: lane partials over
+  // c ascending, then the butterfly; keys bf16(p) << 16 | 0xffff - e;
+  // selection by key), with the top-k taken per warp and merged: the same
+  // selection order as one warp over all E.
+  {
+    __shared__ float s_redmax[kLWarps];
+    __shared__ float s_inv[kLayerMaxT];
+    __shared__ uint32_t s_cand[kLWarps * 32];
+    const int W = kLWarps / T;
+    const int tt = warp / W, wi = warp % W;
+    const bool active = tt < T;
+    const int C = (E + 31) / 32;
+    const int cb = (wi * C) / W, ce = ((wi + 1) * C) / W;
+    float* ex = reinterpret_cast<float*>(sm + L.off_ex) + (size_t)(active ? tt : 0) * C * 32;
     uint32_t* key = reinterpret_cast<uint32_t*>(ex);
-    for (int e = lane; e < E; e += 32)
-      key[e] = ((uint32_t)f2bf(__fmul_rn(ex[e], inv)) << 16) | (uint32_t)(0xffff - e);
-    __syncwarp();
-    float ssum = 0.0f;
-    uint32_t my_key = 0;
-    for (int j = 0; j < k; ++j) {
-      uint32_t best = 0;
-      for (int e = lane; e < E; e += 32) best = key[e] > best ? key[e] : best;
-      const uint32_t win = __reduce_max_sync(0xffffffffu, best);
-      ssum = __fadd_rn(ssum, bf2f((uint16_t)(win >> 16)));
-      const int ew = 0xffff - (int)(win & 0xffffu);
-      if ((ew & 31) == lane) key[ew] = 0;
-      if (lane == j) my_key = win;
-      __syncwarp();
+    const uint16_t* lg = lg_s + (size_t)(active ? tt : 0) * E;
+    float m = -__int_as_float(0x7f800000);
+    if (active)
+      for (int cc = cb; cc < ce; ++cc) {
+        const int e = 32 * cc + lane;
+        const float v = e < E ? bf2f(lg[e]) : -__int_as_float(0x7f800000);
+        ex[32 * cc + lane] = v;
+        m = fmaxf(m, v);
+      }
+    m = warp_max(m);
+    if (lane == 0) s_redmax[warp] = m;
+    __syncthreads();
+    if (active) {
+      float M = s_redmax[tt * W];
+      for (int w2 = 1; w2 < W; ++w2) M = fmaxf(M, s_redmax[tt * W + w2]);
+      for (int cc = cb; cc < ce; ++cc) {
+        const int e = 32 * cc + lane;
+        ex[32 * cc + lane] = e < E ? cexp(__fsub_rn(ex[32 * cc + lane], M)) : 0.0f;
+      }
     }
-    const float sb = bfround(ssum);
-    if (lane < k) {
-      const int e = 0xffff - (int)(my_key & 0xffffu);
-      const uint16_t sc = f2bf(__fdiv_rn(bf2f((uint16_t)(my_key >> 16)), sb));
-      s_idx[tt * k + lane] = e;
-      s_score[tt * k + lane] = bf2f(sc);
-      if (c == 0) {
-        A.idx[(size_t)tt * k + lane] = e;
-        A.scores[(size_t)tt * k + lane] = sc;
+    __syncthreads();
+    if (active && wi == 0) {
+      float part = 0.0f;
+#pragma unroll 4
+      for (int cc = 0; cc < C; ++cc)
+        if (32 * cc + lane < E) part = __fadd_rn(part, ex[32 * cc + lane]);
+      const float inv = __fdiv_rn(1.0f, warp_butterfly_sum(part));
+      if (lane == 0) s_inv[tt] = inv;
+    }
+    __syncthreads();
+    if (active) {
+      const float inv = s_inv[tt];
+      for (int cc = cb; cc < ce; ++cc) {
+        const int e = 32 * cc + lane;
+        key[32 * cc + lane] =
+            e < E ? (((uint32_t)f2bf(__fmul_rn(ex[32 * cc + lane], inv)) << 16) | (uint32_t)(0xffff - e))
+                  : 0u;
+      }
+      __syncwarp();
+      for (int j = 0; j < k; ++j) {                 // this warp's k best, best first
+        uint32_t best = 0;
+        for (int cc = cb; cc < ce; ++cc) best = max(best, key[32 * cc + lane]);
+        const uint32_t win = __reduce_max_sync(0xffffffffu, best);
+        if (win != 0u) {
+          const int ew = 0xffff - (int)(win & 0xffffu);
+          if ((ew & 31) == lane) key[ew] = 0u;
+        }
+        if (lane == 0) s_cand[warp * k + j] = win;
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    if (active && wi == 0) {                        // merge the W lists of the token
+      uint32_t* cand = s_cand + tt * W * k;
+      const int ncand = W * k;
+      float ssum = 0.0f;
+      uint32_t my_key = 0;
+      for (int j = 0; j < k; ++j) {
+        uint32_t best = 0;
+        for (int q = lane; q < ncand; q += 32) best = max(best, cand[q]);
+        const uint32_t win = __reduce_max_sync(0xffffffffu, best);
+        for (int q = lane; q < ncand; q += 32)
+          if (cand[q] == win) cand[q] = 0u;
+        ssum = __fadd_rn(ssum, bf2f((uint16_t)(win >> 16)));
+        if (lane == j) my_key = win;
+        __syncwarp();
+      }
+      const float sb = bfround(ssum);
+      if (lane < k) {
+        const int e = 0xffff - (int)(my_key & 0xffffu);
+        const uint16_t sc = f2bf(__fdiv_rn(bf2f((uint16_t)(my_key >> 16)), sb));
+        s_idx[tt * k + lane] = e;
+        s_score[tt * k + lane] = bf2f(sc);
+        if (c == 0) {
+          A.idx[(size_t)tt * k + lane] = e;
+          A.scores[(size_t)tt * k + lane] = sc;
+        }
       }
     }
   }
@@ -578,79 +708,98 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
     const int tc0 = s_order[p0 + min(2 * t, nc - 1)] / k;
     const int tc1 = s_order[p0 + min(2 * t + 1, nc - 1)] / k;
     const uint8_t* bgh = x16 + (size_t)tg * H * 2;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int ch = 0; ch < cgu; ++ch, ++seq) {
       issue_next();
       cp_async_wait_n<NS - 1>();
       __syncwarp();
-      stage_mma<false>(ring + (seq % NS) * kStageBytes, ch * 8, bgh, bgh, xs + tc0 * G,
-                       xs + tc1 * G, g, t, acc);
+      acc = stage_mma<false>(ring + (seq % NS) * kStageBytes, ch * 8, bgh, bgh, xs + tc0 * G,
+                             xs + tc1 * G, g, t, acc);
       __syncwarp();
     }
     const int row = jb.row0 + g;
-    if (2 * t < nc) A.h[(size_t)s_order[p0 + 2 * t] * I + row] = silu_mul_f32(acc[0], acc[2]);
+    if (2 * t < nc) A.th[(size_t)s_order[p0 + 2 * t] * I + row] = pack_h(silu_mul_f32(acc.x, acc.z));
     if (2 * t + 1 < nc)
-      A.h[(size_t)s_order[p0 + 2 * t + 1] * I + row] = silu_mul_f32(acc[1], acc[3]);
+      A.th[(size_t)s_order[p0 + 2 * t + 1] * I + row] = pack_h(silu_mul_f32(acc.y, acc.w));
+    publish_tiles(A.gucnt, 1ull, lane);
   }
 
-  // ---- 4: every h is written once all CTAs get here
+  // ---- 4: wait until every gate_up tile of this launch is published (one
+  // thread polls one counter), then stage h (routed pairs, then the shared
+  // expert's tokens) as fp16 hi + lo with exact group sums of hi + lo; two
+  // 16-element blocks per thread and pass, loaded before either is converted
+  if (tid == 0) {
+    const unsigned long long need = (unsigned long long)(nuniq * (I / 8) + (Is > 0 ? Is / 8 : 0));
+    bool ok = false;
+    for (uint32_t it = 0; it < kSpin; ++it, spin_pause(it))
+      if (ld_tag64(A.gucnt) - s_gubase >= need) {
+        ok = true;
+        break;
+      }
+    if (!ok) wait_failed(&s_abort);
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  }
   __syncthreads();
-  if (tid == 0) grid_sync(A.bar + 2, A.bar + 3, gen2, nct);
-  __syncthreads();
-  // stage h (routed pairs, then the shared expert's tokens) as fp16 hi + lo
-  // with exact group sums of hi + lo
   {
     const int nb_r = R * (I / 16), nb_s = T * (Is / 16), nb = nb_r + nb_s;
-    for (int base = 0; base < nb; base += kLThreads) {
-      const int b = base + tid;
-      float sum = 0.0f;
-      const bool ok = b < nb;
-      const bool shared = b >= nb_r;
-      const int K = shared ? Is : I;
-      const int bb = shared ? b - nb_r : b;
-      const int col = bb / (K / 16), blk = bb % (K / 16);
-      if (ok) {
-        const float* src = (shared ? A.hs : A.h) + (size_t)col * K + blk * 16;
-        float v[16];
+    for (int base = 0; base < nb; base += 2 * kLThreads) {
+      uint32_t hl[2][16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 f = __ldcg(reinterpret_cast<const float4*>(src) + q);
-          v[4 * q] = f.x;
-          v[4 * q + 1] = f.y;
-          v[4 * q + 2] = f.z;
-          v[4 * q + 3] = f.w;
-        }
-        uint16_t hv[16], lv[16];
+      for (int hh = 0; hh < 2; ++hh) {
+        const int b = base + hh * kLThreads + tid;
+        if (b < nb) {
+          const bool shared = b >= nb_r;
+          const int K = shared ? Is : I;
+          const int bb = shared ? b - nb_r : b;
+          const uint4* src = reinterpret_cast<const uint4*>(
+              (shared ? A.ths : A.th) + (size_t)(bb / (K / 16)) * K + (bb % (K / 16)) * 16);
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const __half hh = __float2half_rn(v[q]);
-          const float hf = __half2float(hh);
-          const __half ll = __float2half_rn(__fsub_rn(v[q], hf));
-          hv[f16p_pos(q)] = __half_as_ushort(hh);
-          lv[f16p_pos(q)] = __half_as_ushort(ll);
-          sum = __fadd_rn(sum, __fadd_rn(hf, __half2float(ll)));
+          for (int q = 0; q < 4; ++q) {
+            const uint4 w = __ldcg(src + q);
+            hl[hh][4 * q] = w.x;
+            hl[hh][4 * q + 1] = w.y;
+            hl[hh][4 * q + 2] = w.z;
+            hl[hh][4 * q + 3] = w.w;
+          }
         }
-        const int cs = shared ? L.cs_s : L.cs_r;
-        uint8_t* dh = sm + (shared ? L.off_sh : L.off_bh) + (size_t)col * cs + blk * 32;
-        uint8_t* dl = sm + (shared ? L.off_sl : L.off_bl) + (size_t)col * cs + blk * 32;
-        reinterpret_cast<uint4*>(dh)[0] =
-            make_uint4(hv[0] | ((uint32_t)hv[1] << 16), hv[2] | ((uint32_t)hv[3] << 16),
-                       hv[4] | ((uint32_t)hv[5] << 16), hv[6] | ((uint32_t)hv[7] << 16));
-        reinterpret_cast<uint4*>(dh)[1] =
-            make_uint4(hv[8] | ((uint32_t)hv[9] << 16), hv[10] | ((uint32_t)hv[11] << 16),
-                       hv[12] | ((uint32_t)hv[13] << 16), hv[14] | ((uint32_t)hv[15] << 16));
-        reinterpret_cast<uint4*>(dl)[0] =
-            make_uint4(lv[0] | ((uint32_t)lv[1] << 16), lv[2] | ((uint32_t)lv[3] << 16),
-                       lv[4] | ((uint32_t)lv[5] << 16), lv[6] | ((uint32_t)lv[7] << 16));
-        reinterpret_cast<uint4*>(dl)[1] =
-            make_uint4(lv[8] | ((uint32_t)lv[9] << 16), lv[10] | ((uint32_t)lv[11] << 16),
-                       lv[12] | ((uint32_t)lv[13] << 16), lv[14] | ((uint32_t)lv[15] << 16));
       }
-      sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
-      sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
-      if (ok && (blk & 3) == 0) {
-        float* xsum = reinterpret_cast<float*>(sm + (shared ? L.off_sx : L.off_bx));
-        xsum[col * (K / 64) + blk / 4] = sum;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int b = base + hh * kLThreads + tid;
+        const bool ok = b < nb;
+        const bool shared = b >= nb_r;
+        const int K = shared ? Is : I;
+        const int bb = shared ? b - nb_r : b;
+        const int col = bb / (K / 16), blk = bb % (K / 16);
+        float sum = 0.0f;
+        if (ok) {
+          uint16_t hv[16], lv[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const uint16_t hb = (uint16_t)(hl[hh][q] & 0xffffu), lb = (uint16_t)(hl[hh][q] >> 16);
+            hv[f16p_pos(q)] = hb;
+            lv[f16p_pos(q)] = lb;
+            sum = __fadd_rn(sum, __fadd_rn(__half2float(__ushort_as_half(hb)),
+                                           __half2float(__ushort_as_half(lb))));
+          }
+          const int cs = shared ? L.cs_s : L.cs_r;
+          uint4* dh = reinterpret_cast<uint4*>(sm + (shared ? L.off_sh : L.off_bh) + (size_t)col * cs + blk * 32);
+          uint4* dl = reinterpret_cast<uint4*>(sm + (shared ? L.off_sl : L.off_bl) + (size_t)col * cs + blk * 32);
+          dh[0] = make_uint4(hv[0] | ((uint32_t)hv[1] << 16), hv[2] | ((uint32_t)hv[3] << 16),
+                             hv[4] | ((uint32_t)hv[5] << 16), hv[6] | ((uint32_t)hv[7] << 16));
+          dh[1] = make_uint4(hv[8] | ((uint32_t)hv[9] << 16), hv[10] | ((uint32_t)hv[11] << 16),
+                             hv[12] | ((uint32_t)hv[13] << 16), hv[14] | ((uint32_t)hv[15] << 16));
+          dl[0] = make_uint4(lv[0] | ((uint32_t)lv[1] << 16), lv[2] | ((uint32_t)lv[3] << 16),
+                             lv[4] | ((uint32_t)lv[5] << 16), lv[6] | ((uint32_t)lv[7] << 16));
+          dl[1] = make_uint4(lv[8] | ((uint32_t)lv[9] << 16), lv[10] | ((uint32_t)lv[11] << 16),
+                             lv[12] | ((uint32_t)lv[13] << 16), lv[14] | ((uint32_t)lv[15] << 16));
+        }
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
+        if (ok && (blk & 3) == 0) {
+          float* xsum = reinterpret_cast<float*>(sm + (shared ? L.off_sx : L.off_bx));
+          xsum[col * (K / 64) + blk / 4] = sum;
+        }
       }
     }
   }
@@ -670,27 +819,27 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
     const uint8_t* bgl = sm + (shared ? L.off_sl : L.off_bl) + (size_t)cg_ * cs;
     const float* xsum = reinterpret_cast<const float*>(sm + (shared ? L.off_sx : L.off_bx));
     const int gk = jb.K / 64;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     const int nchk = jb.K / kChunkK;
     for (int ch = 0; ch < nchk; ++ch, ++seq) {
       issue_next();
       cp_async_wait_n<NS - 1>();
       __syncwarp();
-      stage_mma<true>(ring + (seq % NS) * kStageBytes, ch * 8, bgh, bgl, xsum + cc0 * gk,
-                      xsum + cc1 * gk, g, t, acc);
+      acc = stage_mma<true>(ring + (seq % NS) * kStageBytes, ch * 8, bgh, bgl, xsum + cc0 * gk,
+                            xsum + cc1 * gk, g, t, acc);
       __syncwarp();
     }
     float* rs = res + (size_t)jb.slab * (R + T) * 16;
     const int base_col = shared ? R : 0;
     if (2 * t < nc) {
       const int cl = base_col + col_of(2 * t);
-      rs[cl * 16 + g] = acc[0];
-      rs[cl * 16 + g + 8] = acc[2];
+      rs[cl * 16 + g] = acc.x;
+      rs[cl * 16 + g + 8] = acc.z;
     }
     if (2 * t + 1 < nc) {
       const int cl = base_col + col_of(2 * t + 1);
-      rs[cl * 16 + g] = acc[1];
-      rs[cl * 16 + g + 8] = acc[3];
+      rs[cl * 16 + g] = acc.y;
+      rs[cl * 16 + g + 8] = acc.w;
     }
   }
   cp_async_wait_n<0>();
@@ -703,7 +852,7 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
       const int tt = i >> 4, r = i & 15;
       float a = 0.0f;
       for (int j = 0; j < k; ++j) a = __fmaf_rn(s_score[tt * k + j], rs[(tt * k + j) * 16 + r], a);
-      if (Is > 0) a = __fmaf_rn(csigmoid(__ldcg(A.gate_logit + tt)), rs[(R + tt) * 16 + r], a);
+      if (Is > 0) a = __fmaf_rn(s_gate[tt], rs[(R + tt) * 16 + r], a);
       A.y[(size_t)tt * H + slab * 16 + r] = f2bf(a);
     }
   }
@@ -717,10 +866,11 @@ size_t decode_layer_smem(int T, int H, int E, int k, int I, int Is, int nct, int
 // cannot take the single-launch path.
 int decode_layer_stages(int T, int H, int E, int k, int I, int Is, int nct) {
   if (T < 1 || T > kLayerMaxT || T * k > 128 || k > 32 || E > 1024 || E < k) return 0;
+  if (nct > kLayerMaxCtas) return 0;
   if (H % kChunkK || I % kChunkK || (Is > 0 && Is % kChunkK)) return 0;
   if ((E + 1 + nct - 1) / nct > kMaxRowsPerCta) return 0;
   for (int ns = 4; ns >= 2; --ns)
-    if (decode_layer_smem(T, H, E, k, I, Is, nct, ns) <= 232448) return ns;
+    if (decode_layer_smem(T, H, E, k, I, Is, nct, ns) <= 232448 - 4096) return ns;   // + static
   return 0;
 }
 

@@ -1,7 +1,8 @@
 // Register-fragment helpers shared by the decode kernels (sm_100a):
 // m16n8k16 fp16 MMAs on exact integer weights, the nibble unpacking that
-// feeds them, the permuted activation layout that matches it, and the
-// router's canonical 8-partial bf16 dot product.
+// feeds them, the permuted activation layout that matches it, the router's
+// canonical 8-partial bf16 dot product and the one-warp softmax + top-k of a
+// token.
 #pragma once
 
 #include "common.cuh"
@@ -66,6 +67,76 @@ TMOE_DEV void router_dots(const uint4* wrow_s, const uint4* xsm, int nch, int p,
       for (int q = 0; q < 8; ++q) acc[tt] = __fmaf_rn(xf[q], wf[q], acc[tt]);
     }
   }
+}
+
+struct RouteOut {
+  int e;            // lane j < k: the j-th selected expert
+  uint16_t score;   // its normalised bf16 score
+};
+
+// Softmax + top-k of one token by one warp, keys in registers (lane l holds
+// e = 32c + l): the max, exponentials cexp(l - max), the canonical
+// denominator (lane partials over c ascending, then the butterfly), bf16
+// probabilities, keys (prob << 16 | 0xffff - e) so ties go to the lowest
+// index; each lane sorts its keys (bitonic network, descending) and each of
+// the k rounds takes the warp max of the lane heads, the winning lane dropping
+// its head.  The selected probabilities are summed in selection order and
+// rounded to bf16; score_j = bf16(p_j / sum).
+template <int PER>
+TMOE_DEV RouteOut route_token(const uint16_t* lg, int E, int k, int lane) {
+  float v[PER];
+  float m = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int c = 0; c < PER; ++c) {
+    const int e = 32 * c + lane;
+    v[c] = e < E ? bf2f(lg[e]) : -__int_as_float(0x7f800000);
+    m = fmaxf(m, v[c]);
+  }
+  m = warp_max(m);
+  float part = 0.0f;
+#pragma unroll
+  for (int c = 0; c < PER; ++c)
+    if (32 * c + lane < E) {
+      v[c] = cexp(__fsub_rn(v[c], m));
+      part = __fadd_rn(part, v[c]);
+    }
+  const float inv = __fdiv_rn(1.0f, warp_butterfly_sum(part));
+  uint32_t key[PER];
+#pragma unroll
+  for (int c = 0; c < PER; ++c) {
+    const int e = 32 * c + lane;
+    key[c] = e < E ? (((uint32_t)f2bf(__fmul_rn(v[c], inv)) << 16) | (uint32_t)(0xffff - e)) : 0u;
+  }
+#pragma unroll
+  for (int kk = 2; kk <= PER; kk <<= 1)
+#pragma unroll
+    for (int jj = kk >> 1; jj > 0; jj >>= 1)
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int l = i ^ jj;
+        if (l > i) {
+          const uint32_t a = key[i], b = key[l];
+          const bool desc = (i & kk) == 0;
+          key[i] = desc ? max(a, b) : min(a, b);
+          key[l] = desc ? min(a, b) : max(a, b);
+        }
+      }
+  float ssum = 0.0f;
+  uint32_t my_key = 0;
+  for (int j = 0; j < k; ++j) {
+    const uint32_t win = __reduce_max_sync(0xffffffffu, key[0]);
+    const bool mine = key[0] == win;          // keys are distinct: one lane
+#pragma unroll
+    for (int c = 0; c < PER - 1; ++c) key[c] = mine ? key[c + 1] : key[c];
+    key[PER - 1] = mine ? 0u : key[PER - 1];
+    ssum = __fadd_rn(ssum, bf2f((uint16_t)(win >> 16)));
+    if (lane == j) my_key = win;
+  }
+  const float sb = bfround(ssum);
+  RouteOut r;
+  r.e = 0xffff - (int)(my_key & 0xffffu);
+  r.score = f2bf(__fdiv_rn(bf2f((uint16_t)(my_key >> 16)), sb));
+  return r;
 }
 
 }  // namespace tmoe

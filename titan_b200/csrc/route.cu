@@ -267,12 +267,9 @@ cudaError_t launch_route_plan(const int32_t* idx, int R, int E, int tile_m, int 
 // row E) for every token: warps 0 and 1 hold 4 rows each, 8 lanes per row, one
 // per canonical partial, with the rows and the token vectors staged in shared
 // memory by cp.async.  The last CTA to finish (a device-wide ticket; nobody
-// waits) then routes every token with all 4 warps: the exponentials of a
-// quarter of the experts per warp, the canonical sequential lane sums by one
-// warp, a top-k per warp over its quarter and the final top-k over the 4k
-// candidates (the same selection and tie order as router_topk_kernel), the
-// routing plan over the T*k pairs, and it zeroes the decode combine counters
-// and resets the ticket.
+// waits) then routes the tokens, one warp per token (route_token: the same
+// selection and tie order as router_topk_kernel), builds the routing plan over
+// the T*k pairs, zeroes the decode combine counters and resets the ticket.
 //
 // counters[0] is the ticket; counters[1 .. ncounters] are the combine
 // counters.  counters[0] must be zero when the kernel starts; it is zero again
@@ -293,9 +290,7 @@ __global__ void __launch_bounds__(128) decode_route_kernel(
   __shared__ int32_t cnt[1024];
   __shared__ int32_t off[1025];
   __shared__ uint64_t ws[32];
-  __shared__ float ex_s[1024];                         // exponentials of one token
-  __shared__ uint32_t cand[4][32];                     // per-warp top-k keys
-  __shared__ float red_s[4];
+  __shared__ __align__(16) uint16_t lg_s[4][1024];    // one token's logits per warp
   __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nch = H >> 3;                              // 16-byte chunks per row
@@ -361,89 +356,27 @@ __global__ void __launch_bounds__(128) decode_route_kernel(
   for (int i = tid; i < ncounters; i += 128) counters[1 + i] = 0;
   if (R > 32)
     for (int i = tid; i < E; i += 128) cnt[i] = 0;
-  constexpr int QPER = (PER + 3) / 4;                  // columns c of each warp's quarter
-  for (int t = 0; t < T; ++t) {
-    // (1) max: each warp over c in [warp*QPER, ...), then across warps
+  // every warp routes its tokens (t = warp, warp + 4, ...) from a copy of the
+  // token's logits in shared memory
+  for (int t = warp; t < T; t += 4) {
     const uint16_t* lrow = logits + (size_t)t * E;
-    float lv[QPER];
-    float m = -__int_as_float(0x7f800000);
-#pragma unroll
-    for (int q = 0; q < QPER; ++q) {
-      const int c = warp * QPER + q, ee = 32 * c + lane;
-      lv[q] = (c < PER && ee < E) ? bf2f(__ldcg(lrow + ee)) : -__int_as_float(0x7f800000);
-      m = fmaxf(m, lv[q]);
+    uint16_t* lw = lg_s[warp];
+    if ((E & 7) == 0) {
+      for (int i = lane; i < E / 8; i += 32)
+        reinterpret_cast<uint4*>(lw)[i] = __ldcg(reinterpret_cast<const uint4*>(lrow) + i);
+    } else {
+      for (int i = lane; i < E; i += 32) lw[i] = __ldcg(lrow + i);
     }
-    m = warp_max(m);
-    if (lane == 0) red_s[warp] = m;
-    __syncthreads();
-    m = fmaxf(fmaxf(red_s[0], red_s[1]), fmaxf(red_s[2], red_s[3]));
-    // (2) exponentials in parallel
-#pragma unroll
-    for (int q = 0; q < QPER; ++q) {
-      const int c = warp * QPER + q, ee = 32 * c + lane;
-      if (c < PER) ex_s[32 * c + lane] = (ee < E) ? cexp(__fsub_rn(lv[q], m)) : 0.0f;
+    __syncwarp();
+    const RouteOut ro = route_token<PER>(lw, E, k, lane);
+    if (lane < k) {
+      idx[(size_t)t * k + lane] = ro.e;
+      sidx[t * k + lane] = ro.e;
+      scores[(size_t)t * k + lane] = ro.score;
     }
-    __syncthreads();
-    // (3) the canonical denominator: lane partial over e = 32c + l in order,
-    // then the butterfly (one warp)
-    if (warp == 0) {
-      float part = 0.0f;
-#pragma unroll
-      for (int c = 0; c < PER; ++c)
-        if (32 * c + lane < E) part = __fadd_rn(part, ex_s[32 * c + lane]);
-      const float inv = __fdiv_rn(1.0f, warp_butterfly_sum(part));
-      if (lane == 0) red_s[0] = inv;
-    }
-    __syncthreads();
-    const float inv = red_s[0];
-    // (4) top-k of each warp's quarter by bf16 probability, lowest index on ties
-    uint32_t key[QPER];
-#pragma unroll
-    for (int q = 0; q < QPER; ++q) {
-      const int c = warp * QPER + q, ee = 32 * c + lane;
-      key[q] = (c < PER && ee < E)
-                   ? (((uint32_t)f2bf(__fmul_rn(ex_s[32 * c + lane], inv)) << 16) | (uint32_t)(0xffff - ee))
-                   : 0u;
-    }
-    for (int j = 0; j < k; ++j) {
-      uint32_t best = 0;
-#pragma unroll
-      for (int q = 0; q < QPER; ++q) best = key[q] > best ? key[q] : best;
-      const uint32_t win = __reduce_max_sync(0xffffffffu, best);
-#pragma unroll
-      for (int q = 0; q < QPER; ++q)
-        if (key[q] == win) key[q] = 0;
-      if (lane == j) cand[warp][j] = win;
-    }
-    __syncthreads();
-    // (5) the final top-k over the 4k candidates, in selection order
-    if (warp == 0) {
-      uint32_t ck[4];
-#pragma unroll
-      for (int w = 0; w < 4; ++w) ck[w] = lane < k ? cand[w][lane] : 0u;
-      uint32_t my_key = 0;
-      float ssum = 0.0f;
-      for (int j = 0; j < k; ++j) {
-        uint32_t best = 0;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) best = ck[w] > best ? ck[w] : best;
-        const uint32_t win = __reduce_max_sync(0xffffffffu, best);
-#pragma unroll
-        for (int w = 0; w < 4; ++w)
-          if (ck[w] == win) ck[w] = 0;
-        ssum = __fadd_rn(ssum, bf2f((uint16_t)(win >> 16)));
-        if (lane == j) my_key = win;
-      }
-      const float sb = bfround(ssum);
-      if (lane < k) {
-        const int my_e = 0xffff - (int)(my_key & 0xffffu);
-        idx[(size_t)t * k + lane] = my_e;
-        sidx[t * k + lane] = my_e;
-        scores[(size_t)t * k + lane] = f2bf(__fdiv_rn(bf2f((uint16_t)(my_key >> 16)), sb));
-      }
-    }
-    __syncthreads();
+    __syncwarp();
   }
+  __syncthreads();
   if (R <= 32) {
     // One warp: bitonic sort of (expert, pair) keys; the pair index makes the
     // order stable.  Sorted position j holds pair order[j]; the first position

@@ -129,17 +129,23 @@ struct LayerArgs {
   const uint32_t* dnw; const uint16_t* dns; const uint16_t* dnb;     // down [E][H][..]
   const uint32_t* sguw; const uint16_t* sgus; const uint16_t* sgub;  // shared gate_up [2Is][..]
   const uint32_t* sdnw; const uint16_t* sdns; const uint16_t* sdnb;  // shared down [H][..]
-  uint16_t* logits;      // [T][E] workspace
-  float* gate_logit;     // [T]
-  float* h;              // [T*k][I] fp32
-  float* hs;             // [T][Is] fp32
-  int32_t* bar;          // 4 words: barrier counts and generations (counts zero between launches)
+  // Exchanges between CTAs (no grid barrier): the logits carry the launch
+  // epoch in every word (a reader waits until the tags match); h is
+  // published by a release-increment of gucnt per gate_up tile.
+  int32_t* epoch;                // launch epoch counter, only this kernel writes it
+  unsigned long long* gucnt;     // gate_up tiles finished, all launches (only grows)
+  unsigned long long* tlog;      // [T][E] bf16 logit | epoch << 32
+  unsigned long long* tgate;     // [T] fp32 gate logit | epoch << 32
+  int32_t* tseen;                // [kLayerMaxCtas] epoch seen by each CTA at its start
+  uint32_t* th;                  // [T*k][I] h as fp16 hi | fp16 lo << 16
+  uint32_t* ths;                 // [T][Is] the same for the shared expert
   int32_t* idx;          // [T][k] out
   uint16_t* scores;      // [T][k] out
   uint16_t* y;           // [T][H] out
   int T, H, E, k, I, Is;
 };
 constexpr int kLayerMaxT = 4;
+constexpr int kLayerMaxCtas = 256;   // the grid is one CTA per SM
 // Ring stages for the plan (2..4), or 0 when the shape cannot take this path.
 int decode_layer_stages(int T, int H, int E, int k, int I, int Is, int nct);
 int decode_layer_ctas();

@@ -98,13 +98,21 @@ def _unwire(t: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
     return t.view(torch.bfloat16) if like.dtype == torch.bfloat16 else t
 
 
+def _mark(marks, name):
+    if marks is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        marks.append((name, ev))
+
+
 def ep_forward(x: torch.Tensor, idx: torch.Tensor, experts_per_rank: int, expert_fn: Callable,
-               combine_fn: Callable, group=None):
+               combine_fn: Callable, group=None, marks: list | None = None):
     """One expert-parallel MoE layer on this rank's tokens x [T, H] with their
     expert ids idx [T, k].  expert_fn(rows, pair_row, pair_exp) -> [P, H]
     bf16 applies this rank's experts to the pairs it serves;
     combine_fn(ys, inv) -> [T, H] bf16 forms the output from every token's k
-    expert outputs ys[inv[t*k + j]]."""
+    expert outputs ys[inv[t*k + j]].  marks (GPU runs): a list that receives
+    (phase, CUDA event) after each phase, for timing."""
     world = dist.get_world_size(group)
     T, k = idx.shape
     plan = plan_dispatch(idx, experts_per_rank, world)
@@ -114,18 +122,25 @@ def ep_forward(x: torch.Tensor, idx: torch.Tensor, experts_per_rank: int, expert
     bounds = torch.cumsum(plan.send_counts, 0)
     csum = torch.cat([slots_per_row.new_zeros(1), torch.cumsum(slots_per_row, 0)])
     counts[:, 1] = csum[bounds] - csum[bounds - plan.send_counts]
+    _mark(marks, "plan")
     recv = torch.empty_like(counts)
     dist.all_to_all_single(recv, counts, group=group)
     c = counts.cpu()
     rc = recv.cpu()
+    _mark(marks, "counts")
     rows_out, rows_in = c[:, 0].tolist(), rc[:, 0].tolist()
     pairs_back, pairs_recv = c[:, 1].tolist(), rc[:, 1].tolist()
     rows = _unwire(_exchange(_wire(x[plan.send_token]), rows_out, rows_in, group), x)
     ids = _exchange(plan.local_ids, rows_out, rows_in, group)
+    _mark(marks, "dispatch")
     pair_row, pair_exp = pairs_from_meta(ids)
     y_pairs = expert_fn(rows, pair_row, pair_exp)
+    _mark(marks, "experts")
     back = _unwire(_exchange(_wire(y_pairs), pairs_recv, pairs_back, group), y_pairs)
-    return combine_fn(back, return_slots(plan, T, k))
+    _mark(marks, "return")
+    y = combine_fn(back, return_slots(plan, T, k))
+    _mark(marks, "combine")
+    return y
 
 
 class ExpertParallelMoE(torch.nn.Module):
@@ -197,15 +212,19 @@ class ExpertParallelMoE(torch.nn.Module):
                   ops.stream_ptr(scores.device))
         return y
 
-    def forward(self, x: torch.Tensor, options: _lib.Options | None = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, options: _lib.Options | None = None,
+                marks: list | None = None) -> torch.Tensor:
         xf = x.reshape(-1, self.hidden).contiguous()
+        _mark(marks, "start")
         idx, scores = ops.router_topk(xf, self.gate_weight, self.top_k)
+        _mark(marks, "router")
         shared_out = gate_logit = None
         if self.shared_expert is not None:
             gate_logit = (xf.float() @ self.shared_gate.float().t()).reshape(-1).contiguous()
             shared_out = self.shared_expert(xf).contiguous()
+        _mark(marks, "shared")
         mode = options.wsum_mode if options is not None else 0
         y = ep_forward(xf, idx, self.epr, lambda *a: self.experts(*a, options=options),
                        lambda ys, inv: self.combine(ys, inv, scores, shared_out, gate_logit, mode),
-                       self.group)
+                       self.group, marks)
         return y.reshape(x.shape)
