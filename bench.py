@@ -297,6 +297,17 @@ def bench_decode(args, world, device, blocks):
                          "GBps": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
                          "unique_experts_mean": round(float(np.mean(uniq)), 1),
                          "bytes_per_layer": int(nbytes / len(blocks))}
+        if T <= 4:
+            # the same step on the three-launch pipeline (options.decode_kernel = 1)
+            o1 = decode_opts()
+            o1.decode_kernel = 1
+
+            def step1(x=x, o1=o1):
+                for b in blocks:
+                    b(x, options=o1)
+
+            ms1 = time_graph(step1, args.steps, args.warmup, world)
+            sweep[str(T)]["three_launch_us_per_layer"] = round(1000 * ms1 / len(blocks), 3)
         if T == HEADLINE_T:
             head = (x, ms, us, nbytes)
     return blocks, opts, sweep, head

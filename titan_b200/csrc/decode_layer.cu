@@ -27,9 +27,9 @@
 //      the router) and as the fp16 MMA operand with exact 64-group sums (for
 //      gate_up).  Warp 0 computes the CTA's router rows and publishes them;
 //      the other warps compute the shared expert's gate_up tiles meanwhile.
-//   2. Every CTA waits for all logits and routes every token itself, the
-//      8 warps split over the tokens (8 / T warps per token), and builds the
-//      plan (pairs sorted by expert, distinct experts): no second round trip.
+//   2. Every CTA waits for all logits and routes every token itself (one
+//      warp per token) and builds the plan (pairs sorted by expert, distinct
+//      experts): no second round trip.
 //   3. The routed gate_up tiles (16 weight rows = 8 gate + 8 up rows over the
 //      full K, one warp each) are spread over all CTAs, balanced against each
 //      CTA's down work.  Every warp streams its tiles through a private ring
@@ -123,7 +123,7 @@ TMOE_DEV void cp_async_wait_n() {
 struct LayerPlan {
   int ntp, rpc, R, spc, cs_r, cs_s, gi, gs;
   int off_xraw, off_x16, off_xs, off_rows, off_rt, off_bh, off_bl, off_bx, off_sh, off_sl, off_sx,
-      off_ex, off_res, off_ring, total;
+      off_res, off_ring, total;
   TMOE_HD LayerPlan(int T, int H, int E, int k, int I, int Is, int nct, int ns) {
     ntp = T <= 1 ? 1 : (T <= 2 ? 2 : 4);
     rpc = (E + 1 + nct - 1) / nct;
@@ -142,8 +142,7 @@ struct LayerPlan {
     off_rt = o;   o += (8 * R + 16) * 4;            // routing scratch (ints / floats)
     o = (o + 15) & ~15;
     // h operands: routed pairs, then the shared expert's T columns.  The
-    // routing phase uses the same space first: logits (T x E bf16), then the
-    // exponentials / keys (T x 32 ceil(E / 32) words).
+    // routing phase uses the same space first for the logits (T x E bf16).
     const int st0 = o;
     off_bh = o;   o += R * cs_r;
     off_bl = o;   o += R * cs_r;
@@ -151,8 +150,7 @@ struct LayerPlan {
     off_sh = o;   o += T * cs_s;
     off_sl = o;   o += T * cs_s;
     off_sx = o;   o += T * gs * 4;
-    off_ex = st0 + ((T * E * 2 + 15) & ~15);
-    const int rt_end = off_ex + T * ((E + 31) / 32) * 32 * 4;
+    const int rt_end = st0 + T * E * 2;
     if (o < rt_end) o = rt_end;
     o = (o + 15) & ~15;
     off_res = o;  o += spc * (R + T) * 16 * 4;
@@ -195,7 +193,9 @@ TMOE_DEV void issue_stage(uint8_t* st, const Job& jb, int ch, int lane) {
 
 // One stage of MMAs: 8 groups; B columns from bgh (+ bgl for fp32 sources
 // split into hi + lo), column sums xs0 / xs1 for the thread's two D columns.
-// Out of line, one copy per variant, groups not unrolled (instruction cache).
+// Two groups per iteration and separate hi / lo accumulators, so four
+// independent MMA chains are in flight (each MMA waits for the previous one
+// on the same accumulator); out of line, one copy per variant.
 template <bool LO>
 __device__ __noinline__ float4 stage_mma(const uint8_t* st, int gbase, const uint8_t* bgh,
                                          const uint8_t* bgl, const float* xs0, const float* xs1,
@@ -205,44 +205,61 @@ __device__ __noinline__ float4 stage_mma(const uint8_t* st, int gbase, const uin
   const uint16_t* sp = reinterpret_cast<const uint16_t*>(st + kStageW);
   const uint16_t* bp = sp + 128;
 #pragma unroll 1
-  for (int j = 0; j < 8; ++j) {
-    const int sw = ((2 * j + (t >> 1)) ^ g) << 4;            // chunk 2j + t/2 of rows g, g + 8
-    const uint2 wl = *reinterpret_cast<const uint2*>(wp + sw);
-    const uint2 wh = *reinterpret_cast<const uint2*>(wp + 8 * kRowStride + sw);
-    const int gj = gbase + j;
-    const uint4* hp = reinterpret_cast<const uint4*>(bgh + gj * 128 + t * 32);
-    const uint4 h0 = hp[0], h1 = hp[1];
-    uint4 l0 = h0, l1 = h1;
-    if (LO) {
-      const uint4* lp = reinterpret_cast<const uint4*>(bgl + gj * 128 + t * 32);
-      l0 = lp[0];
-      l1 = lp[1];
-    }
-    uint32_t qL[8], qH[8];
-    qpairs4(wl.x, qL);
-    qpairs4(wl.y, qL + 4);
-    qpairs4(wh.x, qH);
-    qpairs4(wh.y, qH + 4);
-    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int j0 = 0; j0 < 8; j0 += 2) {
+    float d[2][4], e[2][4];
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const int pi = (kk >> 1) * 4 + (kk & 1) * 2;
-      const uint32_t a0 = qL[pi], a1 = qH[pi], a2 = qL[pi + 1], a3 = qH[pi + 1];
-      const uint4 hb = (kk < 2) ? h0 : h1;
-      mma16816(d, a0, a1, a2, a3, (kk & 1) ? hb.z : hb.x, (kk & 1) ? hb.w : hb.y);
+    for (int u = 0; u < 2; ++u) {
+      const int j = j0 + u;
+      const int sw = ((2 * j + (t >> 1)) ^ g) << 4;          // chunk 2j + t/2 of rows g, g + 8
+      const uint2 wl = *reinterpret_cast<const uint2*>(wp + sw);
+      const uint2 wh = *reinterpret_cast<const uint2*>(wp + 8 * kRowStride + sw);
+      const int gj = gbase + j;
+      const uint4* hp = reinterpret_cast<const uint4*>(bgh + gj * 128 + t * 32);
+      const uint4 h0 = hp[0], h1 = hp[1];
+      uint4 l0 = h0, l1 = h1;
       if (LO) {
-        const uint4 lb = (kk < 2) ? l0 : l1;
-        mma16816(d, a0, a1, a2, a3, (kk & 1) ? lb.z : lb.x, (kk & 1) ? lb.w : lb.y);
+        const uint4* lp = reinterpret_cast<const uint4*>(bgl + gj * 128 + t * 32);
+        l0 = lp[0];
+        l1 = lp[1];
+      }
+      uint32_t qL[8], qH[8];
+      qpairs4(wl.x, qL);
+      qpairs4(wl.y, qL + 4);
+      qpairs4(wh.x, qH);
+      qpairs4(wh.y, qH + 4);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        d[u][q] = 0.0f;
+        e[u][q] = 0.0f;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int pi = (kk >> 1) * 4 + (kk & 1) * 2;
+        const uint32_t a0 = qL[pi], a1 = qH[pi], a2 = qL[pi + 1], a3 = qH[pi + 1];
+        const uint4 hb = (kk < 2) ? h0 : h1;
+        mma16816(d[u], a0, a1, a2, a3, (kk & 1) ? hb.z : hb.x, (kk & 1) ? hb.w : hb.y);
+        if (LO) {
+          const uint4 lb = (kk < 2) ? l0 : l1;
+          mma16816(e[u], a0, a1, a2, a3, (kk & 1) ? lb.z : lb.x, (kk & 1) ? lb.w : lb.y);
+        }
       }
     }
-    const float sl = bf2f(sp[g * 8 + j]), sh = bf2f(sp[(g + 8) * 8 + j]);
-    const float bl = __fadd_rn(bf2f(bp[g * 8 + j]), __fmul_rn(8.0f, sl));
-    const float bh = __fadd_rn(bf2f(bp[(g + 8) * 8 + j]), __fmul_rn(8.0f, sh));
-    const float x0 = xs0[gj], x1 = xs1[gj];
-    acc[0] = __fmaf_rn(sl, d[0], __fmaf_rn(bl, x0, acc[0]));
-    acc[1] = __fmaf_rn(sl, d[1], __fmaf_rn(bl, x1, acc[1]));
-    acc[2] = __fmaf_rn(sh, d[2], __fmaf_rn(bh, x0, acc[2]));
-    acc[3] = __fmaf_rn(sh, d[3], __fmaf_rn(bh, x1, acc[3]));
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int j = j0 + u, gj = gbase + j;
+      if (LO) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) d[u][q] = __fadd_rn(d[u][q], e[u][q]);
+      }
+      const float sl = bf2f(sp[g * 8 + j]), sh = bf2f(sp[(g + 8) * 8 + j]);
+      const float bl = __fadd_rn(bf2f(bp[g * 8 + j]), __fmul_rn(8.0f, sl));
+      const float bh = __fadd_rn(bf2f(bp[(g + 8) * 8 + j]), __fmul_rn(8.0f, sh));
+      const float x0 = xs0[gj], x1 = xs1[gj];
+      acc[0] = __fmaf_rn(sl, d[u][0], __fmaf_rn(bl, x0, acc[0]));
+      acc[1] = __fmaf_rn(sl, d[u][1], __fmaf_rn(bl, x1, acc[1]));
+      acc[2] = __fmaf_rn(sh, d[u][2], __fmaf_rn(bh, x0, acc[2]));
+      acc[3] = __fmaf_rn(sh, d[u][3], __fmaf_rn(bh, x1, acc[3]));
+    }
   }
   return make_float4(acc[0], acc[1], acc[2], acc[3]);
 }
@@ -507,101 +524,27 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
   // every CTA has read the gate_up counter by now: the shared-expert tiles of
   // phase 1 are counted from here
   if (n_sh > 0) publish_tiles(A.gucnt, (unsigned long long)n_sh, lane);
-  // Routing: token tt gets W = 8 / T warps; warp wi of the token owns the
-  // columns c in [wi C / W, (wi + 1) C / W) of the lane-major layout
-  // e = 32 c + lane (C = ceil(E / 32)).  The arithmetic of route_token (max,
-  // cexp(l - max), the canonical denominator by one warp: lane partials over
-  // c ascending, then the butterfly; keys bf16(p) << 16 | 0xffff - e;
-  // selection by key), with the top-k taken per warp and merged: the same
-  // selection order as one warp over all E.
-  {
-    __shared__ float s_redmax[kLWarps];
-    __shared__ float s_inv[kLayerMaxT];
-    __shared__ uint32_t s_cand[kLWarps * 32];
-    const int W = kLWarps / T;
-    const int tt = warp / W, wi = warp % W;
-    const bool active = tt < T;
-    const int C = (E + 31) / 32;
-    const int cb = (wi * C) / W, ce = ((wi + 1) * C) / W;
-    float* ex = reinterpret_cast<float*>(sm + L.off_ex) + (size_t)(active ? tt : 0) * C * 32;
-    uint32_t* key = reinterpret_cast<uint32_t*>(ex);
-    const uint16_t* lg = lg_s + (size_t)(active ? tt : 0) * E;
-    float m = -__int_as_float(0x7f800000);
-    if (active)
-      for (int cc = cb; cc < ce; ++cc) {
-        const int e = 32 * cc + lane;
-        const float v = e < E ? bf2f(lg[e]) : -__int_as_float(0x7f800000);
-        ex[32 * cc + lane] = v;
-        m = fmaxf(m, v);
-      }
-    m = warp_max(m);
-    if (lane == 0) s_redmax[warp] = m;
-    __syncthreads();
-    if (active) {
-      float M = s_redmax[tt * W];
-      for (int w2 = 1; w2 < W; ++w2) M = fmaxf(M, s_redmax[tt * W + w2]);
-      for (int cc = cb; cc < ce; ++cc) {
-        const int e = 32 * cc + lane;
-        ex[32 * cc + lane] = e < E ? cexp(__fsub_rn(ex[32 * cc + lane], M)) : 0.0f;
-      }
-    }
-    __syncthreads();
-    if (active && wi == 0) {
-      float part = 0.0f;
-#pragma unroll 4
-      for (int cc = 0; cc < C; ++cc)
-        if (32 * cc + lane < E) part = __fadd_rn(part, ex[32 * cc + lane]);
-      const float inv = __fdiv_rn(1.0f, warp_butterfly_sum(part));
-      if (lane == 0) s_inv[tt] = inv;
-    }
-    __syncthreads();
-    if (active) {
-      const float inv = s_inv[tt];
-      for (int cc = cb; cc < ce; ++cc) {
-        const int e = 32 * cc + lane;
-        key[32 * cc + lane] =
-            e < E ? (((uint32_t)f2bf(__fmul_rn(ex[32 * cc + lane], inv)) << 16) | (uint32_t)(0xffff - e))
-                  : 0u;
-      }
-      __syncwarp();
-      for (int j = 0; j < k; ++j) {                 // this warp's k best, best first
-        uint32_t best = 0;
-        for (int cc = cb; cc < ce; ++cc) best = max(best, key[32 * cc + lane]);
-        const uint32_t win = __reduce_max_sync(0xffffffffu, best);
-        if (win != 0u) {
-          const int ew = 0xffff - (int)(win & 0xffffu);
-          if ((ew & 31) == lane) key[ew] = 0u;
-        }
-        if (lane == 0) s_cand[warp * k + j] = win;
-        __syncwarp();
-      }
-    }
-    __syncthreads();
-    if (active && wi == 0) {                        // merge the W lists of the token
-      uint32_t* cand = s_cand + tt * W * k;
-      const int ncand = W * k;
-      float ssum = 0.0f;
-      uint32_t my_key = 0;
-      for (int j = 0; j < k; ++j) {
-        uint32_t best = 0;
-        for (int q = lane; q < ncand; q += 32) best = max(best, cand[q]);
-        const uint32_t win = __reduce_max_sync(0xffffffffu, best);
-        for (int q = lane; q < ncand; q += 32)
-          if (cand[q] == win) cand[q] = 0u;
-        ssum = __fadd_rn(ssum, bf2f((uint16_t)(win >> 16)));
-        if (lane == j) my_key = win;
-        __syncwarp();
-      }
-      const float sb = bfround(ssum);
-      if (lane < k) {
-        const int e = 0xffff - (int)(my_key & 0xffffu);
-        const uint16_t sc = f2bf(__fdiv_rn(bf2f((uint16_t)(my_key >> 16)), sb));
-        s_idx[tt * k + lane] = e;
-        s_score[tt * k + lane] = bf2f(sc);
-        if (c == 0) {
-          A.idx[(size_t)tt * k + lane] = e;
-          A.scores[(size_t)tt * k + lane] = sc;
-        }
+  // Routing: warp w routes token w (route_token: keys in registers, sorted
+  // per lane, k rounds of warp max over the lane heads)
+  if (warp < T) {
+    const int tt = warp;
+    const uint16_t* lg = lg_s + (size_t)tt * E;
+    const int per = (E + 31) / 32;
+    RouteOut ro;
+    if (per <= 4)
+      ro = route_token<4>(lg, E, k, lane);
+    else if (per <= 8)
+      ro = route_token<8>(lg, E, k, lane);
+    else if (per <= 16)
+      ro = route_token<16>(lg, E, k, lane);
+    else
+      ro = route_token<32>(lg, E, k, lane);
+    if (lane < k) {
+      s_idx[tt * k + lane] = ro.e;
+      s_score[tt * k + lane] = bf2f(ro.score);
+      if (c == 0) {
+        A.idx[(size_t)tt * k + lane] = ro.e;
+        A.scores[(size_t)tt * k + lane] = ro.score;
       }
     }
   }

@@ -410,6 +410,35 @@ __global__ void __launch_bounds__(128) decode_route_kernel(
         plan.ustart[__popc(mask)] = R;
       }
     }
+  } else if (R <= 128) {
+    // one thread per pair: its sorted position is the number of pairs with a
+    // smaller (expert, pair) key; the first pair of an expert opens a segment
+    int e = 0, pos = 0, first = 0;
+    if (tid < R) {
+      e = sidx[tid];
+      first = 1;
+      for (int j = 0; j < R; ++j) {
+        const int ej = sidx[j];
+        pos += (ej < e) || (ej == e && j < tid);
+        if (ej == e && j < tid) first = 0;
+      }
+      plan.order[pos] = tid;
+      plan.inv[tid] = pos;
+      cnt[tid] = first;
+    }
+    __syncthreads();
+    if (tid < R && first) {
+      int u = 0;
+      for (int j = 0; j < R; ++j) u += (cnt[j] && sidx[j] < e);
+      plan.uexp[u] = e;
+      plan.ustart[u] = pos;
+    }
+    if (tid == 0) {
+      int n = 0;
+      for (int j = 0; j < R; ++j) n += cnt[j];
+      plan.nuniq[0] = n;
+      plan.ustart[n] = R;
+    }
   } else {
     for (int i = tid; i < R; i += 128) atomicAdd(&cnt[sidx[i]], 1);
     __syncthreads();
