@@ -255,6 +255,20 @@ int tmoe_moe_experts(const tmoe_layer* layer, const uint16_t* x, int R, const in
                      const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
                      size_t ws_bytes, uint16_t* y_pairs, void* stream);
 
+/* Source side, before the exchanges: the token-local part of the layer on
+ * this rank's tokens, with the kernels and arguments of tmoe_moe_forward's
+ * grouped-GEMM path (language.py:74-84 and 85-90: the router Linear, softmax
+ * top-k, the shared expert and its gate logit).  `layer` needs the router,
+ * and the shared expert with its prepared tables when shared_inter > 0
+ * (routed-expert fields unused).  idx [T, k] int32, scores [T, k] bf16;
+ * gate_logit [T] fp32 and shared_out [T, H] bf16 when shared_inter > 0.
+ * With these, the expert-parallel layer equals the single-device block bit
+ * for bit on the int8 path, shared expert included. */
+size_t tmoe_moe_local_workspace_size(const tmoe_layer* layer, int T, const tmoe_options* opt);
+int tmoe_moe_local(const tmoe_layer* layer, const uint16_t* x, int T, const tmoe_options* opt,
+                   void* ws, size_t ws_bytes, int32_t* idx, uint16_t* scores, float* gate_logit,
+                   uint16_t* shared_out, void* stream);
+
 /* Source side: the block's top-k weighted sum (moe_weighted_sum.py:142-195;
  * mode 0 clone, 1 fast) of every token's k expert outputs ys[inv[t*k+j]] plus
  * the sigmoid-gated shared expert (language.py:85-91; shared_out [T, D] bf16

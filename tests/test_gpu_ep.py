@@ -1,9 +1,9 @@
-"""Expert parallelism on GPUs: the routed experts of a rank on received rows
+"""Expert parallelism on GPUs: the token-local part (router, top-k, shared
+expert: tmoe_moe_local), the routed experts of a rank on received rows
 (tmoe_moe_experts), the NCCL exchanges and the block's weighted sum
-(tmoe_moe_combine), through ExpertParallelMoE.  Without a shared expert the
-layer must equal the single-GPU block bit for bit (int8 path); with one, the
-shared expert and its gate are evaluated by the modular ops, so the output is
-held to the north-star tolerance on the operands of the final add."""
+(tmoe_moe_combine), through ExpertParallelMoE.  The layer must equal the
+single-GPU block bit for bit on the int8 path, with and without a shared
+expert, and stay within the north-star tolerance of the oracle."""
 import os
 import socket
 
@@ -67,6 +67,7 @@ def test_ep_single_rank_matches_block(cuda, oracle):
             y0 = ep0(bf(x), options=_opts(1))
             assert torch.equal(y0.view(torch.int16), blk0(bf(x), options=_opts(1)).view(torch.int16))
             y = ep(bf(x), options=_opts(1))
+            assert torch.equal(y.view(torch.int16), blk(bf(x), options=_opts(1)).view(torch.int16))
             torch.cuda.synchronize()
             _compare(oracle, L, x, nbf(y))
     finally:
@@ -125,5 +126,6 @@ def test_ep_two_gpus_nccl(oracle):
         assert not isinstance(out, str), f"rank {rank}: {out}"
         y, yb, _, _ = out["plain"]
         assert np.array_equal(y, yb), f"rank {rank}: EP differs from the single-GPU block"
-        y, _, ry, ops = out["shared"]
+        y, yb, ry, ops = out["shared"]
+        assert np.array_equal(y, yb), f"rank {rank}: EP with a shared expert differs from the block"
         assert_bf16_close(y, ry, what=f"EP rank {rank}", operands=ops, operand_ulps=4)

@@ -111,6 +111,8 @@ _SIGS = {
     "tmoe_moe_experts": ([C.POINTER(Layer), P, I32, P, P, I32, C.POINTER(Options), P, SZ, P, P],
                          I32),
     "tmoe_moe_combine": ([P, P, P, I32, I32, I32, I32, P, P, P, P], I32),
+    "tmoe_moe_local_workspace_size": ([C.POINTER(Layer), I32, C.POINTER(Options)], SZ),
+    "tmoe_moe_local": ([C.POINTER(Layer), P, I32, C.POINTER(Options), P, SZ, P, P, P, P, P], I32),
 }
 
 EXPORTED = tuple(_SIGS)

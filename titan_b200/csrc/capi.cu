@@ -1097,6 +1097,105 @@ int tmoe_moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_
 // The source side: the block's weighted sum (clone or fast mode) over every
 // token's k expert outputs, wherever they were computed, plus the gated
 // shared expert — the last step of tmoe_moe_forward.
+// ------------------------------------------------ the token-local part of a layer
+
+namespace {
+tmoe_options local_options(const tmoe_options* opt) {
+  tmoe_options o = opt ? *opt : tmoe_options{512, 1, 0, 1, 0, 0};
+  o.min_tokens = 1;   // the prefill (grouped-GEMM) semantics at every T
+  return o;
+}
+}  // namespace
+
+size_t tmoe_moe_local_workspace_size(const tmoe_layer* L, int T, const tmoe_options* opt) {
+  if (!L || T < 0) return 0;
+  const tmoe_options o = local_options(opt);
+  Carve c(nullptr);
+  return carve_block(c, L, T, &o, nullptr);
+}
+
+int tmoe_moe_local(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_options* opt,
+                   void* ws, size_t ws_bytes, int32_t* idx, uint16_t* scores, float* gate_logit,
+                   uint16_t* shared_out, void* stream) {
+  if (!L) return fail(TMOE_ERR_INVALID, "tmoe_moe_local: null layer");
+  const int H = L->hidden, E = L->num_experts, k = L->top_k, Is = L->shared_inter;
+  if (T < 0 || Is < 0) return fail(TMOE_ERR_INVALID, "tmoe_moe_local: bad sizes");
+  if (int rc = check_router(T, H, E, k)) return rc;
+  if (!L->router_w) return fail(TMOE_ERR_INVALID, "tmoe_moe_local: missing router weight");
+  if (Is > 0) {
+    if (!L->shared_gate_up_w || !L->shared_gate_up_st || !L->shared_gate_up_bt ||
+        !L->shared_down_w || !L->shared_down_st || !L->shared_down_bt || !L->shared_gate_w)
+      return fail(TMOE_ERR_INVALID, "tmoe_moe_local: the shared expert needs weights and tables");
+    if (Is % 64) return fail(TMOE_ERR_UNSUPPORTED, "tmoe_moe_local: need Is %% 64 == 0");
+    if (!shared_out || !gate_logit)
+      return fail(TMOE_ERR_INVALID, "tmoe_moe_local: null shared_out or gate_logit");
+  }
+  if (T == 0) return TMOE_OK;
+  if (!x || !idx || !scores) return fail(TMOE_ERR_INVALID, "tmoe_moe_local: null x, idx or scores");
+  const tmoe_options o = local_options(opt);
+  const size_t need = tmoe_moe_local_workspace_size(L, T, opt);
+  if (!ws || ws_bytes < need)
+    return fail(TMOE_ERR_WORKSPACE, "tmoe_moe_local: workspace %zu < %zu bytes", ws_bytes, need);
+  const int G = H / 64;
+  Carve c(ws);
+  BlockWs b;
+  carve_block(c, L, T, &o, &b);
+  cudaStream_t s = S(stream);
+  const uint16_t* wg = Is > 0 ? L->shared_gate_w : nullptr;
+  // the block's prefill steps, the same kernels and arguments
+  TMOE_TRY(launch_router_logits(x, L->router_w, wg, T, H, E, b.logits,
+                                Is > 0 ? gate_logit : b.gate_logit, s),
+           "router_logits");
+  TMOE_TRY(launch_router_topk(b.logits, T, E, k, idx, scores, nullptr, s), "router_topk");
+  if (Is == 0) return TMOE_OK;
+  if (opt_tc05(&o))
+    TMOE_TRY(launch_prep_a16(x, T, H, false, b.sx16p, nullptr, b.sxsum, s), "prep_x");
+  else
+    TMOE_TRY(launch_prep_x(x, T, H, b.sx16p, b.sxsum, G, 1, s), "prep_x");
+  auto gemm = [&](int epi, const GemmParams& P, int ntiles_max) {
+    return opt_tc05(&o) ? launch_gemm_tc05(false, epi, P, ntiles_max, s)
+                        : launch_gemm_grouped(false, epi, P, ntiles_max, s);
+  };
+  const int st = (T + kTileM - 1) / kTileM;
+  TMOE_TRY(launch_dense_tiles(T, kTileM, b.s_tile_row, b.s_tile_exp, b.s_ntiles, b.s_offsets, s),
+           "dense_tiles");
+  GemmParams sg{};
+  sg.A = b.sx16p;
+  sg.ars = b.sxsum;
+  sg.s_r = G;
+  sg.s_g = 1;
+  sg.W = L->shared_gate_up_w;
+  sg.st = L->shared_gate_up_st;
+  sg.bt = L->shared_gate_up_bt;
+  sg.tile_row = b.s_tile_row;
+  sg.tile_exp = b.s_tile_exp;
+  sg.ntiles = b.s_ntiles;
+  sg.offsets = b.s_offsets;
+  sg.K = H;
+  sg.N = 2 * Is;
+  sg.hrs = b.shrs;
+  sg.Rpad_h = T;
+  sg.h16p = b.sh16p;
+  TMOE_TRY(gemm(kEpiSwigluH16, sg, st), "gemm_shared_gate_up");
+  GemmParams sd{};
+  sd.A = b.sh16p;
+  sd.ars = b.shrs;
+  sd.s_r = 1;
+  sd.s_g = T;
+  sd.W = L->shared_down_w;
+  sd.st = L->shared_down_st;
+  sd.bt = L->shared_down_bt;
+  sd.tile_row = b.s_tile_row;
+  sd.tile_exp = b.s_tile_exp;
+  sd.ntiles = b.s_ntiles;
+  sd.offsets = b.s_offsets;
+  sd.K = Is;
+  sd.N = H;
+  sd.Y = shared_out;
+  TMOE_TRY(gemm(kEpiStore, sd, st), "gemm_shared_down");
+  return TMOE_OK;
+}
+
 int tmoe_moe_combine(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
                      int D, int mode, const uint16_t* shared_out, const float* gate_logit,
                      uint16_t* y, void* stream) {

@@ -420,24 +420,46 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty0 + 8 * b);
           }
+          // column scalars read 4 at a time (16-byte aligned in the stage)
+          const float4* cb4 = reinterpret_cast<const float4*>(cb + 32 * hh);
+          const float4* cs4 = reinterpret_cast<const float4*>(cs + 32 * hh);
           if (prescaled) {                     // d = D * s already (exact)
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              acc[32 * hh + c] = __fmaf_rn(d[c], xs, acc[32 * hh + c]);
-              acc[32 * hh + c] = __fmaf_rn(xr, cb[32 * hh + c], acc[32 * hh + c]);
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 b4 = cb4[c4];
+              const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int c = 4 * c4 + q;
+                acc[32 * hh + c] = __fmaf_rn(d[c], xs, acc[32 * hh + c]);
+                acc[32 * hh + c] = __fmaf_rn(xr, bv[q], acc[32 * hh + c]);
+              }
             }
           } else {
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const float t1 = __fmul_rn(d[c], cs[32 * hh + c]);
-              acc[32 * hh + c] = __fmaf_rn(t1, xs, acc[32 * hh + c]);
-              acc[32 * hh + c] = __fmaf_rn(xr, cb[32 * hh + c], acc[32 * hh + c]);
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 b4 = cb4[c4], s4 = cs4[c4];
+              const float bv[4] = {b4.x, b4.y, b4.z, b4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int c = 4 * c4 + q;
+                const float t1 = __fmul_rn(d[c], sv[q]);
+                acc[32 * hh + c] = __fmaf_rn(t1, xs, acc[32 * hh + c]);
+                acc[32 * hh + c] = __fmaf_rn(xr, bv[q], acc[32 * hh + c]);
+              }
             }
           }
         }
       } else {
+        const float4* cb4 = reinterpret_cast<const float4*>(cb);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) acc[c] = __fmaf_rn(xr, cb[c], acc[c]);
+        for (int c4 = 0; c4 < 16; ++c4) {
+          const float4 b4 = cb4[c4];
+          acc[4 * c4] = __fmaf_rn(xr, b4.x, acc[4 * c4]);
+          acc[4 * c4 + 1] = __fmaf_rn(xr, b4.y, acc[4 * c4 + 1]);
+          acc[4 * c4 + 2] = __fmaf_rn(xr, b4.z, acc[4 * c4 + 2]);
+          acc[4 * c4 + 3] = __fmaf_rn(xr, b4.w, acc[4 * c4 + 3]);
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * s);

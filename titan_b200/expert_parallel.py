@@ -21,7 +21,8 @@ the experts' arithmetic is fixed-order (the int8 path).
 
 Plumbing is ``torch.distributed`` (NCCL on GPUs, gloo in the CPU tests); the
 expert arithmetic is ``tmoe_moe_experts`` and the final sum
-``tmoe_moe_combine`` from libtitan_moe.so.  The dispatch plan is computed on
+``tmoe_moe_combine`` from libtitan_moe.so, and the token-local part (router,
+top-k, shared expert) ``tmoe_moe_local`` with the block's own kernels.  The dispatch plan is computed on
 the device with tensor ops; the host reads only the exchanged counts, which
 the variable-size all-to-all needs.
 """
@@ -46,40 +47,73 @@ class DispatchPlan:
     local_ids: torch.Tensor     # [S, k] int32 local expert id per slot, -1 if not on that rank
 
 
-def plan_dispatch(idx: torch.Tensor, experts_per_rank: int, world: int) -> DispatchPlan:
-    """Deduplicated dispatch plan of one rank's tokens; idx [T, k] global
-    expert ids.  Rows are ordered by destination rank, then by token."""
-    T, k = idx.shape
+def _compact(flags: torch.Tensor, n: int, values: torch.Tensor) -> torch.Tensor:
+    """values[flags] in order, for an n = flags.sum() the caller already knows
+    (no host synchronisation): positions from a cumulative sum, the rest of
+    the rows sent to a dummy slot n that is dropped."""
+    pos = torch.cumsum(flags.to(torch.int64), 0) - 1
+    pos = torch.where(flags, pos, torch.full_like(pos, n))
+    out = values.new_empty((n + 1,) + tuple(values.shape[1:]))
+    out.index_copy_(0, pos, values)
+    return out[:n]
+
+
+def _membership(idx: torch.Tensor, experts_per_rank: int, world: int):
+    T = idx.shape[0]
     dest = idx.long() // experts_per_rank                          # [T, k]
     member = torch.zeros(T, world, dtype=torch.bool, device=idx.device)
     if T:
         member.scatter_(1, dest, True)
-    d_idx, t_idx = member.t().nonzero(as_tuple=True)              # destination-major
+    return dest, member
+
+
+def plan_dispatch(idx: torch.Tensor, experts_per_rank: int, world: int,
+                  n_rows: int | None = None) -> DispatchPlan:
+    """Deduplicated dispatch plan of one rank's tokens; idx [T, k] global
+    expert ids.  Rows are ordered by destination rank, then by token.  n_rows
+    (the number of rows sent, if the caller knows it) avoids a host sync."""
+    T, k = idx.shape
+    dest, member = _membership(idx, experts_per_rank, world)
     send_counts = member.sum(0).to(torch.int64)
+    flat = member.t().reshape(-1)                                   # destination-major
+    if n_rows is None:
+        n_rows = int(flat.sum())
+    dev = idx.device
+    t_idx = _compact(flat, n_rows, torch.arange(T, device=dev).repeat(world))
+    d_idx = _compact(flat, n_rows, torch.arange(world, device=dev).repeat_interleave(T))
     on_d = dest[t_idx] == d_idx[:, None]                           # [S, k]
     local = torch.where(on_d, idx[t_idx].long() - d_idx[:, None] * experts_per_rank,
                         torch.full_like(dest[t_idx], -1)).to(torch.int32)
     return DispatchPlan(t_idx, send_counts, local.contiguous())
 
 
-def pairs_from_meta(local_ids: torch.Tensor):
+def pairs_from_meta(local_ids: torch.Tensor, n_pairs: int | None = None):
     """Received k-wide metadata -> the (row, local expert) pairs this rank
-    serves, row-major (row, then slot)."""
-    pair_row, slot = (local_ids >= 0).nonzero(as_tuple=True)
-    pair_exp = local_ids[pair_row, slot]
+    serves, row-major (row, then slot).  n_pairs (if known) avoids a host
+    sync."""
+    R, k = local_ids.shape
+    flags = (local_ids >= 0).reshape(-1)
+    if n_pairs is None:
+        n_pairs = int(flags.sum())
+    rows = torch.arange(R, device=local_ids.device).repeat_interleave(k)
+    pair_row = _compact(flags, n_pairs, rows)
+    pair_exp = _compact(flags, n_pairs, local_ids.reshape(-1))
     return pair_row.to(torch.int32).contiguous(), pair_exp.to(torch.int32).contiguous()
 
 
 def return_slots(plan: DispatchPlan, T: int, k: int) -> torch.Tensor:
     """Where each (token, slot) lands in the combine buffer: the owners send
     their pair outputs back in the order of the sent rows (destination, then
-    token) and, inside a row, of the slots; inv [T*k] int32."""
-    valid = plan.local_ids >= 0
-    r, j = valid.nonzero(as_tuple=True)
-    inv = torch.empty(T * k, dtype=torch.int32, device=plan.local_ids.device)
-    inv[plan.send_token[r] * k + j] = torch.arange(r.numel(), dtype=torch.int32,
-                                                     device=inv.device)
-    return inv
+    token) and, inside a row, of the slots; inv [T*k] int32.  Every (token,
+    slot) is served on exactly one rank, so all T*k entries are written."""
+    dev = plan.local_ids.device
+    valid = (plan.local_ids >= 0).reshape(-1)
+    pos = (torch.cumsum(valid.to(torch.int64), 0) - 1).to(torch.int32)
+    tgt = (plan.send_token.long()[:, None] * k + torch.arange(k, device=dev)[None, :]).reshape(-1)
+    tgt = torch.where(valid, tgt, torch.full_like(tgt, T * k))
+    inv = torch.empty(T * k + 1, dtype=torch.int32, device=dev)
+    inv.index_copy_(0, tgt, pos)
+    return inv[:T * k]
 
 
 def _exchange(t: torch.Tensor, send_counts: list[int], recv_counts: list[int], group) -> torch.Tensor:
@@ -115,13 +149,11 @@ def ep_forward(x: torch.Tensor, idx: torch.Tensor, experts_per_rank: int, expert
     (phase, CUDA event) after each phase, for timing."""
     world = dist.get_world_size(group)
     T, k = idx.shape
-    plan = plan_dispatch(idx, experts_per_rank, world)
-    counts = torch.stack([plan.send_counts,
-                          torch.zeros_like(plan.send_counts)], 1)   # rows, slots (filled below)
-    slots_per_row = (plan.local_ids >= 0).sum(1)
-    bounds = torch.cumsum(plan.send_counts, 0)
-    csum = torch.cat([slots_per_row.new_zeros(1), torch.cumsum(slots_per_row, 0)])
-    counts[:, 1] = csum[bounds] - csum[bounds - plan.send_counts]
+    # counts first (rows and pairs per destination), the one host sync of
+    # the layer (the variable-size all-to-all needs them on the host)
+    dest, member = _membership(idx, experts_per_rank, world)
+    pair_counts = torch.bincount(dest.reshape(-1), minlength=world)[:world]
+    counts = torch.stack([member.sum(0).to(torch.int64), pair_counts.to(torch.int64)], 1)
     _mark(marks, "plan")
     recv = torch.empty_like(counts)
     dist.all_to_all_single(recv, counts, group=group)
@@ -130,10 +162,11 @@ def ep_forward(x: torch.Tensor, idx: torch.Tensor, experts_per_rank: int, expert
     _mark(marks, "counts")
     rows_out, rows_in = c[:, 0].tolist(), rc[:, 0].tolist()
     pairs_back, pairs_recv = c[:, 1].tolist(), rc[:, 1].tolist()
+    plan = plan_dispatch(idx, experts_per_rank, world, n_rows=sum(rows_out))
     rows = _unwire(_exchange(_wire(x[plan.send_token]), rows_out, rows_in, group), x)
     ids = _exchange(plan.local_ids, rows_out, rows_in, group)
     _mark(marks, "dispatch")
-    pair_row, pair_exp = pairs_from_meta(ids)
+    pair_row, pair_exp = pairs_from_meta(ids, n_pairs=sum(pairs_recv))
     y_pairs = expert_fn(rows, pair_row, pair_exp)
     _mark(marks, "experts")
     back = _unwire(_exchange(_wire(y_pairs), pairs_recv, pairs_back, group), y_pairs)
@@ -169,7 +202,14 @@ class ExpertParallelMoE(torch.nn.Module):
         self.tables = (ops.build_tables(*self.gu), ops.build_tables(*self.dn))
         self.shared_expert = block.shared_expert
         self.shared_gate = block.shared_expert_gate_weight
+        self.shared_inter = block.shared_inter
+        self.num_experts = E
+        se = block.shared_expert
+        self.shared_tables = () if se is None else (
+            ops.build_tables(se.gate_up_proj.weight, se.gate_up_proj.scales, se.gate_up_proj.biases),
+            ops.build_tables(se.down_proj.weight, se.down_proj.scales, se.down_proj.biases))
         self._layer = None
+        self._local = None
 
     def _layer_struct(self) -> _lib.Layer:
         if self._layer is None:
@@ -182,6 +222,53 @@ class ExpertParallelMoE(torch.nn.Module):
             L.down_st, L.down_bt = self.tables[1].scales_t.data_ptr(), self.tables[1].biases_t.data_ptr()
             self._layer = L
         return self._layer
+
+    def _local_struct(self) -> _lib.Layer:
+        """The token-local part of the layer: the full router and the shared
+        expert (routed-expert fields left empty)."""
+        if self._local is None:
+            L = _lib.Layer()
+            L.hidden, L.num_experts, L.top_k = self.hidden, self.num_experts, self.top_k
+            L.moe_inter, L.shared_inter = self.moe_inter, self.shared_inter
+            L.router_w = self.gate_weight.data_ptr()
+            if self.shared_expert is not None:
+                se, t = self.shared_expert, self.shared_tables
+                L.shared_gate_up_w = se.gate_up_proj.weight.data_ptr()
+                L.shared_gate_up_s = se.gate_up_proj.scales.data_ptr()
+                L.shared_gate_up_b = se.gate_up_proj.biases.data_ptr()
+                L.shared_down_w = se.down_proj.weight.data_ptr()
+                L.shared_down_s = se.down_proj.scales.data_ptr()
+                L.shared_down_b = se.down_proj.biases.data_ptr()
+                L.shared_gate_up_st, L.shared_gate_up_bt = t[0].scales_t.data_ptr(), t[0].biases_t.data_ptr()
+                L.shared_down_st, L.shared_down_bt = t[1].scales_t.data_ptr(), t[1].biases_t.data_ptr()
+                L.shared_gate_w = self.shared_gate.data_ptr()
+            self._local = L
+        return self._local
+
+    def local(self, xf, options: _lib.Options | None = None):
+        """Router, top-k, shared expert and its gate logit on this rank's
+        tokens (tmoe_moe_local): the block's own kernels."""
+        T, dev = xf.shape[0], xf.device
+        idx = torch.empty(T, self.top_k, dtype=torch.int32, device=dev)
+        scores = torch.empty(T, self.top_k, dtype=torch.bfloat16, device=dev)
+        shared_out = gate_logit = None
+        if self.shared_expert is not None:
+            shared_out = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=dev)
+            gate_logit = torch.empty(T, dtype=torch.float32, device=dev)
+        if T == 0:
+            return idx, scores, shared_out, gate_logit
+        L = self._local_struct()
+        opt = options if options is not None else _lib.Options(512, 1, 0, 1, 0)
+        lib = _lib.load()
+        nb = lib.tmoe_moe_local_workspace_size(L, T, opt)
+        ws = ops.workspace(nb, dev, "ep_local")
+        _lib.check(lib.tmoe_moe_local(L, xf.data_ptr(), T, opt, ws.data_ptr(), ws.numel(),
+                                      idx.data_ptr(), scores.data_ptr(),
+                                      None if gate_logit is None else gate_logit.data_ptr(),
+                                      None if shared_out is None else shared_out.data_ptr(),
+                                      ops.stream_ptr(dev)),
+                   "tmoe_moe_local")
+        return idx, scores, shared_out, gate_logit
 
     def experts(self, rows, pair_row, pair_exp, options: _lib.Options | None = None):
         """This rank's routed experts on received rows (tmoe_moe_experts)."""
@@ -216,13 +303,8 @@ class ExpertParallelMoE(torch.nn.Module):
                 marks: list | None = None) -> torch.Tensor:
         xf = x.reshape(-1, self.hidden).contiguous()
         _mark(marks, "start")
-        idx, scores = ops.router_topk(xf, self.gate_weight, self.top_k)
-        _mark(marks, "router")
-        shared_out = gate_logit = None
-        if self.shared_expert is not None:
-            gate_logit = (xf.float() @ self.shared_gate.float().t()).reshape(-1).contiguous()
-            shared_out = self.shared_expert(xf).contiguous()
-        _mark(marks, "shared")
+        idx, scores, shared_out, gate_logit = self.local(xf, options)
+        _mark(marks, "local")
         mode = options.wsum_mode if options is not None else 0
         y = ep_forward(xf, idx, self.epr, lambda *a: self.experts(*a, options=options),
                        lambda ys, inv: self.combine(ys, inv, scores, shared_out, gate_logit, mode),
