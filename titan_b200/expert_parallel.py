@@ -123,13 +123,18 @@ def _exchange(t: torch.Tensor, send_counts: list[int], recv_counts: list[int], g
 
 
 def _wire(t: torch.Tensor) -> torch.Tensor:
-    """bf16 rows travel as int32 words (every backend moves those; gloo has
-    no 16-bit types)."""
-    return t.view(torch.int32) if t.dtype == torch.bfloat16 else t
+    """Rows travel as int32 words (every backend moves those; gloo has no
+    16-bit types); a row's bytes must be a multiple of 4."""
+    return t.contiguous().view(torch.int32)
+
+
+def _words(x: torch.Tensor) -> int:
+    """int32 words per row of x on the wire."""
+    return x.shape[1] * x.element_size() // 4
 
 
 def _unwire(t: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
-    return t.view(torch.bfloat16) if like.dtype == torch.bfloat16 else t
+    return t.view(like.dtype)
 
 
 def _mark(marks, name):
@@ -163,8 +168,14 @@ def ep_forward(x: torch.Tensor, idx: torch.Tensor, experts_per_rank: int, expert
     rows_out, rows_in = c[:, 0].tolist(), rc[:, 0].tolist()
     pairs_back, pairs_recv = c[:, 1].tolist(), rc[:, 1].tolist()
     plan = plan_dispatch(idx, experts_per_rank, world, n_rows=sum(rows_out))
-    rows = _unwire(_exchange(_wire(x[plan.send_token]), rows_out, rows_in, group), x)
-    ids = _exchange(plan.local_ids, rows_out, rows_in, group)
+    # one exchange per direction: each sent row carries its k local expert
+    # ids as k extra int32 words after the row's words
+    H = x.shape[1]
+    payload = torch.cat([_wire(x[plan.send_token]), plan.local_ids.view(torch.int32)], 1)
+    got = _exchange(payload, rows_out, rows_in, group)
+    nw = _words(x)
+    rows = _unwire(got[:, :nw].contiguous(), x).reshape(-1, H)
+    ids = got[:, nw:].contiguous()
     _mark(marks, "dispatch")
     pair_row, pair_exp = pairs_from_meta(ids, n_pairs=sum(pairs_recv))
     y_pairs = expert_fn(rows, pair_row, pair_exp)
