@@ -264,8 +264,9 @@ cudaError_t launch_route_plan(const int32_t* idx, int R, int E, int tile_m, int 
 // ------------------------------------------------------------ decode routing
 // Decode router (T <= kDecodeRouteMaxT tokens) in one launch.  Each CTA of 4
 // warps computes the logits of 8 rows (experts, plus the shared-expert gate as
-// row E) for every token: warps 0 and 1 hold 4 rows each, 8 lanes per row, one
-// per canonical partial, with the rows and the token vectors staged in shared
+// row E) for every token: 8 lanes per row, one per canonical partial, warps 0
+// and 1 over tokens 0-3 and warps 2 and 3 over tokens 4-7 of each pass of 8,
+// with the rows and the token vectors staged in shared
 // memory by cp.async.  The last CTA to finish (a device-wide ticket; nobody
 // waits) then routes the tokens, one warp per token (route_token: the same
 // selection and tie order as router_topk_kernel), builds the routing plan over
@@ -309,8 +310,10 @@ __global__ void __launch_bounds__(128) decode_route_kernel(
   pdl_wait();                                          // x and the workspace are ours now
   pdl_trigger();
   const int p = lane & 7, sub = lane >> 3;
-  const int rl = warp * 4 + sub, e = r0 + rl;          // warps 0-1
-  const uint4* wrow_s = wsm + (rl & 7) * nch;
+  // warps 0-1 take tokens 0..3 of a pass and warps 2-3 tokens 4..7 of the
+  // same 8 rows, so no lane carries more than 4 tokens
+  const int rl = (warp & 1) * 4 + sub, e = r0 + rl, half = warp >> 1;
+  const uint4* wrow_s = wsm + rl * nch;
   for (int t0 = 0; t0 < T; t0 += kDrTok) {
     const int nt = min(kDrTok, T - t0);
     __syncthreads();                                   // previous pass done with xsm
@@ -320,28 +323,27 @@ __global__ void __launch_bounds__(128) decode_route_kernel(
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    if (warp < 2) {
-      float acc[kDrTok];
-#pragma unroll
-      for (int i = 0; i < kDrTok; ++i) acc[i] = 0.0f;
-      // token count rounded up to 1, 2, 4 or 8: straight-line inner loops
-      // (the extra accumulators read stale rows and are dropped)
-      if (nt == 1)
-        router_dots<1>(wrow_s, xsm, nch, p, acc);
-      else if (nt == 2)
-        router_dots<2>(wrow_s, xsm, nch, p, acc);
-      else if (nt <= 4)
-        router_dots<4>(wrow_s, xsm, nch, p, acc);
+    const int nth = half == 0 ? min(nt, 4) : nt - 4;
+    if (nth > 0) {
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const uint4* xs_h = xsm + half * 4 * nch;
+      // token count rounded up to 1, 2 or 4: straight-line inner loops (the
+      // extra accumulators read stale rows and are dropped)
+      if (nth == 1)
+        router_dots<1>(wrow_s, xs_h, nch, p, acc);
+      else if (nth == 2)
+        router_dots<2>(wrow_s, xs_h, nch, p, acc);
       else
-        router_dots<8>(wrow_s, xsm, nch, p, acc);
+        router_dots<4>(wrow_s, xs_h, nch, p, acc);
 #pragma unroll
-      for (int tt = 0; tt < kDrTok; ++tt) {
+      for (int tt = 0; tt < 4; ++tt) {
         const float s8 = tree8(acc[tt]);
-        if (e < nrows && p == tt && tt < nt) {
+        if (e < nrows && p == tt && tt < nth) {
+          const int tok = t0 + half * 4 + tt;
           if (e < E)
-            logits[(size_t)(t0 + tt) * E + e] = f2bf(s8);
+            logits[(size_t)tok * E + e] = f2bf(s8);
           else
-            gate_logit[t0 + tt] = s8;
+            gate_logit[tok] = s8;
         }
       }
     }
