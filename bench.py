@@ -64,6 +64,11 @@ def parse():
                          "parallelism over the N ranks (strong scaling)")
     ap.add_argument("--ep-tokens", type=int, default=8192, help="ep: global tokens per step")
     ap.add_argument("--ep-layers", type=int, default=36, help="ep: layers per step")
+    ap.add_argument("--ep-exchange", choices=("peer", "nccl"), default="peer",
+                    help="ep: peer = NVLink stores into IPC-mapped buffers with the return "
+                         "fused into the down GEMM; nccl = two all-to-alls per layer")
+    ap.add_argument("--ep-unfused-return", action="store_true",
+                    help="ep peer: return with a copy kernel after the experts")
     return ap.parse_args()
 
 
@@ -418,8 +423,10 @@ def run_ep(args, world, rank, local):
     rank builds the same layers (same seeds) and keeps experts
     [rank*E/N, (rank+1)*E/N); it serves ep_tokens/N tokens per layer: router,
     shared expert and weighted sum on its own tokens, the routed experts of
-    the tokens of every rank that chose one of its experts (two NCCL
-    all-to-alls per layer).  value = global tokens per second."""
+    the tokens of every rank that chose one of its experts (rows stored into
+    the owners' peer-mapped buffers, expert outputs stored back by the down
+    GEMM's epilogue; --ep-exchange nccl: two all-to-alls per layer).
+    value = global tokens per second."""
     import torch
     from titan_b200 import SparseMoeBlock, _lib
     from titan_b200.expert_parallel import ExpertParallelMoE
@@ -451,13 +458,17 @@ def _run_ep(args, world, rank, local, device):
     if args.ep_tokens % world:
         raise SystemExit(f"--ep-tokens {args.ep_tokens} does not split over {world} ranks")
     T = args.ep_tokens // world
+    ex = None
+    if args.ep_exchange == "peer":
+        from titan_b200.expert_parallel import PeerExchange
+        ex = PeerExchange(T, c["H"], c["k"], device=device)
     layers = []
     for l in range(args.ep_layers):
         torch.manual_seed(4321 + l)
         blk = SparseMoeBlock(c["H"], c["E"], c["k"], c["I"], c["Is"], device=device,
                              weight_std=0.02)
         zipf_router_(blk, torch.Generator().manual_seed(777 + l))
-        layers.append(ExpertParallelMoE(blk))
+        layers.append(ExpertParallelMoE(blk, exchange=ex, fuse_return=not args.ep_unfused_return))
         del blk
     torch.cuda.empty_cache()
     gen = torch.Generator(device=device).manual_seed(9000 + rank)
@@ -480,6 +491,8 @@ def _run_ep(args, world, rank, local, device):
         for ep in layers:
             ep(x, options=opts)
 
+    torch.cuda.synchronize()
+    barrier(world)                    # ranks start together (bounded device waits)
     clk = Clocks(local).__enter__()
     for _ in range(max(args.warmup, 3)):
         step()
@@ -506,6 +519,8 @@ def _run_ep(args, world, rank, local, device):
         for (_, a0), (name, b0) in zip(marks, marks[1:]):
             phases[name] = phases.get(name, 0.0) + a0.elapsed_time(b0)
     phases = {k: round(1000 * v / len(layers), 1) for k, v in phases.items()}
+    if ex is not None:
+        ex.close()
     if rank != 0:
         return 0
     line = {
@@ -518,7 +533,11 @@ def _run_ep(args, world, rank, local, device):
                                f"experts, I=512, top-10), {args.ep_tokens} tokens per step, "
                                "Zipf(1.1) expert popularity",
                    "tokens_per_rank": T, "experts_per_rank": c["E"] // world,
-                   "parallelism": f"ep{world}", "collective": "2 NCCL all-to-alls per layer",
+                   "parallelism": f"ep{world}",
+                   "collective": ("2 NCCL all-to-alls per layer" if ex is None else
+                                  "NVLink stores into CUDA-IPC-mapped peer buffers, epoch flags; "
+                                  + ("return in a copy kernel" if args.ep_unfused_return else
+                                     "return stored by the down GEMM's epilogue")),
                    "l2": f"inputs larger than L2: {args.ep_layers} layers of weights cycled",
                    "timing": "CUDA events around the step, max over ranks"},
         "phases_us_per_layer_rank0": phases,

@@ -255,6 +255,14 @@ int tmoe_moe_experts(const tmoe_layer* layer, const uint16_t* x, int R, const in
                      const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
                      size_t ws_bytes, uint16_t* y_pairs, void* stream);
 
+/* tmoe_moe_experts storing the output row of pair p at y_rows[p] (a device
+ * array of P row addresses, in any device's memory that this one can write:
+ * the expert-parallel return writes the sources' rows over NVLink from the
+ * down GEMM's epilogue). */
+int tmoe_moe_experts_to(const tmoe_layer* layer, const uint16_t* x, int R, const int32_t* pair_row,
+                        const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
+                        size_t ws_bytes, uint16_t* const* y_rows, void* stream);
+
 /* Source side, before the exchanges: the token-local part of the layer on
  * this rank's tokens, with the kernels and arguments of tmoe_moe_forward's
  * grouped-GEMM path (language.py:74-84 and 85-90: the router Linear, softmax
@@ -276,6 +284,53 @@ int tmoe_moe_local(const tmoe_layer* layer, const uint16_t* x, int T, const tmoe
 int tmoe_moe_combine(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
                      int D, int mode, const uint16_t* shared_out, const float* gate_logit,
                      uint16_t* y, void* stream);
+
+/* ---- Expert-parallel exchanges over peer memory (no reference counterpart:
+ * the reference runs one device).  Each rank allocates one exchange buffer,
+ * maps every peer's through CUDA IPC, and passes `peers` (a DEVICE array of
+ * world pointers, peers[rank] its own buffer) to dispatch and return.
+ * Buffer layout for `world` ranks, `cap` tokens per source rank, k slots and
+ * T_max tokens of its own; offsets[0..3] (bytes) locate:
+ *   recv_x    [world][cap][H] bf16     rows sent to this rank by each source
+ *   recv_meta [world][cap][k+1] int32  their k local expert ids (-1: not
+ *                                      here), then the source token index
+ *   ret       [T_max*k][H] bf16        expert output of this rank's pairs
+ *   flags     [2][world] uint64        dispatch, return: epoch<<32 | count
+ * Epochs start at 1 and grow by one per layer call; the buffer starts zeroed.
+ * `ticket` is one zeroed device int32 per kernel kind (dispatch, return);
+ * the kernels leave it zeroed.  Waits poll with a bounded back-off; on
+ * timeout they write count -1 and tmoe_device_status returns
+ * TMOE_ERR_TIMEOUT. */
+size_t tmoe_ep_buffer_bytes(int world, int cap, int H, int k, int T_max, size_t* offsets);
+int tmoe_ep_alloc(size_t bytes, void** ptr);
+int tmoe_ep_free(void* ptr);
+/* `handle` receives / supplies a cudaIpcMemHandle_t (64 bytes). */
+int tmoe_ipc_handle(void* ptr, void* handle);
+int tmoe_ipc_open(const void* handle, void** ptr);
+int tmoe_ipc_close(void* ptr);
+/* Source side: token t's row x[t] to every rank owning one of idx[t, :]
+ * (owner = expert / experts_per_rank), at row pos[d*T + t] of that rank's
+ * recv_x block for this source; then counts[d] posted in rank d's dispatch
+ * flag.  pos and counts [world] are device int32 (the row counts per
+ * destination). */
+int tmoe_ep_dispatch(const uint16_t* x, const int32_t* idx, int T, int k, int H,
+                     int experts_per_rank, int world, int rank, const int32_t* pos,
+                     const int32_t* counts, void* const* peers, const size_t* offsets, int cap,
+                     int epoch, int32_t* ticket, void* stream);
+/* Waits for every peer's flag of `which` (0 dispatch, 1 return) at `epoch`
+ * in the buffer `own`, writing the posted counts [world] (device int32). */
+int tmoe_ep_wait(const void* own, const size_t* offsets, int which, int world, int epoch,
+                 int32_t* counts, void* stream);
+/* Owner side: output row p of y_pairs [P, H] (received row pair_row[p] =
+ * source*cap + i, slot pair_slot[p]) to the source's ret row
+ * (token*k + slot); then counts[s] (pairs returned to s) posted in each
+ * rank's return flag.  With P = 0 it only posts the flags: the rows are
+ * already there when tmoe_moe_experts_to stored them (the previous launch
+ * on the stream). */
+int tmoe_ep_return(const uint16_t* y_pairs, const int32_t* pair_row, const int32_t* pair_slot,
+                   int P, const void* own, int k, int H, int cap, int world, int rank,
+                   const int32_t* counts, void* const* peers, const size_t* offsets, int epoch,
+                   int32_t* ticket, void* stream);
 
 #ifdef __cplusplus
 }

@@ -12,7 +12,8 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from titan_b200.expert_parallel import pairs_from_meta, plan_dispatch, return_slots
+from titan_b200.expert_parallel import (_membership, pairs_from_meta, peer_pairs, plan_dispatch,
+                                        received_pairs, return_slots)
 
 H, E, K = 64, 8, 3
 
@@ -78,6 +79,57 @@ def test_pairs_and_return_slots():
     plan = plan_dispatch(idx, E // 2, 2)
     inv = return_slots(plan, 6, K)
     assert sorted(inv.tolist()) == list(range(6 * K))   # every slot exactly once
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_exchange_host_plan(world):
+    """The host side of the peer-memory transport: destination rows (pos,
+    counts) as peer_forward computes them, the metadata rows a dispatch
+    writes (simulated here), and the owner's pair list read back from a
+    buffer whose unwritten rows hold stale ids.  Every (source, token, slot)
+    must be served once, by the owner of its expert, and be returned to
+    ret row token*k + slot of its source."""
+    epr, cap = E // world, 9
+    tokens = [9, 0, 4, 7][:world]
+    g = torch.Generator().manual_seed(77)
+    meta = [torch.randint(-1, epr, (world, cap, K + 1), generator=g, dtype=torch.int32)
+            for _ in range(world)]                  # stale rows from an earlier layer
+    rows_in = [torch.zeros(world, dtype=torch.int32) for _ in range(world)]
+    idxs = []
+    for s in range(world):
+        _, idx, _ = _routing(tokens[s], seed=40 + s)
+        idxs.append(idx)
+        dest, member = _membership(idx, epr, world)
+        pos = (torch.cumsum(member.to(torch.int32), 0, dtype=torch.int32) - 1).t().contiguous()
+        counts = member.sum(0, dtype=torch.int32)
+        for t in range(tokens[s]):
+            for d in range(world):
+                if not member[t, d]:
+                    continue
+                r = int(pos[d, t])
+                assert 0 <= r < int(counts[d])
+                for j in range(K):
+                    e = int(idx[t, j])
+                    meta[d][s, r, j] = e - d * epr if e // epr == d else -1
+                meta[d][s, r, K] = t
+        for d in range(world):
+            rows_in[d][s] = counts[d]
+    served = {}
+    for d in range(world):
+        flags = received_pairs(meta[d], rows_in[d])
+        P = int(flags.sum())
+        pr, pe, ps = peer_pairs(meta[d], flags, P, torch.arange(world * cap * K, dtype=torch.int32))
+        assert pr.dtype == pe.dtype == ps.dtype == torch.int32
+        back = torch.bincount(pr // cap, minlength=world)[:world]
+        for p in range(P):
+            s, t = int(pr[p]) // cap, int(meta[d].view(-1, K + 1)[int(pr[p]), K])
+            slot = int(ps[p])
+            assert int(idxs[s][t, slot]) == d * epr + int(pe[p])
+            key = (s, t * K + slot)
+            assert key not in served
+            served[key] = d
+        assert int(back.sum()) == P
+    assert sorted(served) == [(s, i) for s in range(world) for i in range(tokens[s] * K)]
 
 
 def _worker(rank, world, port, tokens, q):

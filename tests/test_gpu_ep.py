@@ -74,6 +74,80 @@ def test_ep_single_rank_matches_block(cuda, oracle):
         dist.destroy_process_group()
 
 
+def test_ep_peer_single_rank_matches_block(cuda, oracle):
+    """The peer-memory transport on one rank: the dispatch and return
+    kernels write through the rank's own buffer and the flags; two layers
+    share one exchange and run in turn, fused and unfused returns, and an
+    empty call; every output bit-identical to the single-GPU block."""
+    import torch.distributed as dist
+    from titan_b200.expert_parallel import ExpertParallelMoE, PeerExchange
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(_free_port())
+    dist.init_process_group("nccl", rank=0, world_size=1)
+    try:
+        ex = PeerExchange(160, SHAPE["H"], SHAPE["k"])
+        L0, blk0 = _blocks(oracle, cuda, SHAPE0, 33)
+        L, blk = _blocks(oracle, cuda, SHAPE, 31)
+        for fuse in (True, False):
+            eps = (ExpertParallelMoE(blk0, exchange=ex, fuse_return=fuse),
+                   ExpertParallelMoE(blk, exchange=ex, fuse_return=fuse))
+            for T in (150, 7, 160):
+                x = oracle.make_x(T, SHAPE["H"], seed=T + fuse)
+                for ep, b in zip(eps, (blk0, blk)):
+                    y = ep(bf(x), options=_opts(1))
+                    yb = b(bf(x), options=_opts(1))
+                    assert torch.equal(y.view(torch.int16), yb.view(torch.int16)), (fuse, T)
+            y = eps[1](bf(oracle.make_x(0, SHAPE["H"], seed=1)), options=_opts(1))
+            assert y.shape == (0, SHAPE["H"])
+        x = oracle.make_x(150, SHAPE["H"], seed=5)
+        y = ExpertParallelMoE(blk, exchange=ex)(bf(x), options=_opts(1))
+        torch.cuda.synchronize()
+        _compare(oracle, L, x, nbf(y))
+        from titan_b200 import _lib
+        assert _lib.load().tmoe_device_status() == 0
+        ex.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _timeout_child(q):
+    import ctypes as C
+    try:
+        from titan_b200 import _lib
+        lib = _lib.load()
+        torch.cuda.set_device(0)
+        world, offs = 2, (C.c_size_t * 4)()
+        nb = lib.tmoe_ep_buffer_bytes(world, 8, 1024, 8, 8, offs)
+        ptr = C.c_void_p()
+        _lib.check(lib.tmoe_ep_alloc(nb, C.byref(ptr)))
+        counts = torch.full((world,), 7, dtype=torch.int32, device="cuda")
+        # epoch 5: nothing ever posts it, so both waits must give up
+        _lib.check(lib.tmoe_ep_wait(ptr, offs, 0, world, 5, counts.data_ptr(), None))
+        torch.cuda.synchronize()
+        got = counts.tolist()
+        status = int(lib.tmoe_device_status())
+        _lib.check(lib.tmoe_ep_free(ptr))
+        q.put((got, status, None))
+    except Exception as exc:
+        q.put((None, None, repr(exc)))
+
+
+def test_ep_wait_gives_up_and_reports(cuda):
+    """A flag that nothing sets: the wait kernel gives up after its bounded
+    time, writes count -1, the context stays usable, and tmoe_device_status
+    reports TMOE_ERR_TIMEOUT (5).  In a child process: the error is sticky
+    for the life of the library."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_timeout_child, args=(q,))
+    p.start()
+    got, status, err = q.get(timeout=300)
+    p.join(timeout=60)
+    assert err is None, err
+    assert got == [-1, -1]
+    assert status == 5
+
+
 def _worker(rank, world, port, layer_arrays, T, q):
     import torch.distributed as dist
     sys_path = os.path.dirname(os.path.abspath(__file__))
@@ -83,7 +157,7 @@ def _worker(rank, world, port, layer_arrays, T, q):
     from gpu_util import bf, load_block, nbf
     from oracle import oracle
     from titan_b200 import SparseMoeBlock
-    from titan_b200.expert_parallel import ExpertParallelMoE
+    from titan_b200.expert_parallel import ExpertParallelMoE, PeerExchange
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -92,16 +166,34 @@ def _worker(rank, world, port, layer_arrays, T, q):
         dev = torch.device("cuda", rank)
         x = oracle.make_x(T, SHAPE["H"], seed=500 + rank)
         out = {}
+        ex = PeerExchange(128, SHAPE["H"], SHAPE["k"]) if layer_arrays == "peer" else None
+        refs = []
         for shape, seed, tag in ((SHAPE0, 33, "plain"), (SHAPE, 31, "shared")):
             L = oracle.make_layer(seed=seed, **shape)
             blk = SparseMoeBlock(shape["H"], shape["E"], shape["k"], shape["I"], shape["Is"],
                                  device=dev, init=False)
             load_block(blk, L)
-            ep = ExpertParallelMoE(blk)
-            y = nbf(ep(bf(x, dev=dev), options=_opts(1)))
             yb = nbf(blk(bf(x, dev=dev), options=_opts(1)))
             ry, _, _, ops = oracle.moe_prefill(L, x, int8_mode=3, parts=True)
-            out[tag] = (y, yb, ry, ops)
+            refs.append((tag, blk, yb, ry, ops))
+        # the oracle's CPU time differs between ranks: line the ranks up
+        # before the first exchange so no device wait runs long
+        dist.barrier()
+        for tag, blk, yb, ry, ops in refs:
+            if ex is None:
+                ep = ExpertParallelMoE(blk)
+                y = nbf(ep(bf(x, dev=dev), options=_opts(1)))
+                out[tag] = (y, yb, ry, ops)
+                continue
+            for fuse in (True, False):
+                ep = ExpertParallelMoE(blk, exchange=ex, fuse_return=fuse)
+                for _ in range(2):                     # the exchange reused call after call
+                    y = nbf(ep(bf(x, dev=dev), options=_opts(1)))
+                    out[f"{tag}_{fuse}"] = (y, yb, ry, ops)
+        if ex is not None:
+            from titan_b200 import _lib
+            out["status"] = int(_lib.load().tmoe_device_status())
+            ex.close()
         q.put((rank, out, None, None))
     except Exception as exc:
         q.put((rank, repr(exc), None, None))
@@ -129,3 +221,28 @@ def test_ep_two_gpus_nccl(oracle):
         y, yb, ry, ops = out["shared"]
         assert np.array_equal(y, yb), f"rank {rank}: EP with a shared expert differs from the block"
         assert_bf16_close(y, ry, what=f"EP rank {rank}", operands=ops, operand_ulps=4)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_gpus_peer_memory(oracle):
+    """The peer-memory transport over two GPUs (CUDA IPC mappings, NVLink
+    stores, epoch flags): bit-identical to the single-GPU block on each
+    rank's tokens, fused and unfused returns, ranks with unequal tokens."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, "peer", (120, 40)[r], q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, out, _, _ in sorted(res, key=lambda r: r[0]):
+        assert not isinstance(out, str), f"rank {rank}: {out}"
+        assert out.pop("status") == 0, f"rank {rank}: a device wait timed out"
+        for tag, (y, yb, ry, ops) in out.items():
+            assert np.array_equal(y, yb), f"rank {rank} {tag}: peer EP differs from the block"
+            assert_bf16_close(y, ry, what=f"peer EP rank {rank} {tag}", operands=ops,
+                              operand_ulps=4)

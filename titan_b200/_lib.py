@@ -110,9 +110,20 @@ _SIGS = {
     "tmoe_moe_experts_workspace_size": ([C.POINTER(Layer), I32, I32, C.POINTER(Options)], SZ),
     "tmoe_moe_experts": ([C.POINTER(Layer), P, I32, P, P, I32, C.POINTER(Options), P, SZ, P, P],
                          I32),
+    "tmoe_moe_experts_to": ([C.POINTER(Layer), P, I32, P, P, I32, C.POINTER(Options), P, SZ, P,
+                             P], I32),
     "tmoe_moe_combine": ([P, P, P, I32, I32, I32, I32, P, P, P, P], I32),
     "tmoe_moe_local_workspace_size": ([C.POINTER(Layer), I32, C.POINTER(Options)], SZ),
     "tmoe_moe_local": ([C.POINTER(Layer), P, I32, C.POINTER(Options), P, SZ, P, P, P, P, P], I32),
+    "tmoe_ep_buffer_bytes": ([I32, I32, I32, I32, I32, P], SZ),
+    "tmoe_ep_alloc": ([SZ, P], I32),
+    "tmoe_ep_free": ([P], I32),
+    "tmoe_ipc_handle": ([P, P], I32),
+    "tmoe_ipc_open": ([P, P], I32),
+    "tmoe_ipc_close": ([P], I32),
+    "tmoe_ep_dispatch": ([P, P, I32, I32, I32, I32, I32, I32, P, P, P, P, I32, I32, P, P], I32),
+    "tmoe_ep_wait": ([P, P, I32, I32, I32, P, P], I32),
+    "tmoe_ep_return": ([P, P, P, I32, P, I32, I32, I32, I32, I32, P, P, P, I32, P, P], I32),
 }
 
 EXPORTED = tuple(_SIGS)

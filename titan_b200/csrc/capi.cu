@@ -4,6 +4,7 @@
 // per-thread message.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "../../include/titan_moe.h"
@@ -81,6 +82,8 @@ void tmoe_set_stage_hook(tmoe_stage_fn fn, void* ctx) {
 int tmoe_device_status(void) {
   cudaDeviceSynchronize();
   if (tc05_error_flag()) return fail(TMOE_ERR_TIMEOUT, "a tcgen05 kernel's bounded wait timed out");
+  if (ep_error_flag())
+    return fail(TMOE_ERR_TIMEOUT, "an expert-parallel exchange wait timed out");
   if (layer_error_flag())
     return fail(TMOE_ERR_TIMEOUT, "a grid barrier of the single-launch decode layer timed out");
   return TMOE_OK;
@@ -1004,9 +1007,14 @@ size_t tmoe_moe_experts_workspace_size(const tmoe_layer* L, int R, int npairs,
   return carve_experts(c, L, R, npairs, opt, nullptr);
 }
 
-int tmoe_moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pair_row,
-                     const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
-                     size_t ws_bytes, uint16_t* y_pairs, void* stream) {
+}  // extern "C"
+
+namespace {
+// The owner side; the output row of pair p goes to y_pairs[p] or, when
+// y_ptr is set, to y_ptr[p].
+int moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pair_row,
+                const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
+                size_t ws_bytes, uint16_t* y_pairs, uint16_t* const* y_ptr, void* stream) {
   if (!L || R < 0 || npairs < 0) return fail(TMOE_ERR_INVALID, "tmoe_moe_experts: bad arguments");
   const int H = L->hidden, E = L->num_experts, I = L->moe_inter, G = H / 64;
   if (!L->gate_up_w || !L->gate_up_st || !L->gate_up_bt || !L->down_w || !L->down_st ||
@@ -1015,7 +1023,7 @@ int tmoe_moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_
   if (H <= 0 || H % 128 || I <= 0 || I % 64 || E <= 0 || E > 1024)
     return fail(TMOE_ERR_UNSUPPORTED, "tmoe_moe_experts: need H %% 128 == 0, I %% 64 == 0, E <= 1024");
   if (R == 0 || npairs == 0) return TMOE_OK;
-  if (!x || !y_pairs || !pair_row || !pair_exp)
+  if (!x || (!y_pairs && !y_ptr) || !pair_row || !pair_exp)
     return fail(TMOE_ERR_INVALID, "tmoe_moe_experts: null pointer");
   const size_t need = tmoe_moe_experts_workspace_size(L, R, npairs, opt);
   if (!ws || ws_bytes < need)
@@ -1090,8 +1098,27 @@ int tmoe_moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_
   dn.N = H;
   dn.Y = y_pairs;
   dn.y_rows = b.order;         // stored back in pair order
+  dn.y_ptr = y_ptr;
   TMOE_TRY(gemm(d8, kEpiStore, dn), "gemm_down");
   return TMOE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int tmoe_moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pair_row,
+                     const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
+                     size_t ws_bytes, uint16_t* y_pairs, void* stream) {
+  return moe_experts(L, x, R, pair_row, pair_exp, npairs, opt, ws, ws_bytes, y_pairs, nullptr,
+                     stream);
+}
+
+int tmoe_moe_experts_to(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pair_row,
+                        const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
+                        size_t ws_bytes, uint16_t* const* y_rows, void* stream) {
+  if (npairs > 0 && !y_rows) return fail(TMOE_ERR_INVALID, "tmoe_moe_experts_to: null y_rows");
+  return moe_experts(L, x, R, pair_row, pair_exp, npairs, opt, ws, ws_bytes, nullptr, y_rows,
+                     stream);
 }
 
 // The source side: the block's weighted sum (clone or fast mode) over every
@@ -1193,6 +1220,129 @@ int tmoe_moe_local(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_opt
   sd.N = H;
   sd.Y = shared_out;
   TMOE_TRY(gemm(kEpiStore, sd, st), "gemm_shared_down");
+  return TMOE_OK;
+}
+
+// ------------------------------------------- expert-parallel peer exchanges
+
+size_t tmoe_ep_buffer_bytes(int world, int cap, int H, int k, int T_max, size_t* offsets) {
+  size_t off[4];
+  if (world <= 0 || cap < 0 || H <= 0 || k <= 0 || T_max < 0) return 0;
+  const size_t n = ep_layout(world, cap, H, k, T_max, off);
+  if (offsets)
+    for (int i = 0; i < 4; ++i) offsets[i] = off[i];
+  return n;
+}
+
+int tmoe_ep_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(TMOE_ERR_INVALID, "tmoe_ep_alloc: bad arguments");
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  if (e != cudaSuccess) return fail(TMOE_ERR_CUDA, "tmoe_ep_alloc: %s", cudaGetErrorString(e));
+  return TMOE_OK;
+}
+
+int tmoe_ep_free(void* ptr) {
+  if (ptr) {
+    cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) return fail(TMOE_ERR_CUDA, "tmoe_ep_free: %s", cudaGetErrorString(e));
+  }
+  return TMOE_OK;
+}
+
+int tmoe_ipc_handle(void* ptr, void* handle) {
+  if (!ptr || !handle) return fail(TMOE_ERR_INVALID, "tmoe_ipc_handle: null argument");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return fail(TMOE_ERR_CUDA, "tmoe_ipc_handle: %s", cudaGetErrorString(e));
+  memcpy(handle, &h, sizeof(h));
+  return TMOE_OK;
+}
+
+int tmoe_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return fail(TMOE_ERR_INVALID, "tmoe_ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(TMOE_ERR_CUDA, "tmoe_ipc_open: %s", cudaGetErrorString(e));
+  return TMOE_OK;
+}
+
+int tmoe_ipc_close(void* ptr) {
+  if (ptr) {
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) return fail(TMOE_ERR_CUDA, "tmoe_ipc_close: %s", cudaGetErrorString(e));
+  }
+  return TMOE_OK;
+}
+
+int tmoe_ep_dispatch(const uint16_t* x, const int32_t* idx, int T, int k, int H,
+                     int experts_per_rank, int world, int rank, const int32_t* pos,
+                     const int32_t* counts, void* const* peers, const size_t* offsets, int cap,
+                     int epoch, int32_t* ticket, void* stream) {
+  if (T < 0 || k <= 0 || k >= 128 || H <= 0 || H % 8 || experts_per_rank <= 0 || world <= 0 ||
+      world > 32 || rank < 0 || rank >= world || T > cap || !counts || !peers || !offsets ||
+      !ticket || (T > 0 && (!x || !idx || !pos)))
+    return fail(TMOE_ERR_INVALID, "tmoe_ep_dispatch: bad arguments");
+  EpDispatchArgs a{};
+  a.x = x;
+  a.idx = idx;
+  a.pos = pos;
+  a.counts = counts;
+  a.peer = peers;
+  a.off_x = offsets[0];
+  a.off_meta = offsets[1];
+  a.off_flags = offsets[3];
+  a.ticket = ticket;
+  a.T = T;
+  a.k = k;
+  a.H = H;
+  a.epr = experts_per_rank;
+  a.world = world;
+  a.rank = rank;
+  a.cap = cap;
+  a.epoch = epoch;
+  TMOE_TRY(launch_ep_dispatch(a, S(stream)), "ep_dispatch");
+  return TMOE_OK;
+}
+
+int tmoe_ep_wait(const void* own, const size_t* offsets, int which, int world, int epoch,
+                 int32_t* counts, void* stream) {
+  if (!own || !offsets || (which != 0 && which != 1) || world <= 0 || world > 32 || !counts)
+    return fail(TMOE_ERR_INVALID, "tmoe_ep_wait: bad arguments");
+  const unsigned long long* flags = reinterpret_cast<const unsigned long long*>(
+      static_cast<const uint8_t*>(own) + offsets[3]) + (size_t)which * world;
+  TMOE_TRY(launch_ep_wait(flags, world, epoch, counts, S(stream)), "ep_wait");
+  return TMOE_OK;
+}
+
+int tmoe_ep_return(const uint16_t* y_pairs, const int32_t* pair_row, const int32_t* pair_slot,
+                   int P, const void* own, int k, int H, int cap, int world, int rank,
+                   const int32_t* counts, void* const* peers, const size_t* offsets, int epoch,
+                   int32_t* ticket, void* stream) {
+  if (P < 0 || !own || k <= 0 || H <= 0 || H % 8 || cap <= 0 || world <= 0 || world > 32 ||
+      rank < 0 || rank >= world || !counts || !peers || !offsets || !ticket ||
+      (P > 0 && (!y_pairs || !pair_row || !pair_slot)))
+    return fail(TMOE_ERR_INVALID, "tmoe_ep_return: bad arguments");
+  EpReturnArgs a{};
+  a.y_pairs = y_pairs;
+  a.pair_row = pair_row;
+  a.pair_slot = pair_slot;
+  a.meta = reinterpret_cast<const int32_t*>(static_cast<const uint8_t*>(own) + offsets[1]);
+  a.counts = counts;
+  a.peer = peers;
+  a.off_ret = offsets[2];
+  a.off_flags = offsets[3];
+  a.ticket = ticket;
+  a.P = P;
+  a.k = k;
+  a.H = H;
+  a.world = world;
+  a.rank = rank;
+  a.cap = cap;
+  a.epoch = epoch;
+  TMOE_TRY(launch_ep_return(a, S(stream)), "ep_return");
   return TMOE_OK;
 }
 

@@ -1,0 +1,195 @@
+// Expert-parallel exchanges over NVLink peer memory (no reference
+// counterpart: the reference runs one device).
+//
+// Each rank owns one device allocation (tmoe_ep_alloc) that the other ranks
+// map through CUDA IPC.  Layout of rank d's allocation, for W ranks, a
+// capacity of `cap` tokens per source rank, H hidden, k slots, T_max tokens
+// of its own:
+//   recv_x    [W][cap][H] bf16       rows sent to d by each source rank
+//   recv_meta [W][cap][k + 1] int32  their k local expert ids (-1: not on d),
+//                                    then the source's token index
+//   ret       [T_max * k][H] bf16    expert output of d's (token, slot) pairs,
+//                                    written by the owner of each slot
+//   flags     [2][W] uint64          dispatch and return flags, one per peer:
+//                                    epoch << 32 | count
+// Dispatch: a source writes each of its token rows once to every rank that
+// owns one of the token's experts (deduplicated), then posts (epoch, rows) in
+// that rank's dispatch flag.  Return: an owner writes every served pair's
+// output straight into the source's ret row (token, slot), then posts
+// (epoch, pairs) in the source's return flag.  Writes are plain stores to
+// peer memory; the flag of a kernel is posted by its last CTA after a
+// system-scope fence and a ticket, so a reader that sees the flag sees the
+// data.  Waits are bounded (4 s of device time): on timeout the kernel
+// records an error that tmoe_device_status reports and returns.
+//
+// Reuse across layers needs no double buffer: a source dispatches layer L+1
+// only after its weighted sum of layer L, which waited for every owner's
+// return of layer L, and an owner returns only after its experts consumed
+// the rows of layer L.
+#include "common.cuh"
+#include "tmoe_internal.h"
+
+namespace tmoe {
+
+__device__ int g_ep_error = 0;
+
+namespace {
+
+// A wait gives up after kEpLimitNs of device time (%globaltimer), or after
+// kEpSpin polls should the timer not advance; polls past the first kEpFast
+// back off by 256 ns.
+constexpr unsigned long long kEpLimitNs = 4000000000ull;
+constexpr uint32_t kEpSpin = 1u << 26;
+constexpr uint32_t kEpFast = 1u << 10;
+
+TMOE_DEV unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+TMOE_DEV void st_release_sys64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+TMOE_DEV unsigned long long ld_acquire_sys64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One CTA per token: its row (and metadata) to every owning rank.
+__global__ void __launch_bounds__(128) ep_dispatch_kernel(EpDispatchArgs a) {
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const int W = a.world, k = a.k, H = a.H;
+  __shared__ int s_last;
+  const int32_t* ids = a.idx + (size_t)(t < a.T ? t : 0) * k;
+  for (int d = 0; d < W && t < a.T; ++d) {     // a CTA past the tokens only posts flags
+    bool mine = false;
+    for (int j = 0; j < k; ++j) mine |= ids[j] / a.epr == d;
+    if (!mine) continue;
+    const int pos = a.pos[(size_t)d * a.T + t];        // this token's row among those sent to d
+    uint8_t* base = static_cast<uint8_t*>(a.peer[d]);
+    const size_t row = (size_t)a.rank * a.cap + pos;
+    uint4* dst = reinterpret_cast<uint4*>(base + a.off_x + row * H * 2);
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)t * H);
+    for (int i = tid; i < H / 8; i += 128) dst[i] = src[i];
+    int32_t* meta = reinterpret_cast<int32_t*>(base + a.off_meta) + row * (k + 1);
+    if (tid < k) {
+      const int e = ids[tid];
+      meta[tid] = e / a.epr == d ? e - d * a.epr : -1;
+    } else if (tid == k) {
+      meta[k] = t;
+    }
+  }
+  __threadfence_system();     // every writer's stores before the CTA's ticket
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();
+    s_last = ticket_acq_rel(a.ticket) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  if (tid < W) {
+    __threadfence_system();
+    unsigned long long* flags = reinterpret_cast<unsigned long long*>(
+        static_cast<uint8_t*>(a.peer[tid]) + a.off_flags);
+    st_release_sys64(flags + a.rank,
+                     ((unsigned long long)(uint32_t)a.epoch << 32) | (uint32_t)a.counts[tid]);
+  }
+  if (tid == 0) *a.ticket = 0;
+}
+
+// One thread per peer: wait for this epoch's flag; counts[s] = its count,
+// or -1 when the wait gave up.
+__global__ void ep_wait_kernel(const unsigned long long* flags, int W, int epoch, int32_t* counts) {
+  const int s = threadIdx.x;
+  if (s >= W) return;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 0; i < kEpSpin; ++i) {
+    const unsigned long long v = ld_acquire_sys64(flags + s);
+    if ((int)(v >> 32) == epoch) {
+      counts[s] = (int)(v & 0xffffffffu);
+      return;
+    }
+    if (i >= kEpFast) {
+      __nanosleep(256);
+      if (global_ns() - t0 > kEpLimitNs) break;
+    }
+  }
+  counts[s] = -1;
+  atomicExch(&g_ep_error, 1);
+}
+
+// One CTA per served pair: its output row to the source's ret row.  With
+// P = 0 it only posts the flags: the rows were stored straight into the
+// sources' ret rows by the down GEMM's epilogue (GemmParams::y_ptr), whose
+// launch precedes this one on the stream.
+__global__ void __launch_bounds__(128) ep_return_kernel(EpReturnArgs a) {
+  const int p = blockIdx.x, tid = threadIdx.x;
+  const int k = a.k, H = a.H;
+  __shared__ int s_last;
+  if (p < a.P) {                                 // a CTA past the pairs only posts flags
+    const int row = a.pair_row[p];               // received row: source * cap + i
+    const int src = row / a.cap;
+    const int32_t* meta = a.meta + (size_t)row * (k + 1);
+    const int slot = a.pair_slot[p], t = meta[k];
+    uint8_t* base = static_cast<uint8_t*>(a.peer[src]);
+    uint4* dst = reinterpret_cast<uint4*>(base + a.off_ret + ((size_t)t * k + slot) * H * 2);
+    const uint4* y = reinterpret_cast<const uint4*>(a.y_pairs + (size_t)p * H);
+    for (int i = tid; i < H / 8; i += 128) dst[i] = y[i];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();
+    s_last = ticket_acq_rel(a.ticket) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  if (tid < a.world) {
+    __threadfence_system();
+    unsigned long long* flags = reinterpret_cast<unsigned long long*>(
+        static_cast<uint8_t*>(a.peer[tid]) + a.off_flags);
+    st_release_sys64(flags + a.world + a.rank,
+                     ((unsigned long long)(uint32_t)a.epoch << 32) | (uint32_t)a.counts[tid]);
+  }
+  if (tid == 0) *a.ticket = 0;
+}
+
+}  // namespace
+
+cudaError_t launch_ep_dispatch(const EpDispatchArgs& a, cudaStream_t s) {
+  ep_dispatch_kernel<<<a.T > 0 ? a.T : 1, 128, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_wait(const unsigned long long* flags, int W, int epoch, int32_t* counts,
+                           cudaStream_t s) {
+  ep_wait_kernel<<<1, 32, 0, s>>>(flags, W, epoch, counts);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_return(const EpReturnArgs& a, cudaStream_t s) {
+  ep_return_kernel<<<a.P > 0 ? a.P : 1, 128, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ C ABI
+
+size_t ep_layout(int world, int cap, int H, int k, int T_max, size_t* off) {
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  size_t o = 0;
+  off[0] = o; o = up(o + (size_t)world * cap * H * 2);              // recv_x
+  off[1] = o; o = up(o + (size_t)world * cap * (k + 1) * 4);        // recv_meta
+  off[2] = o; o = up(o + (size_t)T_max * k * H * 2);               // ret
+  off[3] = o; o = up(o + (size_t)2 * world * 8);                    // flags
+  return o;
+}
+
+int ep_error_flag() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_ep_error, sizeof(int));
+  return v;
+}
+
+}  // namespace tmoe

@@ -302,7 +302,8 @@ __global__ void __launch_bounds__(256) gemm_grouped_kernel(GemmParams P) {
           const uint32_t v = (uint32_t)f2bf(acc[i][j][2 * hr]) |
                              ((uint32_t)f2bf(acc[i][j][2 * hr + 1]) << 16);
           const int orow = P.y_rows ? P.y_rows[row] : row;
-          *reinterpret_cast<uint32_t*>(P.Y + (size_t)orow * P.N + col) = v;
+          uint16_t* yrow = P.y_ptr ? P.y_ptr[orow] : P.Y + (size_t)orow * P.N;
+          *reinterpret_cast<uint32_t*>(yrow + col) = v;
         }
       }
   } else {

@@ -487,7 +487,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
     if constexpr (EPI == kEpiStore) {
       if (live) {
         const int orow = P.y_rows ? P.y_rows[row] : row;
-        uint4* dst = reinterpret_cast<uint4*>(P.Y + (size_t)orow * P.N + n0 + 64 * half);
+        uint16_t* yrow = P.y_ptr ? P.y_ptr[orow] : P.Y + (size_t)orow * P.N;
+        uint4* dst = reinterpret_cast<uint4*>(yrow + n0 + 64 * half);
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           uint4 pk;

@@ -43,6 +43,7 @@ struct GemmParams {
   int K, N;             // N = weight rows (2I for the SwiGLU epilogues)
   uint16_t* Y;          // store: bf16 [R][N]
   const int32_t* y_rows;  // optional: sorted row r is stored at Y row y_rows[r]
+  uint16_t* const* y_ptr;  // optional: Y row i is stored at y_ptr[i] (any device's memory)
   int8_t* hq;           // SwiGLU-Q8: int8 h [Rpad][N/2]
   float* hsc;           // [N/128][Rpad_h]
   float* hrs;           // [N/128][Rpad_h]
@@ -152,6 +153,35 @@ int decode_layer_ctas();
 size_t decode_layer_smem(int T, int H, int E, int k, int I, int Is, int nct, int ns);
 cudaError_t launch_decode_layer(const LayerArgs& a, int ns, cudaStream_t s);
 int layer_error_flag();
+
+// Expert-parallel exchanges over peer memory (ep_p2p.cu).
+struct EpDispatchArgs {
+  const uint16_t* x;        // [T][H] bf16
+  const int32_t* idx;       // [T][k] global expert ids
+  const int32_t* pos;       // [W][T] row of token t among those sent to rank d
+  const int32_t* counts;    // [W] rows sent to each rank
+  void* const* peer;        // [W] each rank's exchange allocation, mapped here
+  size_t off_x, off_meta, off_flags;
+  int32_t* ticket;          // zero between launches
+  int T, k, H, epr, world, rank, cap, epoch;
+};
+struct EpReturnArgs {
+  const uint16_t* y_pairs;  // [P][H] bf16
+  const int32_t* pair_row;  // [P] received row (source * cap + i)
+  const int32_t* pair_slot; // [P] slot j of the pair
+  const int32_t* meta;      // this rank's recv_meta [W * cap][k + 1]
+  const int32_t* counts;    // [W] pairs returned to each source
+  void* const* peer;
+  size_t off_ret, off_flags;
+  int32_t* ticket;
+  int P, k, H, world, rank, cap, epoch;
+};
+cudaError_t launch_ep_dispatch(const EpDispatchArgs& a, cudaStream_t s);
+cudaError_t launch_ep_wait(const unsigned long long* flags, int W, int epoch, int32_t* counts,
+                           cudaStream_t s);
+cudaError_t launch_ep_return(const EpReturnArgs& a, cudaStream_t s);
+size_t ep_layout(int world, int cap, int H, int k, int T_max, size_t* off);
+int ep_error_flag();
 cudaError_t launch_to_f16p(const uint16_t* x, long long n, uint16_t* y, cudaStream_t s);
 cudaError_t launch_prep_x(const uint16_t* x, int R, int K, uint16_t* x16p, float* xsum,
                           long long sum_sm, long long sum_sg, cudaStream_t s);

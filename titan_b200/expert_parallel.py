@@ -19,15 +19,29 @@ sigmoid-gated shared expert) over the k outputs of every token, so the
 expert-parallel layer reproduces the single-device layer bit for bit wherever
 the experts' arithmetic is fixed-order (the int8 path).
 
-Plumbing is ``torch.distributed`` (NCCL on GPUs, gloo in the CPU tests); the
-expert arithmetic is ``tmoe_moe_experts`` and the final sum
+Two transports carry the exchanges:
+
+  NCCL      ``torch.distributed`` all-to-alls (NCCL on GPUs, gloo in the CPU
+            tests).  The dispatch plan is computed on the device with tensor
+            ops; the host reads only the exchanged counts, which the
+            variable-size all-to-all needs.
+  peer      (:class:`PeerExchange`) every rank's receive buffers are mapped
+            into every other rank through CUDA IPC and the library's kernels
+            write into them over NVLink: tmoe_ep_dispatch stores each token
+            row straight into its owners' receive rows, and the owners' down
+            GEMM (tmoe_moe_experts_to) stores every expert output row straight
+            into the source's return row from its epilogue, so the return
+            exchange is part of the expert kernel.  Epoch-tagged flags
+            (tmoe_ep_wait) replace the collectives; the host reads one pair
+            count per layer.
+
+The expert arithmetic is ``tmoe_moe_experts`` and the final sum
 ``tmoe_moe_combine`` from libtitan_moe.so, and the token-local part (router,
-top-k, shared expert) ``tmoe_moe_local`` with the block's own kernels.  The dispatch plan is computed on
-the device with tensor ops; the host reads only the exchanged counts, which
-the variable-size all-to-all needs.
+top-k, shared expert) ``tmoe_moe_local`` with the block's own kernels.
 """
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass
 from typing import Callable
 
@@ -37,7 +51,7 @@ import torch.distributed as dist
 from . import _lib, ops
 
 __all__ = ["DispatchPlan", "plan_dispatch", "pairs_from_meta", "return_slots",
-           "ExpertParallelMoE", "ep_forward"]
+           "ExpertParallelMoE", "PeerExchange", "ep_forward"]
 
 
 @dataclass
@@ -187,14 +201,204 @@ def ep_forward(x: torch.Tensor, idx: torch.Tensor, experts_per_rank: int, expert
     return y
 
 
+class _DeviceArray:
+    """Raw device memory seen by torch.as_tensor (CUDA array interface)."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+def _view(ptr: int, shape: tuple, dtype: torch.dtype, device) -> torch.Tensor:
+    code = {torch.int32: "<i4", torch.int16: "<i2"}[dtype]
+    return torch.as_tensor(_DeviceArray(ptr, shape, code), device=device)
+
+
+class PeerExchange:
+    """The expert-parallel exchange of one rank over NVLink peer memory.
+
+    One device allocation per rank (tmoe_ep_alloc; layout in
+    include/titan_moe.h) holds the rows other ranks send here, their expert
+    ids and token indices, the returned expert outputs of this rank's own
+    tokens, and the epoch-tagged flags.  Every rank maps every other rank's
+    allocation through CUDA IPC (handles swapped with one
+    ``all_gather_object``), so the library's kernels store into peers
+    directly.  One exchange serves any number of layers in turn: the layers
+    of a step run one after another, and each call advances the epoch.
+    ``cap`` is the most tokens a rank passes to one layer call.  Creating
+    and :meth:`close` are collective over ``group``."""
+
+    def __init__(self, cap: int, hidden: int, top_k: int, group=None, device=None):
+        self.group = group
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.cap, self.hidden, self.top_k = int(cap), int(hidden), int(top_k)
+        self.device = torch.device(device) if device is not None else \
+            torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        self.offsets = (C.c_size_t * 4)()
+        nbytes = lib.tmoe_ep_buffer_bytes(self.world, self.cap, self.hidden, self.top_k,
+                                          self.cap, self.offsets)
+        if nbytes == 0:
+            raise _lib.InvalidArgument(f"bad exchange shape: cap={cap}, H={hidden}, k={top_k}")
+        self.nbytes = int(nbytes)
+        ptr = C.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.tmoe_ep_alloc(self.nbytes, C.byref(ptr)), "tmoe_ep_alloc")
+        self.ptr = ptr.value
+        handle = C.create_string_buffer(64)
+        if self.world > 1:
+            _lib.check(lib.tmoe_ipc_handle(self.ptr, handle), "tmoe_ipc_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened = []
+        peers = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    peers.append(self.ptr)
+                    continue
+                p = C.c_void_p()
+                _lib.check(lib.tmoe_ipc_open(C.create_string_buffer(h, 64), C.byref(p)),
+                           "tmoe_ipc_open")
+                self._opened.append(p.value)
+                peers.append(p.value)
+        self.peers = torch.tensor(peers, dtype=torch.int64, device=self.device)
+        self.tickets = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+        o = [int(v) for v in self.offsets]
+        W, k, H = self.world, self.top_k, self.hidden
+        self.rows = _view(self.ptr + o[0], (W * self.cap, H), torch.int16,
+                          self.device).view(torch.bfloat16)
+        self.meta = _view(self.ptr + o[1], (W, self.cap, k + 1), torch.int32, self.device)
+        self.ret = _view(self.ptr + o[2], (self.cap * k, H), torch.int16,
+                         self.device).view(torch.bfloat16)
+        self.ret_offset = o[2]
+        self._pending = None            # the last layer's return counts (-1: a wait gave up)
+        self._ar = {}
+
+    def arange(self, n: int) -> torch.Tensor:
+        a = self._ar.get(n)
+        if a is None:
+            a = self._ar[n] = torch.arange(n, dtype=torch.int32, device=self.device)
+        return a
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, wait for every rank to do the same, and
+        free this rank's buffer (collective)."""
+        if self.ptr is None:
+            return
+        torch.cuda.synchronize(self.device)
+        lib = _lib.load()
+        for p in self._opened:
+            _lib.check(lib.tmoe_ipc_close(p), "tmoe_ipc_close")
+        self._opened = []
+        dist.barrier(group=self.group)
+        self.rows = self.meta = self.ret = None
+        _lib.check(lib.tmoe_ep_free(self.ptr), "tmoe_ep_free")
+        self.ptr = None
+
+
+def received_pairs(meta: torch.Tensor, rows_in: torch.Tensor) -> torch.Tensor:
+    """Which (received row, slot) entries of a PeerExchange's metadata
+    meta [W, cap, k+1] are pairs this rank serves: the row was written this
+    layer (index < rows_in[source]) and the slot's expert is here (id >= 0).
+    Flat bool [W*cap*k]."""
+    W, cap, k1 = meta.shape
+    live = torch.arange(cap, dtype=torch.int32, device=meta.device)[None, :] < rows_in[:, None]
+    return ((meta[..., :k1 - 1] >= 0) & live[..., None]).reshape(-1)
+
+
+def peer_pairs(meta: torch.Tensor, flags: torch.Tensor, n_pairs: int, flat: torch.Tensor):
+    """The served pairs of received_pairs(), row-major: received row
+    (source * cap + i), local expert and slot of each, int32; flat =
+    arange(W*cap*k) int32."""
+    k = meta.shape[2] - 1
+    pair_row = _compact(flags, n_pairs, flat // k)
+    pair_exp = _compact(flags, n_pairs, meta[..., :k].reshape(-1))
+    pair_slot = _compact(flags, n_pairs, flat % k)
+    return pair_row, pair_exp, pair_slot
+
+
+def peer_forward(x: torch.Tensor, idx: torch.Tensor, ex: PeerExchange, experts_per_rank: int,
+                 expert_fn: Callable, expert_to_fn: Callable, combine_fn: Callable,
+                 fuse_return: bool = True, marks: list | None = None):
+    """One expert-parallel MoE layer over peer memory (the PeerExchange
+    transport): the same layer as :func:`ep_forward`.  expert_to_fn(rows,
+    pair_row, pair_exp, y_addr) stores pair p's output at address y_addr[p]
+    (int64 device tensor); expert_fn as in ep_forward is used when
+    fuse_return is False (outputs gathered locally, then copied by
+    tmoe_ep_return)."""
+    W, rank, cap = ex.world, ex.rank, ex.cap
+    T, k = idx.shape
+    H = x.shape[1]
+    if T > cap:
+        raise _lib.InvalidArgument(f"{T} tokens exceed the exchange capacity {cap}")
+    if k != ex.top_k or H != ex.hidden:
+        raise _lib.InvalidArgument("layer shape differs from the exchange's")
+    lib = _lib.load()
+    stream = ops.stream_ptr(x.device)
+    ex.epoch += 1
+    ep = ex.epoch
+    dest, member = _membership(idx, experts_per_rank, W)
+    pos = (torch.cumsum(member.to(torch.int32), 0, dtype=torch.int32) - 1).t().contiguous()
+    counts = member.sum(0, dtype=torch.int32)
+    _mark(marks, "plan")
+    _lib.check(lib.tmoe_ep_dispatch(x.data_ptr(), idx.data_ptr(), T, k, H, experts_per_rank, W,
+                                    rank, pos.data_ptr(), counts.data_ptr(), ex.peers.data_ptr(),
+                                    ex.offsets, cap, ep, ex.tickets.data_ptr(), stream),
+               "tmoe_ep_dispatch")
+    rows_in = torch.empty(W, dtype=torch.int32, device=x.device)
+    _lib.check(lib.tmoe_ep_wait(ex.ptr, ex.offsets, 0, W, ep, rows_in.data_ptr(), stream),
+               "tmoe_ep_wait")
+    _mark(marks, "dispatch")
+    flags = received_pairs(ex.meta, rows_in)
+    bad = (rows_in < 0).sum()
+    if ex._pending is not None:
+        bad = bad + (ex._pending < 0).sum()
+    stat = torch.stack([flags.sum(), bad]).cpu()       # the layer's one host sync
+    if int(stat[1]):
+        raise _lib.DeviceTimeout("a peer exchange wait gave up (a rank did not post its flag)")
+    P = int(stat[0])
+    pair_row, pair_exp, pair_slot = peer_pairs(ex.meta, flags, P, ex.arange(W * cap * k))
+    src = pair_row // cap
+    back = torch.bincount(src, minlength=W)[:W].to(torch.int32)
+    _mark(marks, "pairs")
+    if fuse_return:
+        tok = ex.meta[..., k].reshape(-1)[pair_row.long()].long()
+        y_addr = ex.peers[src.long()] + ex.ret_offset + (tok * k + pair_slot.long()) * (2 * H)
+        expert_to_fn(ex.rows, pair_row, pair_exp, y_addr)
+        _lib.check(lib.tmoe_ep_return(None, None, None, 0, ex.ptr, k, H, cap, W, rank,
+                                      back.data_ptr(), ex.peers.data_ptr(), ex.offsets, ep,
+                                      ex.tickets[1:].data_ptr(), stream), "tmoe_ep_return")
+        _mark(marks, "experts+return")
+    else:
+        y_pairs = expert_fn(ex.rows, pair_row, pair_exp)
+        _mark(marks, "experts")
+        _lib.check(lib.tmoe_ep_return(y_pairs.data_ptr() if P else None, pair_row.data_ptr(),
+                                      pair_slot.data_ptr(), P, ex.ptr, k, H, cap, W, rank,
+                                      back.data_ptr(), ex.peers.data_ptr(), ex.offsets, ep,
+                                      ex.tickets[1:].data_ptr(), stream), "tmoe_ep_return")
+        _mark(marks, "return")
+    got = torch.empty(W, dtype=torch.int32, device=x.device)
+    _lib.check(lib.tmoe_ep_wait(ex.ptr, ex.offsets, 1, W, ep, got.data_ptr(), stream),
+               "tmoe_ep_wait")
+    ex._pending = got
+    _mark(marks, "wait")
+    y = combine_fn(ex.ret[:T * k], ex.arange(T * k))
+    _mark(marks, "combine")
+    return y
+
+
 class ExpertParallelMoE(torch.nn.Module):
     """A SparseMoeBlock sharded over the ranks of ``group``: this rank holds
     experts [rank * E/W, (rank+1) * E/W) and a full copy of the router and the
     shared expert; the constructor slices them out of a full block."""
 
-    def __init__(self, block, group=None):
+    def __init__(self, block, group=None, exchange: PeerExchange | None = None,
+                 fuse_return: bool = True):
         super().__init__()
         self.group = group
+        self.exchange, self.fuse_return = exchange, fuse_return
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
         E = block.num_experts
@@ -298,6 +502,22 @@ class ExpertParallelMoE(torch.nn.Module):
                    "tmoe_moe_experts")
         return y
 
+    def experts_to(self, rows, pair_row, pair_exp, y_addr, options: _lib.Options | None = None):
+        """This rank's routed experts, pair p's output row stored at address
+        y_addr[p] (tmoe_moe_experts_to)."""
+        R, P = rows.shape[0], pair_row.numel()
+        if P == 0:
+            return
+        L = self._layer_struct()
+        opt = options if options is not None else _lib.Options(512, 1, 0, 1, 0)
+        lib = _lib.load()
+        nb = lib.tmoe_moe_experts_workspace_size(L, R, P, opt)
+        ws = ops.workspace(nb, rows.device, "ep")
+        _lib.check(lib.tmoe_moe_experts_to(L, rows.data_ptr(), R, pair_row.data_ptr(),
+                                           pair_exp.data_ptr(), P, opt, ws.data_ptr(), ws.numel(),
+                                           y_addr.data_ptr(), ops.stream_ptr(rows.device)),
+                   "tmoe_moe_experts_to")
+
     def combine(self, ys, inv, scores, shared_out, gate_logit, mode: int = 0):
         """The block's weighted sum plus gated shared expert (tmoe_moe_combine)."""
         T, k = scores.shape
@@ -317,7 +537,12 @@ class ExpertParallelMoE(torch.nn.Module):
         idx, scores, shared_out, gate_logit = self.local(xf, options)
         _mark(marks, "local")
         mode = options.wsum_mode if options is not None else 0
-        y = ep_forward(xf, idx, self.epr, lambda *a: self.experts(*a, options=options),
-                       lambda ys, inv: self.combine(ys, inv, scores, shared_out, gate_logit, mode),
-                       self.group, marks)
+        experts = lambda *a: self.experts(*a, options=options)  # noqa: E731
+        combine = lambda ys, inv: self.combine(ys, inv, scores, shared_out, gate_logit, mode)  # noqa: E731
+        if self.exchange is not None:
+            y = peer_forward(xf, idx, self.exchange, self.epr, experts,
+                             lambda *a: self.experts_to(*a, options=options), combine,
+                             self.fuse_return, marks)
+        else:
+            y = ep_forward(xf, idx, self.epr, experts, combine, self.group, marks)
         return y.reshape(x.shape)
