@@ -67,8 +67,6 @@ def parse():
     ap.add_argument("--ep-exchange", choices=("peer", "nccl"), default="peer",
                     help="ep: peer = NVLink stores into IPC-mapped buffers with the return "
                          "fused into the down GEMM; nccl = two all-to-alls per layer")
-    ap.add_argument("--ep-unfused-return", action="store_true",
-                    help="ep peer: return with a copy kernel after the experts")
     return ap.parse_args()
 
 
@@ -468,7 +466,7 @@ def _run_ep(args, world, rank, local, device):
         blk = SparseMoeBlock(c["H"], c["E"], c["k"], c["I"], c["Is"], device=device,
                              weight_std=0.02)
         zipf_router_(blk, torch.Generator().manual_seed(777 + l))
-        layers.append(ExpertParallelMoE(blk, exchange=ex, fuse_return=not args.ep_unfused_return))
+        layers.append(ExpertParallelMoE(blk, exchange=ex))
         del blk
     torch.cuda.empty_cache()
     gen = torch.Generator(device=device).manual_seed(9000 + rank)
@@ -520,6 +518,7 @@ def _run_ep(args, world, rank, local, device):
             phases[name] = phases.get(name, 0.0) + a0.elapsed_time(b0)
     phases = {k: round(1000 * v / len(layers), 1) for k, v in phases.items()}
     if ex is not None:
+        ex.check()                    # no device wait gave up
         ex.close()
     if rank != 0:
         return 0
@@ -535,9 +534,9 @@ def _run_ep(args, world, rank, local, device):
                    "tokens_per_rank": T, "experts_per_rank": c["E"] // world,
                    "parallelism": f"ep{world}",
                    "collective": ("2 NCCL all-to-alls per layer" if ex is None else
-                                  "NVLink stores into CUDA-IPC-mapped peer buffers, epoch flags; "
-                                  + ("return in a copy kernel" if args.ep_unfused_return else
-                                     "return stored by the down GEMM's epilogue")),
+                                  "NVLink stores into CUDA-IPC-mapped peer buffers, epoch "
+                                  "flags, return stored by the down GEMM's epilogue, no host "
+                                  "sync"),
                    "l2": f"inputs larger than L2: {args.ep_layers} layers of weights cycled",
                    "timing": "CUDA events around the step, max over ranks"},
         "phases_us_per_layer_rank0": phases,

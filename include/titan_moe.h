@@ -99,7 +99,8 @@ int tmoe_router_topk(const uint16_t* x, const uint16_t* router_w, int T, int H, 
  * titan/kernels/moe_gather_ws.py:176-202 (build_tiles, TileTable).
  * order [R]: sorted row -> flat index; inv_order [R]: flat -> sorted row;
  * offsets [E+1]; tile_row / tile_exp [maxt] (tiles of 128 rows, may be NULL);
- * ntiles [1].  maxt >= ceil(R/128) + E. */
+ * ntiles [1].  maxt >= ceil(R/128) + E.  Negative ids are left out: their
+ * inv_order is -1 and offsets[E] counts the others. */
 size_t tmoe_route_workspace_size(int R, int E);
 int tmoe_route_sort(const int32_t* idx, int R, int E, void* ws, size_t ws_bytes, int32_t* order,
                     int32_t* inv_order, int32_t* offsets, int32_t* tile_row, int32_t* tile_exp,
@@ -255,13 +256,17 @@ int tmoe_moe_experts(const tmoe_layer* layer, const uint16_t* x, int R, const in
                      const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
                      size_t ws_bytes, uint16_t* y_pairs, void* stream);
 
-/* tmoe_moe_experts storing the output row of pair p at y_rows[p] (a device
- * array of P row addresses, in any device's memory that this one can write:
- * the expert-parallel return writes the sources' rows over NVLink from the
- * down GEMM's epilogue). */
-int tmoe_moe_experts_to(const tmoe_layer* layer, const uint16_t* x, int R, const int32_t* pair_row,
-                        const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
-                        size_t ws_bytes, uint16_t* const* y_rows, void* stream);
+/* tmoe_moe_experts in slot form, for receive buffers of fixed capacity: pair
+ * f = row*top_k + j of the R rows x [R, H] is served when slot_exp[f] >= 0
+ * (its local expert; negative: skipped), and its output row is stored at
+ * address y_rows[f] — in any device's memory that this one can write (the
+ * expert-parallel return stores into the sources' buffers over NVLink from
+ * the down GEMM's epilogue).  slot_exp [R*top_k] int32, y_rows [R*top_k]
+ * device addresses; workspace tmoe_moe_experts_workspace_size(layer, R,
+ * R*top_k, opt).  Every count stays on the device. */
+int tmoe_moe_experts_slots(const tmoe_layer* layer, const uint16_t* x, int R,
+                           const int32_t* slot_exp, const tmoe_options* opt, void* ws,
+                           size_t ws_bytes, uint16_t* const* y_rows, void* stream);
 
 /* Source side, before the exchanges: the token-local part of the layer on
  * this rank's tokens, with the kernels and arguments of tmoe_moe_forward's
@@ -297,8 +302,8 @@ int tmoe_moe_combine(const uint16_t* ys, const int32_t* inv, const uint16_t* sco
  *   ret       [T_max*k][H] bf16        expert output of this rank's pairs
  *   flags     [2][world] uint64        dispatch, return: epoch<<32 | count
  * Epochs start at 1 and grow by one per layer call; the buffer starts zeroed.
- * `ticket` is one zeroed device int32 per kernel kind (dispatch, return);
- * the kernels leave it zeroed.  Waits poll with a bounded back-off; on
+ * `ticket` is one zeroed device int32 for tmoe_ep_dispatch, which leaves
+ * it zeroed.  Waits poll with a bounded back-off; on
  * timeout they write count -1 and tmoe_device_status returns
  * TMOE_ERR_TIMEOUT. */
 size_t tmoe_ep_buffer_bytes(int world, int cap, int H, int k, int T_max, size_t* offsets);
@@ -321,16 +326,12 @@ int tmoe_ep_dispatch(const uint16_t* x, const int32_t* idx, int T, int k, int H,
  * in the buffer `own`, writing the posted counts [world] (device int32). */
 int tmoe_ep_wait(const void* own, const size_t* offsets, int which, int world, int epoch,
                  int32_t* counts, void* stream);
-/* Owner side: output row p of y_pairs [P, H] (received row pair_row[p] =
- * source*cap + i, slot pair_slot[p]) to the source's ret row
- * (token*k + slot); then counts[s] (pairs returned to s) posted in each
- * rank's return flag.  With P = 0 it only posts the flags: the rows are
- * already there when tmoe_moe_experts_to stored them (the previous launch
- * on the stream). */
-int tmoe_ep_return(const uint16_t* y_pairs, const int32_t* pair_row, const int32_t* pair_slot,
-                   int P, const void* own, int k, int H, int cap, int world, int rank,
-                   const int32_t* counts, void* const* peers, const size_t* offsets, int epoch,
-                   int32_t* ticket, void* stream);
+/* Posts (epoch, counts[d]) — count 0 when counts is NULL — in this rank's
+ * slot of flag row `which` (0 dispatch, 1 return) of every rank d, after a
+ * system-scope fence.  The owner side of the return: launched after
+ * tmoe_moe_experts_slots has stored the sources' rows. */
+int tmoe_ep_post(int which, const int32_t* counts, int world, int rank, void* const* peers,
+                 const size_t* offsets, int epoch, void* stream);
 
 #ifdef __cplusplus
 }

@@ -12,8 +12,8 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from titan_b200.expert_parallel import (_membership, pairs_from_meta, peer_pairs, plan_dispatch,
-                                        received_pairs, return_slots)
+from titan_b200.expert_parallel import (_membership, pairs_from_meta, plan_dispatch,
+                                        return_addresses, return_slots, slot_experts)
 
 H, E, K = 64, 8, 3
 
@@ -85,10 +85,10 @@ def test_pairs_and_return_slots():
 def test_peer_exchange_host_plan(world):
     """The host side of the peer-memory transport: destination rows (pos,
     counts) as peer_forward computes them, the metadata rows a dispatch
-    writes (simulated here), and the owner's pair list read back from a
-    buffer whose unwritten rows hold stale ids.  Every (source, token, slot)
-    must be served once, by the owner of its expert, and be returned to
-    ret row token*k + slot of its source."""
+    writes (simulated here), and the owner's slot list and return addresses
+    read back from a buffer whose unwritten rows hold stale ids.  Every
+    (source, token, slot) must be served once, by the owner of its expert,
+    and be returned to ret row token*k + slot of its source."""
     epr, cap = E // world, 9
     tokens = [9, 0, 4, 7][:world]
     g = torch.Generator().manual_seed(77)
@@ -115,20 +115,21 @@ def test_peer_exchange_host_plan(world):
         for d in range(world):
             rows_in[d][s] = counts[d]
     served = {}
+    H_, ret_off = 32, 4096
+    peers = torch.tensor([(s + 1) << 40 for s in range(world)], dtype=torch.int64)
     for d in range(world):
-        flags = received_pairs(meta[d], rows_in[d])
-        P = int(flags.sum())
-        pr, pe, ps = peer_pairs(meta[d], flags, P, torch.arange(world * cap * K, dtype=torch.int32))
-        assert pr.dtype == pe.dtype == ps.dtype == torch.int32
-        back = torch.bincount(pr // cap, minlength=world)[:world]
-        for p in range(P):
-            s, t = int(pr[p]) // cap, int(meta[d].view(-1, K + 1)[int(pr[p]), K])
-            slot = int(ps[p])
-            assert int(idxs[s][t, slot]) == d * epr + int(pe[p])
+        se = slot_experts(meta[d], rows_in[d], epr)
+        addr = return_addresses(meta[d], peers, ret_off, H_)
+        assert se.dtype == torch.int32 and se.shape == (world * cap * K,)
+        for f in torch.nonzero(se >= 0).flatten().tolist():
+            s, i, slot = f // (cap * K), (f // K) % cap, f % K
+            t = int(meta[d][s, i, K])
+            assert int(idxs[s][t, slot]) == d * epr + int(se[f])
+            off = int(addr[f]) - int(peers[s]) - ret_off
+            assert off % (2 * H_) == 0 and off // (2 * H_) == t * K + slot
             key = (s, t * K + slot)
             assert key not in served
             served[key] = d
-        assert int(back.sum()) == P
     assert sorted(served) == [(s, i) for s in range(world) for i in range(tokens[s] * K)]
 
 

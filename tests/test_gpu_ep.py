@@ -77,7 +77,7 @@ def test_ep_single_rank_matches_block(cuda, oracle):
 def test_ep_peer_single_rank_matches_block(cuda, oracle):
     """The peer-memory transport on one rank: the dispatch and return
     kernels write through the rank's own buffer and the flags; two layers
-    share one exchange and run in turn, fused and unfused returns, and an
+    share one exchange and run in turn, with calls of different sizes and an
     empty call; every output bit-identical to the single-GPU block."""
     import torch.distributed as dist
     from titan_b200.expert_parallel import ExpertParallelMoE, PeerExchange
@@ -88,23 +88,20 @@ def test_ep_peer_single_rank_matches_block(cuda, oracle):
         ex = PeerExchange(160, SHAPE["H"], SHAPE["k"])
         L0, blk0 = _blocks(oracle, cuda, SHAPE0, 33)
         L, blk = _blocks(oracle, cuda, SHAPE, 31)
-        for fuse in (True, False):
-            eps = (ExpertParallelMoE(blk0, exchange=ex, fuse_return=fuse),
-                   ExpertParallelMoE(blk, exchange=ex, fuse_return=fuse))
-            for T in (150, 7, 160):
-                x = oracle.make_x(T, SHAPE["H"], seed=T + fuse)
-                for ep, b in zip(eps, (blk0, blk)):
-                    y = ep(bf(x), options=_opts(1))
-                    yb = b(bf(x), options=_opts(1))
-                    assert torch.equal(y.view(torch.int16), yb.view(torch.int16)), (fuse, T)
-            y = eps[1](bf(oracle.make_x(0, SHAPE["H"], seed=1)), options=_opts(1))
-            assert y.shape == (0, SHAPE["H"])
+        eps = (ExpertParallelMoE(blk0, exchange=ex), ExpertParallelMoE(blk, exchange=ex))
+        for T in (150, 7, 160, 1, 150):
+            x = oracle.make_x(T, SHAPE["H"], seed=T)
+            for ep, b in zip(eps, (blk0, blk)):
+                y = ep(bf(x), options=_opts(1))
+                yb = b(bf(x), options=_opts(1))
+                assert torch.equal(y.view(torch.int16), yb.view(torch.int16)), T
+        y = eps[1](bf(oracle.make_x(0, SHAPE["H"], seed=1)), options=_opts(1))
+        assert y.shape == (0, SHAPE["H"])
         x = oracle.make_x(150, SHAPE["H"], seed=5)
         y = ExpertParallelMoE(blk, exchange=ex)(bf(x), options=_opts(1))
         torch.cuda.synchronize()
         _compare(oracle, L, x, nbf(y))
-        from titan_b200 import _lib
-        assert _lib.load().tmoe_device_status() == 0
+        ex.check()
         ex.close()
     finally:
         dist.destroy_process_group()
@@ -185,11 +182,10 @@ def _worker(rank, world, port, layer_arrays, T, q):
                 y = nbf(ep(bf(x, dev=dev), options=_opts(1)))
                 out[tag] = (y, yb, ry, ops)
                 continue
-            for fuse in (True, False):
-                ep = ExpertParallelMoE(blk, exchange=ex, fuse_return=fuse)
-                for _ in range(2):                     # the exchange reused call after call
-                    y = nbf(ep(bf(x, dev=dev), options=_opts(1)))
-                    out[f"{tag}_{fuse}"] = (y, yb, ry, ops)
+            ep = ExpertParallelMoE(blk, exchange=ex)
+            for i in range(3):                         # the exchange reused call after call
+                y = nbf(ep(bf(x, dev=dev), options=_opts(1)))
+                out[f"{tag}_{i}"] = (y, yb, ry, ops)
         if ex is not None:
             from titan_b200 import _lib
             out["status"] = int(_lib.load().tmoe_device_status())
@@ -227,7 +223,7 @@ def test_ep_two_gpus_nccl(oracle):
 def test_ep_two_gpus_peer_memory(oracle):
     """The peer-memory transport over two GPUs (CUDA IPC mappings, NVLink
     stores, epoch flags): bit-identical to the single-GPU block on each
-    rank's tokens, fused and unfused returns, ranks with unequal tokens."""
+    rank's tokens, calls in a row, ranks with unequal tokens."""
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

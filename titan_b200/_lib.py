@@ -110,8 +110,8 @@ _SIGS = {
     "tmoe_moe_experts_workspace_size": ([C.POINTER(Layer), I32, I32, C.POINTER(Options)], SZ),
     "tmoe_moe_experts": ([C.POINTER(Layer), P, I32, P, P, I32, C.POINTER(Options), P, SZ, P, P],
                          I32),
-    "tmoe_moe_experts_to": ([C.POINTER(Layer), P, I32, P, P, I32, C.POINTER(Options), P, SZ, P,
-                             P], I32),
+    "tmoe_moe_experts_slots": ([C.POINTER(Layer), P, I32, P, C.POINTER(Options), P, SZ, P, P],
+                               I32),
     "tmoe_moe_combine": ([P, P, P, I32, I32, I32, I32, P, P, P, P], I32),
     "tmoe_moe_local_workspace_size": ([C.POINTER(Layer), I32, C.POINTER(Options)], SZ),
     "tmoe_moe_local": ([C.POINTER(Layer), P, I32, C.POINTER(Options), P, SZ, P, P, P, P, P], I32),
@@ -123,7 +123,7 @@ _SIGS = {
     "tmoe_ipc_close": ([P], I32),
     "tmoe_ep_dispatch": ([P, P, I32, I32, I32, I32, I32, I32, P, P, P, P, I32, I32, P, P], I32),
     "tmoe_ep_wait": ([P, P, I32, I32, I32, P, P], I32),
-    "tmoe_ep_return": ([P, P, P, I32, P, I32, I32, I32, I32, I32, P, P, P, I32, P, P], I32),
+    "tmoe_ep_post": ([I32, P, I32, I32, P, P, I32, P], I32),
 }
 
 EXPORTED = tuple(_SIGS)

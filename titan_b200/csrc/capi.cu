@@ -1011,10 +1011,12 @@ size_t tmoe_moe_experts_workspace_size(const tmoe_layer* L, int R, int npairs,
 
 namespace {
 // The owner side; the output row of pair p goes to y_pairs[p] or, when
-// y_ptr is set, to y_ptr[p].
+// y_ptr is set, to y_ptr[p].  With slot_k > 0 there is no pair_row: pair p
+// reads row p / slot_k, and pairs whose expert id is negative are skipped.
 int moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pair_row,
-                const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
-                size_t ws_bytes, uint16_t* y_pairs, uint16_t* const* y_ptr, void* stream) {
+                int slot_k, const int32_t* pair_exp, int npairs, const tmoe_options* opt,
+                void* ws, size_t ws_bytes, uint16_t* y_pairs, uint16_t* const* y_ptr,
+                void* stream) {
   if (!L || R < 0 || npairs < 0) return fail(TMOE_ERR_INVALID, "tmoe_moe_experts: bad arguments");
   const int H = L->hidden, E = L->num_experts, I = L->moe_inter, G = H / 64;
   if (!L->gate_up_w || !L->gate_up_st || !L->gate_up_bt || !L->down_w || !L->down_st ||
@@ -1023,7 +1025,7 @@ int moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pa
   if (H <= 0 || H % 128 || I <= 0 || I % 64 || E <= 0 || E > 1024)
     return fail(TMOE_ERR_UNSUPPORTED, "tmoe_moe_experts: need H %% 128 == 0, I %% 64 == 0, E <= 1024");
   if (R == 0 || npairs == 0) return TMOE_OK;
-  if (!x || (!y_pairs && !y_ptr) || !pair_row || !pair_exp)
+  if (!x || (!y_pairs && !y_ptr) || (!pair_row && slot_k <= 0) || !pair_exp)
     return fail(TMOE_ERR_INVALID, "tmoe_moe_experts: null pointer");
   const size_t need = tmoe_moe_experts_workspace_size(L, R, npairs, opt);
   if (!ws || ws_bytes < need)
@@ -1064,8 +1066,8 @@ int moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pa
   g.s_r = G;
   g.s_g = 1;
   g.a_rows = b.order;          // sorted position -> pair
-  g.a_map = pair_row;          // pair -> received row
-  g.a_div = 1;
+  g.a_map = slot_k > 0 ? nullptr : pair_row;   // pair -> received row
+  g.a_div = slot_k > 0 ? slot_k : 1;
   g.W = L->gate_up_w;
   g.st = L->gate_up_st;
   g.bt = L->gate_up_bt;
@@ -1109,15 +1111,20 @@ extern "C" {
 int tmoe_moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pair_row,
                      const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
                      size_t ws_bytes, uint16_t* y_pairs, void* stream) {
-  return moe_experts(L, x, R, pair_row, pair_exp, npairs, opt, ws, ws_bytes, y_pairs, nullptr,
-                     stream);
+  return moe_experts(L, x, R, pair_row, 0, pair_exp, npairs, opt, ws, ws_bytes, y_pairs,
+                     nullptr, stream);
 }
 
-int tmoe_moe_experts_to(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pair_row,
-                        const int32_t* pair_exp, int npairs, const tmoe_options* opt, void* ws,
-                        size_t ws_bytes, uint16_t* const* y_rows, void* stream) {
-  if (npairs > 0 && !y_rows) return fail(TMOE_ERR_INVALID, "tmoe_moe_experts_to: null y_rows");
-  return moe_experts(L, x, R, pair_row, pair_exp, npairs, opt, ws, ws_bytes, nullptr, y_rows,
+int tmoe_moe_experts_slots(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* slot_exp,
+                           const tmoe_options* opt, void* ws, size_t ws_bytes,
+                           uint16_t* const* y_rows, void* stream) {
+  if (!L || R < 0) return fail(TMOE_ERR_INVALID, "tmoe_moe_experts_slots: bad arguments");
+  if (R > 0 && (!y_rows || !slot_exp))
+    return fail(TMOE_ERR_INVALID, "tmoe_moe_experts_slots: null pointer");
+  const int k = L->top_k;
+  if (k <= 0 || (long long)R * k > (1ll << 30))
+    return fail(TMOE_ERR_INVALID, "tmoe_moe_experts_slots: bad top_k or too many slots");
+  return moe_experts(L, x, R, nullptr, k, slot_exp, R * k, opt, ws, ws_bytes, nullptr, y_rows,
                      stream);
 }
 
@@ -1317,32 +1324,20 @@ int tmoe_ep_wait(const void* own, const size_t* offsets, int which, int world, i
   return TMOE_OK;
 }
 
-int tmoe_ep_return(const uint16_t* y_pairs, const int32_t* pair_row, const int32_t* pair_slot,
-                   int P, const void* own, int k, int H, int cap, int world, int rank,
-                   const int32_t* counts, void* const* peers, const size_t* offsets, int epoch,
-                   int32_t* ticket, void* stream) {
-  if (P < 0 || !own || k <= 0 || H <= 0 || H % 8 || cap <= 0 || world <= 0 || world > 32 ||
-      rank < 0 || rank >= world || !counts || !peers || !offsets || !ticket ||
-      (P > 0 && (!y_pairs || !pair_row || !pair_slot)))
-    return fail(TMOE_ERR_INVALID, "tmoe_ep_return: bad arguments");
-  EpReturnArgs a{};
-  a.y_pairs = y_pairs;
-  a.pair_row = pair_row;
-  a.pair_slot = pair_slot;
-  a.meta = reinterpret_cast<const int32_t*>(static_cast<const uint8_t*>(own) + offsets[1]);
+int tmoe_ep_post(int which, const int32_t* counts, int world, int rank, void* const* peers,
+                 const size_t* offsets, int epoch, void* stream) {
+  if ((which != 0 && which != 1) || world <= 0 || world > 32 || rank < 0 || rank >= world ||
+      !peers || !offsets)
+    return fail(TMOE_ERR_INVALID, "tmoe_ep_post: bad arguments");
+  EpPostArgs a{};
   a.counts = counts;
   a.peer = peers;
-  a.off_ret = offsets[2];
   a.off_flags = offsets[3];
-  a.ticket = ticket;
-  a.P = P;
-  a.k = k;
-  a.H = H;
+  a.which = which;
   a.world = world;
   a.rank = rank;
-  a.cap = cap;
   a.epoch = epoch;
-  TMOE_TRY(launch_ep_return(a, S(stream)), "ep_return");
+  TMOE_TRY(launch_ep_post(a, S(stream)), "ep_post");
   return TMOE_OK;
 }
 

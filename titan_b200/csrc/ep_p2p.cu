@@ -14,12 +14,13 @@
 //                                    epoch << 32 | count
 // Dispatch: a source writes each of its token rows once to every rank that
 // owns one of the token's experts (deduplicated), then posts (epoch, rows) in
-// that rank's dispatch flag.  Return: an owner writes every served pair's
-// output straight into the source's ret row (token, slot), then posts
-// (epoch, pairs) in the source's return flag.  Writes are plain stores to
-// peer memory; the flag of a kernel is posted by its last CTA after a
-// system-scope fence and a ticket, so a reader that sees the flag sees the
-// data.  Waits are bounded (4 s of device time): on timeout the kernel
+// that rank's dispatch flag.  Return: an owner's down GEMM stores every served
+// pair's output straight into the source's ret row (token, slot) from its
+// epilogue, then ep_post posts the epoch in every source's return flag.
+// Writes are plain stores to peer memory; the dispatch flag is posted after
+// a system-scope fence by every writer and a ticket that picks the kernel's
+// last CTA, the return flag by the launch after the GEMM, so a reader that
+// sees a flag (an acquire load) sees the data.  Waits are bounded (4 s of device time): on timeout the kernel
 // records an error that tmoe_device_status reports and returns.
 //
 // Reuse across layers needs no double buffer: a source dispatches layer L+1
@@ -120,40 +121,21 @@ __global__ void ep_wait_kernel(const unsigned long long* flags, int W, int epoch
   atomicExch(&g_ep_error, 1);
 }
 
-// One CTA per served pair: its output row to the source's ret row.  With
-// P = 0 it only posts the flags: the rows were stored straight into the
-// sources' ret rows by the down GEMM's epilogue (GemmParams::y_ptr), whose
-// launch precedes this one on the stream.
-__global__ void __launch_bounds__(128) ep_return_kernel(EpReturnArgs a) {
-  const int p = blockIdx.x, tid = threadIdx.x;
-  const int k = a.k, H = a.H;
-  __shared__ int s_last;
-  if (p < a.P) {                                 // a CTA past the pairs only posts flags
-    const int row = a.pair_row[p];               // received row: source * cap + i
-    const int src = row / a.cap;
-    const int32_t* meta = a.meta + (size_t)row * (k + 1);
-    const int slot = a.pair_slot[p], t = meta[k];
-    uint8_t* base = static_cast<uint8_t*>(a.peer[src]);
-    uint4* dst = reinterpret_cast<uint4*>(base + a.off_ret + ((size_t)t * k + slot) * H * 2);
-    const uint4* y = reinterpret_cast<const uint4*>(a.y_pairs + (size_t)p * H);
-    for (int i = tid; i < H / 8; i += 128) dst[i] = y[i];
-  }
+// One thread per rank d: (epoch, counts[d]) into this rank's slot of d's
+// flag row `which`.  The return's rows were stored into the sources' ret rows
+// by the down GEMM's epilogue (GemmParams::y_ptr), an earlier launch on the
+// stream: a kernel's stores, peer stores included, are performed at system
+// scope when it completes (the completion is what makes them visible to the
+// host), so the flag, stored after that, cannot overtake them.
+__global__ void ep_post_kernel(EpPostArgs a) {
+  const int d = threadIdx.x;
+  if (d >= a.world) return;
   __threadfence_system();
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence_system();
-    s_last = ticket_acq_rel(a.ticket) == (int)gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  if (tid < a.world) {
-    __threadfence_system();
-    unsigned long long* flags = reinterpret_cast<unsigned long long*>(
-        static_cast<uint8_t*>(a.peer[tid]) + a.off_flags);
-    st_release_sys64(flags + a.world + a.rank,
-                     ((unsigned long long)(uint32_t)a.epoch << 32) | (uint32_t)a.counts[tid]);
-  }
-  if (tid == 0) *a.ticket = 0;
+  unsigned long long* flags = reinterpret_cast<unsigned long long*>(
+      static_cast<uint8_t*>(a.peer[d]) + a.off_flags);
+  const uint32_t n = a.counts ? (uint32_t)a.counts[d] : 0u;
+  st_release_sys64(flags + (size_t)a.which * a.world + a.rank,
+                   ((unsigned long long)(uint32_t)a.epoch << 32) | n);
 }
 
 }  // namespace
@@ -169,8 +151,8 @@ cudaError_t launch_ep_wait(const unsigned long long* flags, int W, int epoch, in
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_return(const EpReturnArgs& a, cudaStream_t s) {
-  ep_return_kernel<<<a.P > 0 ? a.P : 1, 128, 0, s>>>(a);
+cudaError_t launch_ep_post(const EpPostArgs& a, cudaStream_t s) {
+  ep_post_kernel<<<1, 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -5,6 +5,9 @@
 // the decode kernels iterate over.  No host synchronisation: every count
 // stays on the device and the consumers read it there.
 //
+// Negative ids are skipped: they get no sorted row (inv = -1) and the sorted
+// rows end at offsets[E] = the number of non-negative ids.
+//
 // Small plans (R <= kSmallRows) are one CTA; large plans are three kernels:
 // per-block histograms, a per-expert scan across blocks, and a stable
 // scatter that ranks equal ids within a block with __match_any_sync.  The
@@ -105,27 +108,32 @@ TMOE_DEV void plan_from_counts(const int32_t* cnt, int32_t* off, int E, int R, i
 
 // Totals of the tile and distinct-expert counts and the closing entries of
 // the offsets and distinct-expert lists.
-TMOE_DEV void plan_totals(const int32_t* cnt, int E, int R, int tile_m, int maxt,
+// The sorted rows end at the number of placed ids (R unless some are
+// negative).
+TMOE_DEV void plan_totals(const int32_t* cnt, int E, int tile_m, int maxt,
                           const RoutePlan& plan) {
-  __shared__ int s_tiles, s_uniq;
+  __shared__ int s_tiles, s_uniq, s_rows;
   if (threadIdx.x == 0) {
     s_tiles = 0;
     s_uniq = 0;
+    s_rows = 0;
   }
   __syncthreads();
-  int tl = 0, un = 0;
+  int tl = 0, un = 0, nr = 0;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     tl += (cnt[e] + tile_m - 1) / tile_m;
     un += cnt[e] > 0;
+    nr += cnt[e];
   }
   atomicAdd(&s_tiles, tl);
   atomicAdd(&s_uniq, un);
+  atomicAdd(&s_rows, nr);
   __syncthreads();
   if (threadIdx.x == 0) {
-    plan.offsets[E] = R;
+    plan.offsets[E] = s_rows;
     if (plan.ntiles) plan.ntiles[0] = s_tiles < maxt ? s_tiles : maxt;
     if (plan.nuniq) plan.nuniq[0] = s_uniq;
-    if (plan.ustart) plan.ustart[s_uniq] = R;
+    if (plan.ustart) plan.ustart[s_uniq] = s_rows;
   }
 }
 
@@ -144,13 +152,18 @@ __global__ void __launch_bounds__(1024) route_plan_small(
   for (int i = tid; i < R; i += blockDim.x) sidx[i] = idx[i];
   for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
-  for (int i = tid; i < R; i += blockDim.x) atomicAdd(&cnt[sidx[i]], 1);
+  for (int i = tid; i < R; i += blockDim.x)
+    if (sidx[i] >= 0) atomicAdd(&cnt[sidx[i]], 1);
   __syncthreads();
   plan_from_counts(cnt, off, E, R, tile_m, maxt, plan, ws);
-  plan_totals(cnt, E, R, tile_m, maxt, plan);
+  plan_totals(cnt, E, tile_m, maxt, plan);
   __syncthreads();
   for (int i = tid; i < R; i += blockDim.x) {
     const int e = sidx[i];
+    if (e < 0) {
+      plan.inv[i] = -1;
+      continue;
+    }
     int rank = 0;
     for (int j = 0; j < i; ++j) rank += (sidx[j] == e);
     const int pos = off[e] + rank;
@@ -169,7 +182,7 @@ __global__ void __launch_bounds__(kBlk) route_hist(const int32_t* __restrict__ i
   for (int e = threadIdx.x; e < E; e += kBlk) h[e] = 0;
   __syncthreads();
   const int i = blockIdx.x * kBlk + threadIdx.x;
-  if (i < R) atomicAdd(&h[idx[i]], 1);
+  if (i < R && idx[i] >= 0) atomicAdd(&h[idx[i]], 1);
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += kBlk) blockhist[(size_t)blockIdx.x * E + e] = h[e];
 }
@@ -193,7 +206,7 @@ __global__ void __launch_bounds__(1024) route_scan(int32_t* __restrict__ blockhi
   }
   __syncthreads();
   plan_from_counts(tot, off, E, R, tile_m, maxt, plan, ws);
-  plan_totals(tot, E, R, tile_m, maxt, plan);
+  plan_totals(tot, E, tile_m, maxt, plan);
 }
 
 // Stable scatter: rank = offsets[e] + (ids of e in earlier blocks) +
@@ -206,8 +219,10 @@ __global__ void __launch_bounds__(kBlk) route_scatter(const int32_t* __restrict_
   for (int i = tid; i < 32 * E; i += kBlk) wc[i] = 0;
   __syncthreads();
   const int i = blockIdx.x * kBlk + tid;
-  const bool ok = i < R;
-  const int e = ok ? idx[i] : -1 - lane;  // distinct dummies never match
+  const int id = i < R ? idx[i] : -1;
+  const bool ok = id >= 0;                // negative ids are not placed
+  if (i < R && !ok) plan.inv[i] = -1;
+  const int e = ok ? id : -1 - lane;      // distinct dummies never match
   const unsigned mask = __match_any_sync(0xffffffffu, e);
   const int rank_w = __popc(mask & ((1u << lane) - 1u));
   if (ok && rank_w == 0) wc[warp * E + e] = __popc(mask);
@@ -445,7 +460,7 @@ __global__ void __launch_bounds__(128) decode_route_kernel(
     for (int i = tid; i < R; i += 128) atomicAdd(&cnt[sidx[i]], 1);
     __syncthreads();
     plan_from_counts(cnt, off, E, R, 1, 0, plan, ws);
-    plan_totals(cnt, E, R, 1, 0, plan);
+    plan_totals(cnt, E, 1, 0, plan);
     __syncthreads();
     for (int i = tid; i < R; i += 128) {
       const int ee = sidx[i];

@@ -165,21 +165,16 @@ struct EpDispatchArgs {
   int32_t* ticket;          // zero between launches
   int T, k, H, epr, world, rank, cap, epoch;
 };
-struct EpReturnArgs {
-  const uint16_t* y_pairs;  // [P][H] bf16
-  const int32_t* pair_row;  // [P] received row (source * cap + i)
-  const int32_t* pair_slot; // [P] slot j of the pair
-  const int32_t* meta;      // this rank's recv_meta [W * cap][k + 1]
-  const int32_t* counts;    // [W] pairs returned to each source
+struct EpPostArgs {
+  const int32_t* counts;   // [world] or null (count 0)
   void* const* peer;
-  size_t off_ret, off_flags;
-  int32_t* ticket;
-  int P, k, H, world, rank, cap, epoch;
+  size_t off_flags;
+  int which, world, rank, epoch;
 };
 cudaError_t launch_ep_dispatch(const EpDispatchArgs& a, cudaStream_t s);
 cudaError_t launch_ep_wait(const unsigned long long* flags, int W, int epoch, int32_t* counts,
                            cudaStream_t s);
-cudaError_t launch_ep_return(const EpReturnArgs& a, cudaStream_t s);
+cudaError_t launch_ep_post(const EpPostArgs& a, cudaStream_t s);
 size_t ep_layout(int world, int cap, int H, int k, int T_max, size_t* off);
 int ep_error_flag();
 cudaError_t launch_to_f16p(const uint16_t* x, long long n, uint16_t* y, cudaStream_t s);

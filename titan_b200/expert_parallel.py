@@ -29,11 +29,11 @@ Two transports carry the exchanges:
             into every other rank through CUDA IPC and the library's kernels
             write into them over NVLink: tmoe_ep_dispatch stores each token
             row straight into its owners' receive rows, and the owners' down
-            GEMM (tmoe_moe_experts_to) stores every expert output row straight
-            into the source's return row from its epilogue, so the return
-            exchange is part of the expert kernel.  Epoch-tagged flags
-            (tmoe_ep_wait) replace the collectives; the host reads one pair
-            count per layer.
+            GEMM (tmoe_moe_experts_slots) stores every expert output row
+            straight into the source's return row from its epilogue, so the
+            return exchange is part of the expert kernel.  Epoch-tagged flags
+            (tmoe_ep_wait) replace the collectives, and the receive buffers
+            have a fixed capacity, so no count ever goes to the host.
 
 The expert arithmetic is ``tmoe_moe_experts`` and the final sum
 ``tmoe_moe_combine`` from libtitan_moe.so, and the token-local part (router,
@@ -273,7 +273,6 @@ class PeerExchange:
         self.ret = _view(self.ptr + o[2], (self.cap * k, H), torch.int16,
                          self.device).view(torch.bfloat16)
         self.ret_offset = o[2]
-        self._pending = None            # the last layer's return counts (-1: a wait gave up)
         self._ar = {}
 
     def arange(self, n: int) -> torch.Tensor:
@@ -281,6 +280,11 @@ class PeerExchange:
         if a is None:
             a = self._ar[n] = torch.arange(n, dtype=torch.int32, device=self.device)
         return a
+
+    def check(self) -> None:
+        """Raise DeviceTimeout if a wait of the library has given up (a rank
+        did not post its flag within the bound); synchronises the host."""
+        _lib.check(_lib.load().tmoe_device_status(), "peer exchange")
 
     def close(self) -> None:
         """Unmap the peers' buffers, wait for every rank to do the same, and
@@ -298,36 +302,42 @@ class PeerExchange:
         self.ptr = None
 
 
-def received_pairs(meta: torch.Tensor, rows_in: torch.Tensor) -> torch.Tensor:
-    """Which (received row, slot) entries of a PeerExchange's metadata
-    meta [W, cap, k+1] are pairs this rank serves: the row was written this
-    layer (index < rows_in[source]) and the slot's expert is here (id >= 0).
-    Flat bool [W*cap*k]."""
+def slot_experts(meta: torch.Tensor, rows_in: torch.Tensor, experts_per_rank: int) -> torch.Tensor:
+    """The slot-form pair list of a PeerExchange's metadata meta [W, cap, k+1]:
+    slot j of received row (source s, i) is served here by local expert
+    meta[s, i, j] when the row was written this layer (i < rows_in[s]) and
+    that id is one of this rank's experts; -1 otherwise.  int32 [W*cap*k]."""
     W, cap, k1 = meta.shape
     live = torch.arange(cap, dtype=torch.int32, device=meta.device)[None, :] < rows_in[:, None]
-    return ((meta[..., :k1 - 1] >= 0) & live[..., None]).reshape(-1)
+    ids = meta[..., :k1 - 1]
+    ok = live[..., None] & (ids >= 0) & (ids < experts_per_rank)
+    return torch.where(ok, ids, -1).reshape(-1)
 
 
-def peer_pairs(meta: torch.Tensor, flags: torch.Tensor, n_pairs: int, flat: torch.Tensor):
-    """The served pairs of received_pairs(), row-major: received row
-    (source * cap + i), local expert and slot of each, int32; flat =
-    arange(W*cap*k) int32."""
-    k = meta.shape[2] - 1
-    pair_row = _compact(flags, n_pairs, flat // k)
-    pair_exp = _compact(flags, n_pairs, meta[..., :k].reshape(-1))
-    pair_slot = _compact(flags, n_pairs, flat % k)
-    return pair_row, pair_exp, pair_slot
+def return_addresses(meta: torch.Tensor, peers: torch.Tensor, ret_offset: int,
+                     hidden: int) -> torch.Tensor:
+    """Where the output of slot j of received row (s, i) goes: the ret row
+    token*k + j of source s's buffer (peers [W] int64 base addresses), token =
+    meta[s, i, k].  int64 [W*cap*k]; entries of unserved slots are never
+    used."""
+    W, cap, k1 = meta.shape
+    k = k1 - 1
+    tok = meta[..., k].long()
+    slot = torch.arange(k, dtype=torch.int64, device=meta.device)
+    return (peers[:, None, None] + ret_offset + (tok[..., None] * k + slot) * (2 * hidden)).reshape(-1)
 
 
 def peer_forward(x: torch.Tensor, idx: torch.Tensor, ex: PeerExchange, experts_per_rank: int,
-                 expert_fn: Callable, expert_to_fn: Callable, combine_fn: Callable,
-                 fuse_return: bool = True, marks: list | None = None):
+                 expert_fn: Callable, combine_fn: Callable, marks: list | None = None):
     """One expert-parallel MoE layer over peer memory (the PeerExchange
-    transport): the same layer as :func:`ep_forward`.  expert_to_fn(rows,
-    pair_row, pair_exp, y_addr) stores pair p's output at address y_addr[p]
-    (int64 device tensor); expert_fn as in ep_forward is used when
-    fuse_return is False (outputs gathered locally, then copied by
-    tmoe_ep_return)."""
+    transport), the same layer as :func:`ep_forward` without a host
+    synchronisation: every count stays on the device.
+
+    expert_fn(rows, slot_exp, y_addr) applies this rank's experts to the
+    served slots of the received rows and stores slot f's output at address
+    y_addr[f] (the sources' ret rows; tmoe_moe_experts_slots).  A wait that
+    gives up leaves the layer's output undefined and is reported by
+    :meth:`PeerExchange.check` (tmoe_device_status)."""
     W, rank, cap = ex.world, ex.rank, ex.cap
     T, k = idx.shape
     H = x.shape[1]
@@ -351,38 +361,16 @@ def peer_forward(x: torch.Tensor, idx: torch.Tensor, ex: PeerExchange, experts_p
     _lib.check(lib.tmoe_ep_wait(ex.ptr, ex.offsets, 0, W, ep, rows_in.data_ptr(), stream),
                "tmoe_ep_wait")
     _mark(marks, "dispatch")
-    flags = received_pairs(ex.meta, rows_in)
-    bad = (rows_in < 0).sum()
-    if ex._pending is not None:
-        bad = bad + (ex._pending < 0).sum()
-    stat = torch.stack([flags.sum(), bad]).cpu()       # the layer's one host sync
-    if int(stat[1]):
-        raise _lib.DeviceTimeout("a peer exchange wait gave up (a rank did not post its flag)")
-    P = int(stat[0])
-    pair_row, pair_exp, pair_slot = peer_pairs(ex.meta, flags, P, ex.arange(W * cap * k))
-    src = pair_row // cap
-    back = torch.bincount(src, minlength=W)[:W].to(torch.int32)
-    _mark(marks, "pairs")
-    if fuse_return:
-        tok = ex.meta[..., k].reshape(-1)[pair_row.long()].long()
-        y_addr = ex.peers[src.long()] + ex.ret_offset + (tok * k + pair_slot.long()) * (2 * H)
-        expert_to_fn(ex.rows, pair_row, pair_exp, y_addr)
-        _lib.check(lib.tmoe_ep_return(None, None, None, 0, ex.ptr, k, H, cap, W, rank,
-                                      back.data_ptr(), ex.peers.data_ptr(), ex.offsets, ep,
-                                      ex.tickets[1:].data_ptr(), stream), "tmoe_ep_return")
-        _mark(marks, "experts+return")
-    else:
-        y_pairs = expert_fn(ex.rows, pair_row, pair_exp)
-        _mark(marks, "experts")
-        _lib.check(lib.tmoe_ep_return(y_pairs.data_ptr() if P else None, pair_row.data_ptr(),
-                                      pair_slot.data_ptr(), P, ex.ptr, k, H, cap, W, rank,
-                                      back.data_ptr(), ex.peers.data_ptr(), ex.offsets, ep,
-                                      ex.tickets[1:].data_ptr(), stream), "tmoe_ep_return")
-        _mark(marks, "return")
+    slot_exp = slot_experts(ex.meta, rows_in, experts_per_rank)
+    y_addr = return_addresses(ex.meta, ex.peers, ex.ret_offset, H)
+    _mark(marks, "slots")
+    expert_fn(ex.rows, slot_exp, y_addr)
+    _lib.check(lib.tmoe_ep_post(1, None, W, rank, ex.peers.data_ptr(), ex.offsets, ep, stream),
+               "tmoe_ep_post")
+    _mark(marks, "experts+return")
     got = torch.empty(W, dtype=torch.int32, device=x.device)
     _lib.check(lib.tmoe_ep_wait(ex.ptr, ex.offsets, 1, W, ep, got.data_ptr(), stream),
                "tmoe_ep_wait")
-    ex._pending = got
     _mark(marks, "wait")
     y = combine_fn(ex.ret[:T * k], ex.arange(T * k))
     _mark(marks, "combine")
@@ -394,11 +382,10 @@ class ExpertParallelMoE(torch.nn.Module):
     experts [rank * E/W, (rank+1) * E/W) and a full copy of the router and the
     shared expert; the constructor slices them out of a full block."""
 
-    def __init__(self, block, group=None, exchange: PeerExchange | None = None,
-                 fuse_return: bool = True):
+    def __init__(self, block, group=None, exchange: PeerExchange | None = None):
         super().__init__()
         self.group = group
-        self.exchange, self.fuse_return = exchange, fuse_return
+        self.exchange = exchange
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
         E = block.num_experts
@@ -502,21 +489,22 @@ class ExpertParallelMoE(torch.nn.Module):
                    "tmoe_moe_experts")
         return y
 
-    def experts_to(self, rows, pair_row, pair_exp, y_addr, options: _lib.Options | None = None):
-        """This rank's routed experts, pair p's output row stored at address
-        y_addr[p] (tmoe_moe_experts_to)."""
-        R, P = rows.shape[0], pair_row.numel()
-        if P == 0:
+    def experts_slots(self, rows, slot_exp, y_addr, options: _lib.Options | None = None):
+        """This rank's routed experts on the served slots of rows (slot_exp
+        [R*k], -1: not served), slot f's output row stored at address
+        y_addr[f] (tmoe_moe_experts_slots)."""
+        R = rows.shape[0]
+        if R == 0:
             return
         L = self._layer_struct()
         opt = options if options is not None else _lib.Options(512, 1, 0, 1, 0)
         lib = _lib.load()
-        nb = lib.tmoe_moe_experts_workspace_size(L, R, P, opt)
+        nb = lib.tmoe_moe_experts_workspace_size(L, R, R * self.top_k, opt)
         ws = ops.workspace(nb, rows.device, "ep")
-        _lib.check(lib.tmoe_moe_experts_to(L, rows.data_ptr(), R, pair_row.data_ptr(),
-                                           pair_exp.data_ptr(), P, opt, ws.data_ptr(), ws.numel(),
-                                           y_addr.data_ptr(), ops.stream_ptr(rows.device)),
-                   "tmoe_moe_experts_to")
+        _lib.check(lib.tmoe_moe_experts_slots(L, rows.data_ptr(), R, slot_exp.data_ptr(), opt,
+                                              ws.data_ptr(), ws.numel(), y_addr.data_ptr(),
+                                              ops.stream_ptr(rows.device)),
+                   "tmoe_moe_experts_slots")
 
     def combine(self, ys, inv, scores, shared_out, gate_logit, mode: int = 0):
         """The block's weighted sum plus gated shared expert (tmoe_moe_combine)."""
@@ -540,9 +528,8 @@ class ExpertParallelMoE(torch.nn.Module):
         experts = lambda *a: self.experts(*a, options=options)  # noqa: E731
         combine = lambda ys, inv: self.combine(ys, inv, scores, shared_out, gate_logit, mode)  # noqa: E731
         if self.exchange is not None:
-            y = peer_forward(xf, idx, self.exchange, self.epr, experts,
-                             lambda *a: self.experts_to(*a, options=options), combine,
-                             self.fuse_return, marks)
+            y = peer_forward(xf, idx, self.exchange, self.epr,
+                             lambda *a: self.experts_slots(*a, options=options), combine, marks)
         else:
             y = ep_forward(xf, idx, self.epr, experts, combine, self.group, marks)
         return y.reshape(x.shape)
