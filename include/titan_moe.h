@@ -302,8 +302,8 @@ int tmoe_moe_combine(const uint16_t* ys, const int32_t* inv, const uint16_t* sco
  *   ret       [T_max*k][H] bf16        expert output of this rank's pairs
  *   flags     [2][world] uint64        dispatch, return: epoch<<32 | count
  * Epochs start at 1 and grow by one per layer call; the buffer starts zeroed.
- * `ticket` is one zeroed device int32 for tmoe_ep_dispatch, which leaves
- * it zeroed.  Waits poll with a bounded back-off; on
+ * tmoe_ep_dispatch takes world + 1 zeroed device int32 counters and
+ * leaves them zeroed.  Waits poll with a bounded back-off; on
  * timeout they write count -1 and tmoe_device_status returns
  * TMOE_ERR_TIMEOUT. */
 size_t tmoe_ep_buffer_bytes(int world, int cap, int H, int k, int T_max, size_t* offsets);
@@ -313,19 +313,31 @@ int tmoe_ep_free(void* ptr);
 int tmoe_ipc_handle(void* ptr, void* handle);
 int tmoe_ipc_open(const void* handle, void** ptr);
 int tmoe_ipc_close(void* ptr);
-/* Source side: token t's row x[t] to every rank owning one of idx[t, :]
- * (owner = expert / experts_per_rank), at row pos[d*T + t] of that rank's
- * recv_x block for this source; then counts[d] posted in rank d's dispatch
- * flag.  pos and counts [world] are device int32 (the row counts per
- * destination). */
+/* Source side: token t's row x[t] to every rank d owning one of idx[t, :]
+ * (d = expert / experts_per_rank), at the next free row of this source's
+ * recv_x block on d (rows land in no fixed order; the metadata row carries
+ * the token index), then the number of rows sent posted in d's dispatch
+ * flag.  counters: device int32 [world + 1], zeroed once; every call leaves
+ * them zeroed. */
 int tmoe_ep_dispatch(const uint16_t* x, const int32_t* idx, int T, int k, int H,
-                     int experts_per_rank, int world, int rank, const int32_t* pos,
-                     const int32_t* counts, void* const* peers, const size_t* offsets, int cap,
-                     int epoch, int32_t* ticket, void* stream);
+                     int experts_per_rank, int world, int rank, void* const* peers,
+                     const size_t* offsets, int cap, int epoch, int32_t* counters, void* stream);
 /* Waits for every peer's flag of `which` (0 dispatch, 1 return) at `epoch`
  * in the buffer `own`, writing the posted counts [world] (device int32). */
 int tmoe_ep_wait(const void* own, const size_t* offsets, int which, int world, int epoch,
                  int32_t* counts, void* stream);
+/* Owner side, after the dispatch wait: the slot form of the received rows
+ * for tmoe_moe_experts_slots.  For f = (source * cap + i) * k + j,
+ * slot_exp[f] is the local expert of slot j of received row i from that
+ * source when the row was written this layer (i < rows_in[source], the
+ * counts tmoe_ep_wait returned) and the expert is one of this rank's, else
+ * -1; y_rows[f] is the address of the source's ret row token * k + j (NULL
+ * where slot_exp is -1).  slot_exp [world*cap*k] int32, y_rows
+ * [world*cap*k] device pointers. */
+int tmoe_ep_slots(const void* own, const size_t* offsets, const int32_t* rows_in, int world,
+                  int cap, int k, int experts_per_rank, int H, void* const* peers,
+                  int32_t* slot_exp, uint16_t** y_rows, void* stream);
+
 /* Posts (epoch, counts[d]) — count 0 when counts is NULL — in this rank's
  * slot of flag row `which` (0 dispatch, 1 return) of every rank d, after a
  * system-scope fence.  The owner side of the return: launched after

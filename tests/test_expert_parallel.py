@@ -119,7 +119,8 @@ def test_peer_exchange_host_plan(world):
     peers = torch.tensor([(s + 1) << 40 for s in range(world)], dtype=torch.int64)
     for d in range(world):
         se = slot_experts(meta[d], rows_in[d], epr)
-        addr = return_addresses(meta[d], peers, ret_off, H_)
+        addr = return_addresses(meta[d], se, peers, ret_off, H_)
+        assert bool((addr[se < 0] == 0).all())
         assert se.dtype == torch.int32 and se.shape == (world * cap * K,)
         for f in torch.nonzero(se >= 0).flatten().tolist():
             s, i, slot = f // (cap * K), (f // K) % cap, f % K

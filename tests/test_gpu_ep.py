@@ -107,6 +107,43 @@ def test_ep_peer_single_rank_matches_block(cuda, oracle):
         dist.destroy_process_group()
 
 
+def test_ep_slots_kernel_matches_tensor_statement(cuda):
+    """tmoe_ep_slots against its tensor statement (slot_experts,
+    return_addresses) on a 3-source buffer holding random metadata: rows past
+    each source's count, negative ids and ids of other ranks must come out as
+    -1 with a NULL address, and a source whose wait gave up (-1) as no rows."""
+    import ctypes as C
+    from titan_b200 import _lib
+    from titan_b200.expert_parallel import _view, return_addresses, slot_experts
+    lib = _lib.load()
+    W, cap, k, H, epr = 3, 37, 5, 256, 6
+    offs = (C.c_size_t * 4)()
+    nb = lib.tmoe_ep_buffer_bytes(W, cap, H, k, cap, offs)
+    ptr = C.c_void_p()
+    _lib.check(lib.tmoe_ep_alloc(nb, C.byref(ptr)))
+    try:
+        meta = _view(ptr.value + offs[1], (W, cap, k + 1), torch.int32, cuda)
+        g = torch.Generator(device=cuda).manual_seed(3)
+        meta[..., :k] = torch.randint(-2, epr + 3, (W, cap, k), generator=g, device=cuda,
+                                      dtype=torch.int32)
+        meta[..., k] = torch.randint(0, cap, (W, cap), generator=g, device=cuda, dtype=torch.int32)
+        peers = torch.tensor([ptr.value + (s << 30) for s in range(W)], dtype=torch.int64,
+                             device=cuda)
+        for rows in ([cap, 0, 11], [5, -1, cap]):
+            rows_in = torch.tensor(rows, dtype=torch.int32, device=cuda)
+            se = torch.full((W * cap * k,), 99, dtype=torch.int32, device=cuda)
+            yr = torch.full((W * cap * k,), 99, dtype=torch.int64, device=cuda)
+            _lib.check(lib.tmoe_ep_slots(ptr, offs, rows_in.data_ptr(), W, cap, k, epr, H,
+                                         peers.data_ptr(), se.data_ptr(), yr.data_ptr(), None))
+            want = slot_experts(meta, rows_in, epr)
+            assert torch.equal(se, want)
+            assert torch.equal(yr, return_addresses(meta, want, peers, int(offs[2]), H))
+            assert int((want >= 0).sum()) > 0
+    finally:
+        torch.cuda.synchronize()
+        _lib.check(lib.tmoe_ep_free(ptr))
+
+
 def _timeout_child(q):
     import ctypes as C
     try:

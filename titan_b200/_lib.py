@@ -121,7 +121,8 @@ _SIGS = {
     "tmoe_ipc_handle": ([P, P], I32),
     "tmoe_ipc_open": ([P, P], I32),
     "tmoe_ipc_close": ([P], I32),
-    "tmoe_ep_dispatch": ([P, P, I32, I32, I32, I32, I32, I32, P, P, P, P, I32, I32, P, P], I32),
+    "tmoe_ep_dispatch": ([P, P, I32, I32, I32, I32, I32, I32, P, P, I32, I32, P, P], I32),
+    "tmoe_ep_slots": ([P, P, P, I32, I32, I32, I32, I32, P, P, P, P], I32),
     "tmoe_ep_wait": ([P, P, I32, I32, I32, P, P], I32),
     "tmoe_ep_post": ([I32, P, I32, I32, P, P, I32, P], I32),
 }

@@ -1285,23 +1285,20 @@ int tmoe_ipc_close(void* ptr) {
 }
 
 int tmoe_ep_dispatch(const uint16_t* x, const int32_t* idx, int T, int k, int H,
-                     int experts_per_rank, int world, int rank, const int32_t* pos,
-                     const int32_t* counts, void* const* peers, const size_t* offsets, int cap,
-                     int epoch, int32_t* ticket, void* stream) {
+                     int experts_per_rank, int world, int rank, void* const* peers,
+                     const size_t* offsets, int cap, int epoch, int32_t* counters, void* stream) {
   if (T < 0 || k <= 0 || k >= 128 || H <= 0 || H % 8 || experts_per_rank <= 0 || world <= 0 ||
-      world > 32 || rank < 0 || rank >= world || T > cap || !counts || !peers || !offsets ||
-      !ticket || (T > 0 && (!x || !idx || !pos)))
+      world > 32 || rank < 0 || rank >= world || T > cap || !peers || !offsets || !counters ||
+      (T > 0 && (!x || !idx)))
     return fail(TMOE_ERR_INVALID, "tmoe_ep_dispatch: bad arguments");
   EpDispatchArgs a{};
   a.x = x;
   a.idx = idx;
-  a.pos = pos;
-  a.counts = counts;
   a.peer = peers;
   a.off_x = offsets[0];
   a.off_meta = offsets[1];
   a.off_flags = offsets[3];
-  a.ticket = ticket;
+  a.counters = counters;
   a.T = T;
   a.k = k;
   a.H = H;
@@ -1311,6 +1308,28 @@ int tmoe_ep_dispatch(const uint16_t* x, const int32_t* idx, int T, int k, int H,
   a.cap = cap;
   a.epoch = epoch;
   TMOE_TRY(launch_ep_dispatch(a, S(stream)), "ep_dispatch");
+  return TMOE_OK;
+}
+
+int tmoe_ep_slots(const void* own, const size_t* offsets, const int32_t* rows_in, int world,
+                  int cap, int k, int experts_per_rank, int H, void* const* peers,
+                  int32_t* slot_exp, uint16_t** y_rows, void* stream) {
+  if (!own || !offsets || !rows_in || world <= 0 || world > 32 || cap < 0 || k <= 0 ||
+      experts_per_rank <= 0 || H <= 0 || !peers || !slot_exp || !y_rows)
+    return fail(TMOE_ERR_INVALID, "tmoe_ep_slots: bad arguments");
+  EpSlotsArgs a{};
+  a.meta = reinterpret_cast<const int32_t*>(static_cast<const uint8_t*>(own) + offsets[1]);
+  a.rows_in = rows_in;
+  a.peer = peers;
+  a.off_ret = offsets[2];
+  a.slot_exp = slot_exp;
+  a.y_rows = reinterpret_cast<unsigned long long*>(y_rows);
+  a.world = world;
+  a.cap = cap;
+  a.k = k;
+  a.epr = experts_per_rank;
+  a.H = H;
+  TMOE_TRY(launch_ep_slots(a, S(stream)), "ep_slots");
   return TMOE_OK;
 }
 

@@ -58,46 +58,80 @@ TMOE_DEV unsigned long long ld_acquire_sys64(const unsigned long long* p) {
   return v;
 }
 
-// One CTA per token: its row (and metadata) to every owning rank.
+// One CTA per token: its row (and metadata) to every owning rank, at a row
+// taken from that rank's counter (rows land in any order: the owner serves
+// each row on its own, so the order changes no bit of any output).  The last
+// CTA posts the final counts and clears the counters for the next launch.
 __global__ void __launch_bounds__(128) ep_dispatch_kernel(EpDispatchArgs a) {
   const int t = blockIdx.x, tid = threadIdx.x;
   const int W = a.world, k = a.k, H = a.H;
   __shared__ int s_last;
-  const int32_t* ids = a.idx + (size_t)(t < a.T ? t : 0) * k;
-  for (int d = 0; d < W && t < a.T; ++d) {     // a CTA past the tokens only posts flags
-    bool mine = false;
-    for (int j = 0; j < k; ++j) mine |= ids[j] / a.epr == d;
-    if (!mine) continue;
-    const int pos = a.pos[(size_t)d * a.T + t];        // this token's row among those sent to d
-    uint8_t* base = static_cast<uint8_t*>(a.peer[d]);
-    const size_t row = (size_t)a.rank * a.cap + pos;
-    uint4* dst = reinterpret_cast<uint4*>(base + a.off_x + row * H * 2);
-    const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)t * H);
-    for (int i = tid; i < H / 8; i += 128) dst[i] = src[i];
-    int32_t* meta = reinterpret_cast<int32_t*>(base + a.off_meta) + row * (k + 1);
-    if (tid < k) {
-      const int e = ids[tid];
-      meta[tid] = e / a.epr == d ? e - d * a.epr : -1;
-    } else if (tid == k) {
-      meta[k] = t;
+  __shared__ int s_row[32];
+  if (t < a.T) {                                  // a CTA past the tokens only posts flags
+    const int32_t* ids = a.idx + (size_t)t * k;
+    if (tid < W) {
+      bool mine = false;
+      for (int j = 0; j < k; ++j) mine |= ids[j] / a.epr == tid;
+      s_row[tid] = mine ? atomicAdd(a.counters + 1 + tid, 1) : -1;
+    }
+    __syncthreads();
+    for (int d = 0; d < W; ++d) {
+      const int pos = s_row[d];
+      if (pos < 0) continue;
+      uint8_t* base = static_cast<uint8_t*>(a.peer[d]);
+      const size_t row = (size_t)a.rank * a.cap + pos;
+      uint4* dst = reinterpret_cast<uint4*>(base + a.off_x + row * H * 2);
+      const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)t * H);
+      for (int i = tid; i < H / 8; i += 128) dst[i] = src[i];
+      int32_t* meta = reinterpret_cast<int32_t*>(base + a.off_meta) + row * (k + 1);
+      if (tid < k) {
+        const int e = ids[tid];
+        meta[tid] = e / a.epr == d ? e - d * a.epr : -1;
+      } else if (tid == k) {
+        meta[k] = t;
+      }
     }
   }
   __threadfence_system();     // every writer's stores before the CTA's ticket
   __syncthreads();
   if (tid == 0) {
     __threadfence_system();
-    s_last = ticket_acq_rel(a.ticket) == (int)gridDim.x - 1;
+    s_last = ticket_acq_rel(a.counters) == (int)gridDim.x - 1;
   }
   __syncthreads();
   if (!s_last) return;
   if (tid < W) {
+    const int n = atomicExch(a.counters + 1 + tid, 0);   // final: every CTA added before its ticket
     __threadfence_system();
     unsigned long long* flags = reinterpret_cast<unsigned long long*>(
         static_cast<uint8_t*>(a.peer[tid]) + a.off_flags);
-    st_release_sys64(flags + a.rank,
-                     ((unsigned long long)(uint32_t)a.epoch << 32) | (uint32_t)a.counts[tid]);
+    st_release_sys64(flags + a.rank, ((unsigned long long)(uint32_t)a.epoch << 32) | (uint32_t)n);
   }
-  if (tid == 0) *a.ticket = 0;
+  if (tid == 0) a.counters[0] = 0;
+}
+
+// The owner's slot list over its receive buffer, one thread per (row, slot)
+// f = (s * cap + i) * k + j: the local expert of slot j of row i from source
+// s when that row was written this layer (i < rows_in[s]) and the expert is
+// here, else -1; and the address of the source's ret row token * k + j
+// (0 for a slot not served).
+__global__ void __launch_bounds__(256) ep_slots_kernel(EpSlotsArgs a) {
+  const long long n = (long long)a.world * a.cap * a.k;
+  const long long f = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= n) return;
+  const int k = a.k;
+  const long long row = f / k;
+  const int j = (int)(f - row * k);
+  const int s = (int)(row / a.cap), i = (int)(row - (long long)s * a.cap);
+  const int32_t* m = a.meta + row * (k + 1);
+  const int id = m[j];
+  const bool ok = i < a.rows_in[s] && id >= 0 && id < a.epr;
+  a.slot_exp[f] = ok ? id : -1;
+  unsigned long long addr = 0;
+  if (ok)
+    addr = reinterpret_cast<unsigned long long>(a.peer[s]) + a.off_ret +
+           ((unsigned long long)m[k] * k + j) * 2ull * a.H;
+  a.y_rows[f] = addr;
 }
 
 // One thread per peer: wait for this epoch's flag; counts[s] = its count,
@@ -148,6 +182,13 @@ cudaError_t launch_ep_dispatch(const EpDispatchArgs& a, cudaStream_t s) {
 cudaError_t launch_ep_wait(const unsigned long long* flags, int W, int epoch, int32_t* counts,
                            cudaStream_t s) {
   ep_wait_kernel<<<1, 32, 0, s>>>(flags, W, epoch, counts);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_slots(const EpSlotsArgs& a, cudaStream_t s) {
+  const long long n = (long long)a.world * a.cap * a.k;
+  if (n == 0) return cudaSuccess;
+  ep_slots_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -158,12 +158,19 @@ int layer_error_flag();
 struct EpDispatchArgs {
   const uint16_t* x;        // [T][H] bf16
   const int32_t* idx;       // [T][k] global expert ids
-  const int32_t* pos;       // [W][T] row of token t among those sent to rank d
-  const int32_t* counts;    // [W] rows sent to each rank
   void* const* peer;        // [W] each rank's exchange allocation, mapped here
   size_t off_x, off_meta, off_flags;
-  int32_t* ticket;          // zero between launches
+  int32_t* counters;        // [1 + W]: ticket, rows taken per rank; zero between launches
   int T, k, H, epr, world, rank, cap, epoch;
+};
+struct EpSlotsArgs {
+  const int32_t* meta;      // this rank's recv_meta [W][cap][k+1]
+  const int32_t* rows_in;   // [W] rows posted by each source (-1: its wait gave up)
+  void* const* peer;
+  size_t off_ret;
+  int32_t* slot_exp;               // [W*cap*k]
+  unsigned long long* y_rows;      // [W*cap*k]
+  int world, cap, k, epr, H;
 };
 struct EpPostArgs {
   const int32_t* counts;   // [world] or null (count 0)
@@ -175,6 +182,7 @@ cudaError_t launch_ep_dispatch(const EpDispatchArgs& a, cudaStream_t s);
 cudaError_t launch_ep_wait(const unsigned long long* flags, int W, int epoch, int32_t* counts,
                            cudaStream_t s);
 cudaError_t launch_ep_post(const EpPostArgs& a, cudaStream_t s);
+cudaError_t launch_ep_slots(const EpSlotsArgs& a, cudaStream_t s);
 size_t ep_layout(int world, int cap, int H, int k, int T_max, size_t* off);
 int ep_error_flag();
 cudaError_t launch_to_f16p(const uint16_t* x, long long n, uint16_t* y, cudaStream_t s);

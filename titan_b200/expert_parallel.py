@@ -263,7 +263,12 @@ class PeerExchange:
                 self._opened.append(p.value)
                 peers.append(p.value)
         self.peers = torch.tensor(peers, dtype=torch.int64, device=self.device)
-        self.tickets = torch.zeros(2, dtype=torch.int32, device=self.device)
+        W, k = self.world, self.top_k
+        self.counters = torch.zeros(W + 1, dtype=torch.int32, device=self.device)
+        self.rows_in = torch.zeros(W, dtype=torch.int32, device=self.device)
+        self.returned = torch.zeros(W, dtype=torch.int32, device=self.device)
+        self.slot_exp = torch.empty(W * self.cap * k, dtype=torch.int32, device=self.device)
+        self.y_rows = torch.empty(W * self.cap * k, dtype=torch.int64, device=self.device)
         self.epoch = 0
         o = [int(v) for v in self.offsets]
         W, k, H = self.world, self.top_k, self.hidden
@@ -306,7 +311,9 @@ def slot_experts(meta: torch.Tensor, rows_in: torch.Tensor, experts_per_rank: in
     """The slot-form pair list of a PeerExchange's metadata meta [W, cap, k+1]:
     slot j of received row (source s, i) is served here by local expert
     meta[s, i, j] when the row was written this layer (i < rows_in[s]) and
-    that id is one of this rank's experts; -1 otherwise.  int32 [W*cap*k]."""
+    that id is one of this rank's experts; -1 otherwise.  int32 [W*cap*k].
+    The tensor statement of tmoe_ep_slots (tests check one against the
+    other)."""
     W, cap, k1 = meta.shape
     live = torch.arange(cap, dtype=torch.int32, device=meta.device)[None, :] < rows_in[:, None]
     ids = meta[..., :k1 - 1]
@@ -314,17 +321,18 @@ def slot_experts(meta: torch.Tensor, rows_in: torch.Tensor, experts_per_rank: in
     return torch.where(ok, ids, -1).reshape(-1)
 
 
-def return_addresses(meta: torch.Tensor, peers: torch.Tensor, ret_offset: int,
-                     hidden: int) -> torch.Tensor:
+def return_addresses(meta: torch.Tensor, slot_exp: torch.Tensor, peers: torch.Tensor,
+                     ret_offset: int, hidden: int) -> torch.Tensor:
     """Where the output of slot j of received row (s, i) goes: the ret row
     token*k + j of source s's buffer (peers [W] int64 base addresses), token =
-    meta[s, i, k].  int64 [W*cap*k]; entries of unserved slots are never
-    used."""
+    meta[s, i, k]; 0 for a slot not served (slot_exp -1).  int64 [W*cap*k].
+    With slot_experts, the tensor statement of tmoe_ep_slots."""
     W, cap, k1 = meta.shape
     k = k1 - 1
     tok = meta[..., k].long()
     slot = torch.arange(k, dtype=torch.int64, device=meta.device)
-    return (peers[:, None, None] + ret_offset + (tok[..., None] * k + slot) * (2 * hidden)).reshape(-1)
+    addr = (peers[:, None, None] + ret_offset + (tok[..., None] * k + slot) * (2 * hidden)).reshape(-1)
+    return torch.where(slot_exp >= 0, addr, 0)
 
 
 def peer_forward(x: torch.Tensor, idx: torch.Tensor, ex: PeerExchange, experts_per_rank: int,
@@ -349,27 +357,21 @@ def peer_forward(x: torch.Tensor, idx: torch.Tensor, ex: PeerExchange, experts_p
     stream = ops.stream_ptr(x.device)
     ex.epoch += 1
     ep = ex.epoch
-    dest, member = _membership(idx, experts_per_rank, W)
-    pos = (torch.cumsum(member.to(torch.int32), 0, dtype=torch.int32) - 1).t().contiguous()
-    counts = member.sum(0, dtype=torch.int32)
-    _mark(marks, "plan")
     _lib.check(lib.tmoe_ep_dispatch(x.data_ptr(), idx.data_ptr(), T, k, H, experts_per_rank, W,
-                                    rank, pos.data_ptr(), counts.data_ptr(), ex.peers.data_ptr(),
-                                    ex.offsets, cap, ep, ex.tickets.data_ptr(), stream),
-               "tmoe_ep_dispatch")
-    rows_in = torch.empty(W, dtype=torch.int32, device=x.device)
-    _lib.check(lib.tmoe_ep_wait(ex.ptr, ex.offsets, 0, W, ep, rows_in.data_ptr(), stream),
+                                    rank, ex.peers.data_ptr(), ex.offsets, cap, ep,
+                                    ex.counters.data_ptr(), stream), "tmoe_ep_dispatch")
+    _lib.check(lib.tmoe_ep_wait(ex.ptr, ex.offsets, 0, W, ep, ex.rows_in.data_ptr(), stream),
                "tmoe_ep_wait")
     _mark(marks, "dispatch")
-    slot_exp = slot_experts(ex.meta, rows_in, experts_per_rank)
-    y_addr = return_addresses(ex.meta, ex.peers, ex.ret_offset, H)
+    _lib.check(lib.tmoe_ep_slots(ex.ptr, ex.offsets, ex.rows_in.data_ptr(), W, cap, k,
+                                 experts_per_rank, H, ex.peers.data_ptr(), ex.slot_exp.data_ptr(),
+                                 ex.y_rows.data_ptr(), stream), "tmoe_ep_slots")
     _mark(marks, "slots")
-    expert_fn(ex.rows, slot_exp, y_addr)
+    expert_fn(ex.rows, ex.slot_exp, ex.y_rows)
     _lib.check(lib.tmoe_ep_post(1, None, W, rank, ex.peers.data_ptr(), ex.offsets, ep, stream),
                "tmoe_ep_post")
     _mark(marks, "experts+return")
-    got = torch.empty(W, dtype=torch.int32, device=x.device)
-    _lib.check(lib.tmoe_ep_wait(ex.ptr, ex.offsets, 1, W, ep, got.data_ptr(), stream),
+    _lib.check(lib.tmoe_ep_wait(ex.ptr, ex.offsets, 1, W, ep, ex.returned.data_ptr(), stream),
                "tmoe_ep_wait")
     _mark(marks, "wait")
     y = combine_fn(ex.ret[:T * k], ex.arange(T * k))
