@@ -64,6 +64,9 @@ def parse():
                          "parallelism over the N ranks (strong scaling)")
     ap.add_argument("--ep-tokens", type=int, default=8192, help="ep: global tokens per step")
     ap.add_argument("--ep-layers", type=int, default=36, help="ep: layers per step")
+    ap.add_argument("--ep-placement", choices=("balanced", "contiguous"), default="balanced",
+                    help="ep: balanced = experts placed by load measured on a separate "
+                         "calibration batch (balanced_placement); contiguous = E/N in order")
     ap.add_argument("--ep-exchange", choices=("peer", "nccl"), default="peer",
                     help="ep: peer = NVLink stores into IPC-mapped buffers with the return "
                          "fused into the down GEMM; nccl = two all-to-alls per layer")
@@ -466,7 +469,22 @@ def _run_ep(args, world, rank, local, device):
         blk = SparseMoeBlock(c["H"], c["E"], c["k"], c["I"], c["Is"], device=device,
                              weight_std=0.02)
         zipf_router_(blk, torch.Generator().manual_seed(777 + l))
-        layers.append(ExpertParallelMoE(blk, exchange=ex))
+        placement = None
+        if args.ep_placement == "balanced":
+            # expert load from a calibration batch (other tokens than the
+            # timed ones), summed over the ranks
+            from titan_b200 import ops as _ops
+            from titan_b200.expert_parallel import balanced_placement
+            gc = torch.Generator(device=device).manual_seed(7000 + 97 * l + rank)
+            xc = torch.randn(T, c["H"], generator=gc, device=device)
+            xc[:, 0] = 1.0
+            ic, _ = _ops.router_topk(xc.to(torch.bfloat16), blk.gate_weight, c["k"])
+            load = torch.bincount(ic.reshape(-1).long(), minlength=c["E"]).to(torch.int64)
+            if world > 1:
+                import torch.distributed as dist
+                dist.all_reduce(load)
+            placement = balanced_placement(load.cpu().tolist(), world)
+        layers.append(ExpertParallelMoE(blk, exchange=ex, placement=placement))
         del blk
     torch.cuda.empty_cache()
     gen = torch.Generator(device=device).manual_seed(9000 + rank)
@@ -533,6 +551,9 @@ def _run_ep(args, world, rank, local, device):
                                "Zipf(1.1) expert popularity",
                    "tokens_per_rank": T, "experts_per_rank": c["E"] // world,
                    "parallelism": f"ep{world}",
+                   "placement": ("experts placed by the load of a separate calibration batch "
+                                 "(balanced_placement)" if args.ep_placement == "balanced"
+                                 else "contiguous E/N per rank"),
                    "collective": ("2 NCCL all-to-alls per layer" if ex is None else
                                   "NVLink stores into CUDA-IPC-mapped peer buffers, epoch "
                                   "flags, return stored by the down GEMM's epilogue, no host "

@@ -12,8 +12,9 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from titan_b200.expert_parallel import (_membership, pairs_from_meta, plan_dispatch,
-                                        return_addresses, return_slots, slot_experts)
+from titan_b200.expert_parallel import (_membership, balanced_placement, pairs_from_meta,
+                                        plan_dispatch, return_addresses, return_slots,
+                                        slot_experts)
 
 H, E, K = 64, 8, 3
 
@@ -134,7 +135,20 @@ def test_peer_exchange_host_plan(world):
     assert sorted(served) == [(s, i) for s in range(world) for i in range(tokens[s] * K)]
 
 
-def _worker(rank, world, port, tokens, q):
+def test_balanced_placement():
+    world, E = 4, 16
+    load = [100, 90, 1, 1, 80, 2, 3, 70, 1, 1, 60, 5, 1, 50, 1, 4]
+    perm = balanced_placement(load, world)
+    assert sorted(perm) == list(range(E))
+    per_rank = [sum(load[e] for e in perm[r * 4:(r + 1) * 4]) for r in range(world)]
+    contiguous = [sum(load[r * 4:(r + 1) * 4]) for r in range(world)]
+    assert max(per_rank) - min(per_rank) <= max(load)
+    assert max(per_rank) < max(contiguous)
+    with pytest.raises(ValueError):
+        balanced_placement(load[:15], world)
+
+
+def _worker(rank, world, port, tokens, q, placed=False):
     import torch.distributed as dist
     from titan_b200.expert_parallel import ep_forward
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -145,15 +159,22 @@ def _worker(rank, world, port, tokens, q):
         mats = _expert_mats()
         x, idx, sc = _routing(tokens[rank], seed=100 + rank)
 
+        # with a placement, rank r holds experts perm[r*epr:(r+1)*epr] and the
+        # ids travel as places (as ExpertParallelMoE maps them)
+        perm = balanced_placement(list(range(E, 0, -1)), world) if placed else list(range(E))
+        place = torch.empty(E, dtype=torch.int32)
+        place[torch.tensor(perm)] = torch.arange(E, dtype=torch.int32)
+
         def expert_fn(rows, pair_row, pair_exp):
             out = torch.empty(pair_row.numel(), H, dtype=torch.bfloat16)
             for p in range(pair_row.numel()):
-                e = rank * epr + int(pair_exp[p])
+                e = perm[rank * epr + int(pair_exp[p])]
                 out[p] = _expert_out(mats, e, rows[int(pair_row[p]):int(pair_row[p]) + 1])[0]
             return out
 
         for _ in range(2):                       # two layers in a row on one group
-            y = ep_forward(x, idx, epr, expert_fn, lambda ys, inv: _combine(ys, inv, sc))
+            y = ep_forward(x, place[idx.long()], epr, expert_fn,
+                           lambda ys, inv: _combine(ys, inv, sc))
         T = x.shape[0]
         ys_full = torch.empty(T * K, H, dtype=torch.bfloat16)
         for t in range(T):
@@ -167,13 +188,15 @@ def _worker(rank, world, port, tokens, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("tokens", [(7, 5), (6, 0)], ids=["both", "one_rank_empty"])
-def test_ep_forward_two_gloo_ranks(tokens):
+@pytest.mark.parametrize("tokens,placed", [((7, 5), False), ((6, 0), False), ((7, 5), True)],
+                         ids=["both", "one_rank_empty", "placed"])
+def test_ep_forward_two_gloo_ranks(tokens, placed):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, tokens, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, tokens, q, placed))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=240) for _ in range(world)]

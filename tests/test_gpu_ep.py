@@ -97,6 +97,12 @@ def test_ep_peer_single_rank_matches_block(cuda, oracle):
                 assert torch.equal(y.view(torch.int16), yb.view(torch.int16)), T
         y = eps[1](bf(oracle.make_x(0, SHAPE["H"], seed=1)), options=_opts(1))
         assert y.shape == (0, SHAPE["H"])
+        # a placement permutes the experts (here reversed) without changing a bit
+        placed = ExpertParallelMoE(blk, exchange=ex, placement=list(range(SHAPE["E"]))[::-1])
+        for T in (150, 3):
+            x = oracle.make_x(T, SHAPE["H"], seed=40 + T)
+            y = placed(bf(x), options=_opts(1))
+            assert torch.equal(y.view(torch.int16), blk(bf(x), options=_opts(1)).view(torch.int16))
         x = oracle.make_x(150, SHAPE["H"], seed=5)
         y = ExpertParallelMoE(blk, exchange=ex)(bf(x), options=_opts(1))
         torch.cuda.synchronize()
@@ -223,6 +229,11 @@ def _worker(rank, world, port, layer_arrays, T, q):
             for i in range(3):                         # the exchange reused call after call
                 y = nbf(ep(bf(x, dev=dev), options=_opts(1)))
                 out[f"{tag}_{i}"] = (y, yb, ry, ops)
+            # experts interleaved over the ranks by a placement
+            E = shape["E"]
+            ep = ExpertParallelMoE(blk, exchange=ex,
+                                   placement=[e for r in range(world) for e in range(r, E, world)])
+            out[f"{tag}_placed"] = (nbf(ep(bf(x, dev=dev), options=_opts(1))), yb, ry, ops)
         if ex is not None:
             from titan_b200 import _lib
             out["status"] = int(_lib.load().tmoe_device_status())

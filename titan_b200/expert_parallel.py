@@ -51,7 +51,7 @@ import torch.distributed as dist
 from . import _lib, ops
 
 __all__ = ["DispatchPlan", "plan_dispatch", "pairs_from_meta", "return_slots",
-           "ExpertParallelMoE", "PeerExchange", "ep_forward"]
+           "ExpertParallelMoE", "PeerExchange", "balanced_placement", "ep_forward"]
 
 
 @dataclass
@@ -379,12 +379,39 @@ def peer_forward(x: torch.Tensor, idx: torch.Tensor, ex: PeerExchange, experts_p
     return y
 
 
+def balanced_placement(load, world: int) -> list[int]:
+    """An expert placement for ``world`` ranks from per-expert load (token
+    counts, say): longest-processing-time greedy, the most loaded expert
+    first onto the rank with the least load that still has a free place, E/W
+    places per rank.  Returns perm: rank r holds experts perm[r*E/W:(r+1)*E/W]
+    in that order."""
+    load = [float(v) for v in load]
+    E = len(load)
+    if E % world:
+        raise _lib.InvalidArgument(f"{E} experts do not split over {world} ranks")
+    epr = E // world
+    order = sorted(range(E), key=lambda e: (-load[e], e))
+    total = [0.0] * world
+    places: list[list[int]] = [[] for _ in range(world)]
+    for e in order:
+        r = min((r for r in range(world) if len(places[r]) < epr), key=lambda r: (total[r], r))
+        places[r].append(e)
+        total[r] += load[e]
+    return [e for r in range(world) for e in sorted(places[r])]
+
+
 class ExpertParallelMoE(torch.nn.Module):
     """A SparseMoeBlock sharded over the ranks of ``group``: this rank holds
-    experts [rank * E/W, (rank+1) * E/W) and a full copy of the router and the
-    shared expert; the constructor slices them out of a full block."""
+    E/W routed experts and a full copy of the router and the shared expert;
+    the constructor slices them out of a full block.  Without a placement
+    rank r holds experts [r*E/W, (r+1)*E/W); with one (a permutation of the
+    experts, e.g. from balanced_placement, the same on every rank) it holds
+    placement[r*E/W:(r+1)*E/W], and the router's expert ids are mapped to
+    their places before the exchanges (one gather; the outputs keep every
+    bit, since a slot's expert and the slot order are unchanged)."""
 
-    def __init__(self, block, group=None, exchange: PeerExchange | None = None):
+    def __init__(self, block, group=None, exchange: PeerExchange | None = None,
+                 placement=None):
         super().__init__()
         self.group = group
         self.exchange = exchange
@@ -398,11 +425,23 @@ class ExpertParallelMoE(torch.nn.Module):
         self.moe_inter = block.moe_inter
         lo, hi = rank * self.epr, (rank + 1) * self.epr
         sm = block.switch_mlp
+        dev = block.gate_weight.device
+        self.place = None
+        if placement is not None:
+            perm = torch.as_tensor(list(placement), dtype=torch.int64)
+            if perm.numel() != E or not torch.equal(perm.sort().values, torch.arange(E)):
+                raise _lib.InvalidArgument("placement must be a permutation of the experts")
+            place = torch.empty(E, dtype=torch.int32)
+            place[perm] = torch.arange(E, dtype=torch.int32)
+            self.place = place.to(dev)                  # expert -> its place
+            mine = perm[lo:hi].to(dev)
+        else:
+            mine = torch.arange(lo, hi, device=dev)
         self.gate_weight = block.gate_weight
-        self.gu = (sm.gate_up_proj.weight[lo:hi].contiguous(), sm.gate_up_proj.scales[lo:hi].contiguous(),
-                   sm.gate_up_proj.biases[lo:hi].contiguous())
-        self.dn = (sm.down_proj.weight[lo:hi].contiguous(), sm.down_proj.scales[lo:hi].contiguous(),
-                   sm.down_proj.biases[lo:hi].contiguous())
+        self.gu = tuple(t.index_select(0, mine.to(t.device)).contiguous() for t in
+                        (sm.gate_up_proj.weight, sm.gate_up_proj.scales, sm.gate_up_proj.biases))
+        self.dn = tuple(t.index_select(0, mine.to(t.device)).contiguous() for t in
+                        (sm.down_proj.weight, sm.down_proj.scales, sm.down_proj.biases))
         self.tables = (ops.build_tables(*self.gu), ops.build_tables(*self.dn))
         self.shared_expert = block.shared_expert
         self.shared_gate = block.shared_expert_gate_weight
@@ -525,6 +564,8 @@ class ExpertParallelMoE(torch.nn.Module):
         xf = x.reshape(-1, self.hidden).contiguous()
         _mark(marks, "start")
         idx, scores, shared_out, gate_logit = self.local(xf, options)
+        if self.place is not None and idx.numel():
+            idx = self.place[idx.long()]
         _mark(marks, "local")
         mode = options.wsum_mode if options is not None else 0
         experts = lambda *a: self.experts(*a, options=options)  # noqa: E731
