@@ -1,9 +1,12 @@
 """Expert parallelism on GPUs: the token-local part (router, top-k, shared
 expert: tmoe_moe_local), the routed experts of a rank on received rows
-(tmoe_moe_experts), the NCCL exchanges and the block's weighted sum
-(tmoe_moe_combine), through ExpertParallelMoE.  The layer must equal the
-single-GPU block bit for bit on the int8 path, with and without a shared
-expert, and stay within the north-star tolerance of the oracle."""
+(tmoe_moe_experts, or tmoe_moe_experts_slots storing into the sources'
+buffers), both transports (NCCL exchanges; peer-memory dispatch, slot list,
+flags and bounded waits) and the block's weighted sum (tmoe_moe_combine),
+through ExpertParallelMoE, with and without an expert placement.  The layer
+must equal the single-GPU block bit for bit on the int8 path, with and
+without a shared expert, and stay within the north-star tolerance of the
+oracle."""
 import os
 import socket
 
