@@ -345,6 +345,20 @@ int tmoe_ep_slots(const void* own, const size_t* offsets, const int32_t* rows_in
 int tmoe_ep_post(int which, const int32_t* counts, int world, int rank, void* const* peers,
                  const size_t* offsets, int epoch, void* stream);
 
+/* The owner side of the return with failure propagation: as tmoe_ep_post(1,
+ * NULL, ...), except that the count posted to every source is -1 when any
+ * entry of rows_in [world] (the dispatch counts tmoe_ep_wait wrote) is
+ * negative, i.e. when a dispatch wait of this layer gave up and this rank's
+ * experts could not serve every row. */
+int tmoe_ep_post_return(const int32_t* rows_in, int world, int rank, void* const* peers,
+                        const size_t* offsets, int epoch, void* stream);
+
+/* The source side after tmoe_moe_combine: when any of counts [world] (the
+ * return counts tmoe_ep_wait wrote) is negative, the layer's output is not
+ * valid; the call then records the error that tmoe_device_status reports and
+ * overwrites y [n] (bf16) with NaN.  Otherwise it changes nothing. */
+int tmoe_ep_guard(const int32_t* counts, int world, uint16_t* y, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

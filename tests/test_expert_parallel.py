@@ -205,3 +205,62 @@ def test_ep_forward_two_gloo_ranks(tokens, placed):
     for rank, ok, shape in sorted(results):
         assert ok is True, f"rank {rank}: {ok}"
         assert shape == (tokens[rank], H)
+
+
+def _skipping_worker(rank, world, port, q):
+    """Rank 1 leaves before the layer's exchange (its post never comes); rank
+    0 must get an error from its exchange within the process group's short
+    timeout, not hang and not return a result."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+    from titan_b200.expert_parallel import ep_forward
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    try:
+        epr = E // world
+        mats = _expert_mats()
+        x, idx, sc = _routing(6, seed=300 + rank)
+        if rank == 1:
+            time.sleep(8)                          # never joins the exchange
+            q.put((rank, "skipped"))
+            return
+
+        def expert_fn(rows, pair_row, pair_exp):
+            out = torch.empty(pair_row.numel(), H, dtype=torch.bfloat16)
+            for p in range(pair_row.numel()):
+                out[p] = _expert_out(mats, rank * epr + int(pair_exp[p]),
+                                     rows[int(pair_row[p]):int(pair_row[p]) + 1])[0]
+            return out
+
+        t0 = time.monotonic()
+        try:
+            ep_forward(x, idx, epr, expert_fn, lambda ys, inv: _combine(ys, inv, sc))
+            q.put((rank, "returned a result"))
+        except Exception as exc:                   # the expected outcome
+            q.put((rank, f"raised after {time.monotonic() - t0:.1f}s: {type(exc).__name__}"))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_ep_forward_peer_that_never_posts_raises():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_skipping_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert results[1] == "skipped"
+    assert results[0].startswith("raised"), results[0]

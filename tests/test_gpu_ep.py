@@ -168,6 +168,21 @@ def _timeout_child(q):
         _lib.check(lib.tmoe_ep_wait(ptr, offs, 0, world, 5, counts.data_ptr(), None))
         torch.cuda.synchronize()
         got = counts.tolist()
+        # an owner whose dispatch wait gave up passes count -1 on with its
+        # return post; the source's wait reads it and the guard NaN-fills y
+        peers = torch.tensor([ptr.value], dtype=torch.int64, device="cuda")
+        rows_in = torch.tensor([-1], dtype=torch.int32, device="cuda")
+        _lib.check(lib.tmoe_ep_post_return(rows_in.data_ptr(), 1, 0, peers.data_ptr(), offs, 6,
+                                           None))
+        ret = torch.full((1,), 7, dtype=torch.int32, device="cuda")
+        _lib.check(lib.tmoe_ep_wait(ptr, offs, 1, 1, 6, ret.data_ptr(), None))
+        y = torch.ones(4, 1024, dtype=torch.bfloat16, device="cuda")
+        _lib.check(lib.tmoe_ep_guard(ret.data_ptr(), 1, y.data_ptr(), y.numel(), None))
+        ok = torch.zeros(1, dtype=torch.int32, device="cuda")
+        y2 = torch.ones(4, 1024, dtype=torch.bfloat16, device="cuda")
+        _lib.check(lib.tmoe_ep_guard(ok.data_ptr(), 1, y2.data_ptr(), y2.numel(), None))
+        torch.cuda.synchronize()
+        got = (got, ret.tolist(), bool(torch.isnan(y).all()), bool((y2 == 1).all()))
         status = int(lib.tmoe_device_status())
         _lib.check(lib.tmoe_ep_free(ptr))
         q.put((got, status, None))
@@ -178,7 +193,9 @@ def _timeout_child(q):
 def test_ep_wait_gives_up_and_reports(cuda):
     """A flag that nothing sets: the wait kernel gives up after its bounded
     time, writes count -1, the context stays usable, and tmoe_device_status
-    reports TMOE_ERR_TIMEOUT (5).  In a child process: the error is sticky
+    reports TMOE_ERR_TIMEOUT (5).  A failed dispatch wait is carried into the
+    return (tmoe_ep_post_return posts -1) and the source's guard turns the
+    layer output into NaN.  In a child process: the error is sticky
     for the life of the library."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -187,7 +204,11 @@ def test_ep_wait_gives_up_and_reports(cuda):
     got, status, err = q.get(timeout=300)
     p.join(timeout=60)
     assert err is None, err
-    assert got == [-1, -1]
+    counts, ret, y_nan, y_kept = got
+    assert counts == [-1, -1]
+    assert ret == [-1], "a poisoned return post must read as count -1"
+    assert y_nan, "the guard must NaN-fill the output of a failed layer"
+    assert y_kept, "the guard must leave a valid layer's output alone"
     assert status == 5
 
 

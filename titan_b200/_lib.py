@@ -125,6 +125,8 @@ _SIGS = {
     "tmoe_ep_slots": ([P, P, P, I32, I32, I32, I32, I32, P, P, P, P], I32),
     "tmoe_ep_wait": ([P, P, I32, I32, I32, P, P], I32),
     "tmoe_ep_post": ([I32, P, I32, I32, P, P, I32, P], I32),
+    "tmoe_ep_post_return": ([P, I32, I32, P, P, I32, P], I32),
+    "tmoe_ep_guard": ([P, I32, P, I64, P], I32),
 }
 
 EXPORTED = tuple(_SIGS)

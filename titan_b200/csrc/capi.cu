@@ -1360,6 +1360,30 @@ int tmoe_ep_post(int which, const int32_t* counts, int world, int rank, void* co
   return TMOE_OK;
 }
 
+int tmoe_ep_post_return(const int32_t* rows_in, int world, int rank, void* const* peers,
+                        const size_t* offsets, int epoch, void* stream) {
+  if (!rows_in || world <= 0 || world > 32 || rank < 0 || rank >= world || !peers || !offsets)
+    return fail(TMOE_ERR_INVALID, "tmoe_ep_post_return: bad arguments");
+  EpPostArgs a{};
+  a.poison = rows_in;
+  a.npoison = world;
+  a.peer = peers;
+  a.off_flags = offsets[3];
+  a.which = 1;
+  a.world = world;
+  a.rank = rank;
+  a.epoch = epoch;
+  TMOE_TRY(launch_ep_post(a, S(stream)), "ep_post");
+  return TMOE_OK;
+}
+
+int tmoe_ep_guard(const int32_t* counts, int world, uint16_t* y, int64_t n, void* stream) {
+  if (!counts || world <= 0 || world > 32 || n < 0 || (n > 0 && !y))
+    return fail(TMOE_ERR_INVALID, "tmoe_ep_guard: bad arguments");
+  TMOE_TRY(launch_ep_guard(counts, world, y, (long long)n, S(stream)), "ep_guard");
+  return TMOE_OK;
+}
+
 int tmoe_moe_combine(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
                      int D, int mode, const uint16_t* shared_out, const float* gate_logit,
                      uint16_t* y, void* stream) {

@@ -457,7 +457,7 @@ cudaError_t launch_gemv_stream(int mode, const StreamParams& P, int max_cols, cu
   dim3 grid(nb_x, nb_y);
   cudaError_t err = cudaSuccess;
   auto go = [&](auto kernel) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = ensure_smem_attr((const void*)kernel, smem);
     return e != cudaSuccess ? e : launch_pdl(kernel, grid, dim3(kThreads), (size_t)smem, s, P, ncol);
   };
   if (mode == 0) err = go(gemv_stream_kernel<0>);

@@ -817,24 +817,14 @@ int decode_layer_stages(int T, int H, int E, int k, int I, int Is, int nct) {
   return 0;
 }
 
-int decode_layer_ctas() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 1;
-  }
-  return n;
-}
+int decode_layer_ctas() { return device_sm_count(); }
 
 cudaError_t launch_decode_layer(const LayerArgs& a, int ns, cudaStream_t s) {
   const int nct = decode_layer_ctas();
   const size_t smem = decode_layer_smem(a.T, a.H, a.E, a.k, a.I, a.Is, nct, ns);
   cudaError_t err = cudaSuccess;
   auto go = [&](auto kernel) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = ensure_smem_attr((const void*)kernel, (int)smem);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kLThreads, smem);

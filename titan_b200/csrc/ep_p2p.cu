@@ -71,7 +71,14 @@ __global__ void __launch_bounds__(128) ep_dispatch_kernel(EpDispatchArgs a) {
     const int32_t* ids = a.idx + (size_t)t * k;
     if (tid < W) {
       bool mine = false;
-      for (int j = 0; j < k; ++j) mine |= ids[j] / a.epr == tid;
+      for (int j = 0; j < k; ++j) {
+        const int e = ids[j];
+        if (e < 0 || e >= W * a.epr) {          // no owner: the slot's return row would stay stale
+          if (tid == 0) atomicExch(&g_ep_error, 2);
+          continue;
+        }
+        mine |= e / a.epr == tid;
+      }
       s_row[tid] = mine ? atomicAdd(a.counters + 1 + tid, 1) : -1;
     }
     __syncthreads();
@@ -86,7 +93,7 @@ __global__ void __launch_bounds__(128) ep_dispatch_kernel(EpDispatchArgs a) {
       int32_t* meta = reinterpret_cast<int32_t*>(base + a.off_meta) + row * (k + 1);
       if (tid < k) {
         const int e = ids[tid];
-        meta[tid] = e / a.epr == d ? e - d * a.epr : -1;
+        meta[tid] = (e >= 0 && e / a.epr == d) ? e - d * a.epr : -1;
       } else if (tid == k) {
         meta[k] = t;
       }
@@ -167,12 +174,40 @@ __global__ void ep_post_kernel(EpPostArgs a) {
   __threadfence_system();
   unsigned long long* flags = reinterpret_cast<unsigned long long*>(
       static_cast<uint8_t*>(a.peer[d]) + a.off_flags);
-  const uint32_t n = a.counts ? (uint32_t)a.counts[d] : 0u;
+  uint32_t n = a.counts ? (uint32_t)a.counts[d] : 0u;
+  // a failed wait upstream (a dispatch count of -1) is passed on as count -1,
+  // so the sources' guard sees that this layer's return is not valid
+  for (int i = 0; a.poison && i < a.npoison; ++i)
+    if (a.poison[i] < 0) n = 0xffffffffu;
   st_release_sys64(flags + (size_t)a.which * a.world + a.rank,
                    ((unsigned long long)(uint32_t)a.epoch << 32) | n);
 }
 
+// After the source's combine: when any return count is negative (an owner's
+// wait gave up upstream, or this rank's own return wait did) the layer's
+// output is not valid.  The guard then records the error for
+// tmoe_device_status and overwrites the output with bf16 NaN, so no caller
+// can take it for a result.  Grid-stride over n bf16 values.
+__global__ void ep_guard_kernel(const int32_t* counts, int W, uint16_t* y, long long n) {
+  bool bad = false;
+  for (int s = 0; s < W; ++s) bad |= counts[s] < 0;
+  if (!bad) return;
+  if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(&g_ep_error, 1);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = 0x7fc0u;
+}
+
 }  // namespace
+
+cudaError_t launch_ep_guard(const int32_t* counts, int W, uint16_t* y, long long n,
+                            cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 1184) blocks = 1184;
+  ep_guard_kernel<<<(unsigned)blocks, 256, 0, s>>>(counts, W, y, n);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_ep_dispatch(const EpDispatchArgs& a, cudaStream_t s) {
   ep_dispatch_kernel<<<a.T > 0 ? a.T : 1, 128, 0, s>>>(a);

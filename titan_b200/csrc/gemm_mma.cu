@@ -386,13 +386,8 @@ __global__ void __launch_bounds__(256) gemm_grouped_kernel(GemmParams P) {
 template <bool I8, int EPI>
 static cudaError_t launch_one(const GemmParams& P, int maxt, cudaStream_t s) {
   using C = Cfg<I8>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t err = cudaFuncSetAttribute(gemm_grouped_kernel<I8, EPI>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (err != cudaSuccess) return err;
-    attr = true;
-  }
+  cudaError_t err = ensure_smem_attr((const void*)gemm_grouped_kernel<I8, EPI>, C::SMEM);
+  if (err != cudaSuccess) return err;
   const int gx = (EPI == kEpiStore) ? P.N / 128 : (P.N / 2) / 64;
   dim3 grid(gx, maxt);
   gemm_grouped_kernel<I8, EPI><<<grid, 256, C::SMEM, s>>>(P);

@@ -570,13 +570,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
 
 template <bool I8, int EPI>
 static cudaError_t launch_tc05_one(const GemmParams& P, int maxt, cudaStream_t s) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t err = cudaFuncSetAttribute(gemm_tc05_kernel<I8, EPI>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    if (err != cudaSuccess) return err;
-    attr = true;
-  }
+  cudaError_t err = ensure_smem_attr((const void*)gemm_tc05_kernel<I8, EPI>, SMEM);
+  if (err != cudaSuccess) return err;
   const int gx = (EPI == kEpiStore) ? P.N / BN : (P.N / 2) / 64;
   gemm_tc05_kernel<I8, EPI><<<dim3(gx, maxt), NTHREADS, SMEM, s>>>(P);
   return cudaGetLastError();

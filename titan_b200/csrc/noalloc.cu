@@ -10,7 +10,11 @@
 // Set-up: the first call on each device looks the array up with
 // cudaGetSymbolAddress, with that device current (it is the calling thread's
 // current device).  That lookup may load this library's device module, so
-// make the first call on a device before any stream capture begins.
+// make the first call on a device before any stream capture begins.  The
+// address is cached with the CUDA context it belongs to; after a
+// cudaDeviceReset (a new primary context, into which the module is loaded
+// again) the next call sees a different context and looks the array up anew,
+// so it is again a set-up call that must come before any capture.
 //
 // Sharing: every call on a device uses the same array.  Two calls in flight at
 // once (on two streams, or from two host threads) overwrite each other's
@@ -32,6 +36,25 @@ __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 std::mutex g_setup_mutex;
 void* g_scratch_ptr[kMaxDevices] = {};
+void* g_scratch_ctx[kMaxDevices] = {};   // the context g_scratch_ptr[dev] was looked up in
+
+// The calling thread's current CUDA context (cuCtxGetCurrent through the
+// runtime's driver entry point, so the library needs no libcuda link), or
+// null when it cannot be read.
+void* current_context() {
+  typedef int (*CtxGetCurrent)(void**);
+  static CtxGetCurrent fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<CtxGetCurrent>(f);
+  }();
+  void* ctx = nullptr;
+  if (!fn || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
 
 // Per-device set-up: the scratch array's device address, looked up once.
 int scratch_for_current_device(void** out, char* msg, size_t msg_len) {
@@ -45,8 +68,9 @@ int scratch_for_current_device(void** out, char* msg, size_t msg_len) {
     snprintf(msg, msg_len, "device ordinal %d outside 0..%d", dev, kMaxDevices - 1);
     return TMOE_ERR_UNSUPPORTED;
   }
+  void* ctx = current_context();           // null until the runtime made a context current
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (!g_scratch_ptr[dev]) {
+  if (!g_scratch_ptr[dev] || !ctx || ctx != g_scratch_ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess || !p) {
@@ -55,6 +79,7 @@ int scratch_for_current_device(void** out, char* msg, size_t msg_len) {
       return TMOE_ERR_CUDA;
     }
     g_scratch_ptr[dev] = p;
+    g_scratch_ctx[dev] = current_context();   // the lookup made the primary context current
   }
   *out = g_scratch_ptr[dev];
   return TMOE_OK;

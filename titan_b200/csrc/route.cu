@@ -251,13 +251,6 @@ size_t route_plan_scratch_bytes(int R, int E) {
   return nb * (size_t)E * sizeof(int32_t);
 }
 
-void route_init_attributes() {
-  static bool done = false;
-  if (!done) {
-    cudaFuncSetAttribute(route_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    done = true;
-  }
-}
 
 cudaError_t launch_route_plan(const int32_t* idx, int R, int E, int tile_m, int maxt,
                               const RoutePlan& plan, void* scratch, cudaStream_t s) {
@@ -266,13 +259,15 @@ cudaError_t launch_route_plan(const int32_t* idx, int R, int E, int tile_m, int 
     route_plan_small<<<1, 1024, smem, s>>>(idx, R, E, tile_m, maxt, plan);
     return cudaGetLastError();
   }
-  route_init_attributes();
+  const size_t scatter_smem = sizeof(int32_t) * 32 * (size_t)E;
+  cudaError_t err = ensure_smem_attr((const void*)route_scatter, (int)scatter_smem);
+  if (err != cudaSuccess) return err;
   const int nb = (R + kBlk - 1) / kBlk;
   int32_t* bh = static_cast<int32_t*>(scratch);
   route_hist<<<nb, kBlk, sizeof(int32_t) * E, s>>>(idx, R, E, bh);
   route_scan<<<1, 1024, sizeof(int32_t) * (2 * (size_t)E + 1), s>>>(bh, nb, R, E, tile_m, maxt,
                                                                      plan);
-  route_scatter<<<nb, kBlk, sizeof(int32_t) * 32 * (size_t)E, s>>>(idx, R, E, bh, plan);
+  route_scatter<<<nb, kBlk, scatter_smem, s>>>(idx, R, E, bh, plan);
   return cudaGetLastError();
 }
 
@@ -487,8 +482,7 @@ cudaError_t launch_decode_route(const uint16_t* x, const uint16_t* wr, const uin
   cudaError_t err = cudaSuccess;
 #define TMOE_DR(P)                                                                              \
   do {                                                                                          \
-    err = cudaFuncSetAttribute(decode_route_kernel<P>,                                          \
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);         \
+    err = ensure_smem_attr((const void*)decode_route_kernel<P>, (int)smem);                     \
     if (err == cudaSuccess)                                                                     \
       err = launch_pdl(decode_route_kernel<P>, dim3(grid), dim3(128), smem, s, x, wr, wg, T, H, \
                        E, k, logits, gate_logit, idx, scores, plan, counters, ncounters);       \

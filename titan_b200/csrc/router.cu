@@ -251,13 +251,8 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const ui
   const int nrows = E + (wg ? 1 : 0);
   if (T <= 32) {
     const size_t smem = (size_t)(4 + kGemvTok) * H * 2;
-    static int attr_h = 0;
-    if (smem > 48 * 1024 && attr_h < H) {
-      cudaError_t e = cudaFuncSetAttribute(router_logits_gemv,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      attr_h = H;
-    }
+    cudaError_t e = ensure_smem_attr((const void*)router_logits_gemv, (int)smem);
+    if (e != cudaSuccess) return e;
     router_logits_gemv<<<(nrows + 3) / 4, 32, smem, s>>>(x, wr, wg, T, H, E, logits, gate_logit);
   } else {
     dim3 grid((T + 63) / 64, (nrows + 31) / 32);

@@ -174,6 +174,8 @@ struct EpSlotsArgs {
 };
 struct EpPostArgs {
   const int32_t* counts;   // [world] or null (count 0)
+  const int32_t* poison;   // [npoison] or null: any negative entry posts count -1
+  int npoison;
   void* const* peer;
   size_t off_flags;
   int which, world, rank, epoch;
@@ -183,6 +185,7 @@ cudaError_t launch_ep_wait(const unsigned long long* flags, int W, int epoch, in
                            cudaStream_t s);
 cudaError_t launch_ep_post(const EpPostArgs& a, cudaStream_t s);
 cudaError_t launch_ep_slots(const EpSlotsArgs& a, cudaStream_t s);
+cudaError_t launch_ep_guard(const int32_t* counts, int W, uint16_t* y, long long n, cudaStream_t s);
 size_t ep_layout(int world, int cap, int H, int k, int T_max, size_t* off);
 int ep_error_flag();
 cudaError_t launch_to_f16p(const uint16_t* x, long long n, uint16_t* y, cudaStream_t s);
@@ -199,6 +202,12 @@ cudaError_t launch_prepare_tables(const uint16_t* scales, const uint16_t* biases
 cudaError_t launch_qsum(const uint32_t* w, int E, int N, int K, uint16_t* qsum, cudaStream_t s);
 cudaError_t launch_dense_tiles(int R, int tile_m, int32_t* tile_row, int32_t* tile_exp,
                                int32_t* ntiles, int32_t* offsets, cudaStream_t s);
+
+// Raises `func`'s dynamic shared-memory limit to `bytes` on the current
+// device, once per (kernel, device); thread-safe (host_util.cu).
+cudaError_t ensure_smem_attr(const void* func, int bytes);
+// SMs of the current device, cached per device; thread-safe.
+int device_sm_count();
 
 // Records `msg` as this thread's tmoe_last_error() text and returns `code`.
 int record_error(int code, const char* msg);

@@ -344,8 +344,10 @@ def peer_forward(x: torch.Tensor, idx: torch.Tensor, ex: PeerExchange, experts_p
     expert_fn(rows, slot_exp, y_addr) applies this rank's experts to the
     served slots of the received rows and stores slot f's output at address
     y_addr[f] (the sources' ret rows; tmoe_moe_experts_slots).  A wait that
-    gives up leaves the layer's output undefined and is reported by
-    :meth:`PeerExchange.check` (tmoe_device_status)."""
+    gives up anywhere in the layer (an owner's dispatch wait is passed on as
+    a return count of -1) turns this rank's output into NaN, and
+    :meth:`PeerExchange.check` (tmoe_device_status) raises DeviceTimeout;
+    callers check at their step boundary."""
     W, rank, cap = ex.world, ex.rank, ex.cap
     T, k = idx.shape
     H = x.shape[1]
@@ -368,13 +370,18 @@ def peer_forward(x: torch.Tensor, idx: torch.Tensor, ex: PeerExchange, experts_p
                                  ex.y_rows.data_ptr(), stream), "tmoe_ep_slots")
     _mark(marks, "slots")
     expert_fn(ex.rows, ex.slot_exp, ex.y_rows)
-    _lib.check(lib.tmoe_ep_post(1, None, W, rank, ex.peers.data_ptr(), ex.offsets, ep, stream),
-               "tmoe_ep_post")
+    # count -1 to every source when a dispatch wait above gave up
+    _lib.check(lib.tmoe_ep_post_return(ex.rows_in.data_ptr(), W, rank, ex.peers.data_ptr(),
+                                       ex.offsets, ep, stream), "tmoe_ep_post_return")
     _mark(marks, "experts+return")
     _lib.check(lib.tmoe_ep_wait(ex.ptr, ex.offsets, 1, W, ep, ex.returned.data_ptr(), stream),
                "tmoe_ep_wait")
     _mark(marks, "wait")
     y = combine_fn(ex.ret[:T * k], ex.arange(T * k))
+    # a negative return count (an owner's or this rank's wait gave up): the
+    # output becomes NaN and tmoe_device_status reports the timeout
+    _lib.check(lib.tmoe_ep_guard(ex.returned.data_ptr(), W, y.data_ptr(), y.numel(), stream),
+               "tmoe_ep_guard")
     _mark(marks, "combine")
     return y
 
