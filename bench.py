@@ -1,24 +1,24 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 quantised MoE block (BASELINE.json metric: MoE-layer
-decode µs/layer and prefill tok/s, with % of the HBM / int8 tensor roofline).
+"""Benchmark of the B200 quantised MoE block: MoE-layer prefill tok/s and
+decode µs/layer, each with its roofline fraction.
 
-Headline (N=1 workload): decode of a Qwen3-Next-80B-A3B
-shaped MoE layer — H=2048, 512 routed experts + 1 shared (I=512), top-10,
-int4 g64 affine weights for 48 layers resident in HBM — at T=1 token.  One
-step runs the block of all 48 layers (inputs resident), replayed as one CUDA
-graph; weights of different layers never share L2 (43.5 GB cycled), so every
-step streams the selected experts from HBM.  value = µs per layer.
+Headline (every N, N=1 included): the expert-parallel prefill step — 36 MoE
+layers of the Qwen3-Next-80B-A3B shape (H=2048, 512 routed experts + 1
+shared, I=512, top-10, int4 g64 affine weights, 32.6 GB, so L2 never holds
+them), 8192 tokens per step split over the N ranks, router logits drawn so
+expert popularity follows Zipf(1.1).  Experts are sharded over the ranks by a
+load-balanced placement; tokens travel to their experts' owners and back
+over NVLink peer memory.  value = global tokens per second (strong scaling).
+The same code path runs at N=1 (a one-rank exchange).  Each rank checks a
+token subset of layer 0 bit for bit against the single-GPU block
+(`ep_check`).
 
-Also reported in the same JSON line: the decode sweep T in {1,2,4,8,32}, the
-config-3 prefill (H=3072, 512 experts, I=768, shared 3072, int8 overlay) at
-T=4096 in tok/s and TOP/s, the roofline of the dominant kernel, the e2e
-number through the public API with host<->device copies, the CPU baseline
-(the oracle port on the host cores) and the SM clocks seen while timing.
+At N=1 the same JSON line also carries: the 48-layer decode sweep (T in
+{1,2,4,8,32}) with its HBM roofline and e2e, the cold-prefill block (H=3072,
+512 experts, I=768, shared 3072) at T in {4096, 16384, 65536}, the CPU
+baseline (the oracle on the host cores) and the single-layer CPU timing.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl titan|reference]
-Multi-GPU (torchrun, one rank per GPU): every rank runs its own replica of
-the workload (weak scaling, no collective on the data path); the time is the
-max over ranks.
 """
 from __future__ import annotations
 
@@ -47,11 +47,11 @@ EXPERT_BYTES_CFG2 = 1_769_472      # one expert's int4 weights + bf16 scales/bia
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("titan", "reference"), default="titan")
     ap.add_argument("--layers", type=int, default=48)
-    ap.add_argument("--prefill-T", default="4096", help="comma list; empty to skip")
+    ap.add_argument("--prefill-T", default="4096,16384,65536", help="comma list; empty to skip")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--traffic-file", default=os.path.join(ROOT, "profiles", "traffic.txt"))
@@ -59,9 +59,10 @@ def parse():
                     help="run a small untimed case for an ncu capture and exit")
     ap.add_argument("--gemm-kernel", type=int, default=0,
                     help="prefill grouped GEMMs: 0 tcgen05 (default), 1 mma.sync baseline")
-    ap.add_argument("--workload", choices=("decode", "ep"), default="decode",
-                    help="decode: the headline (replicas at N>1); ep: config 4, expert "
-                         "parallelism over the N ranks (strong scaling)")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="only the expert-parallel headline (no decode / prefill / CPU extras)")
+    ap.add_argument("--ref-tokens", type=int, default=64,
+                    help="tokens per oracle call of the CPU baseline and the reference arm")
     ap.add_argument("--ep-tokens", type=int, default=8192, help="ep: global tokens per step")
     ap.add_argument("--ep-layers", type=int, default=36, help="ep: layers per step")
     ap.add_argument("--ep-placement", choices=("balanced", "contiguous"), default="balanced",
@@ -166,6 +167,16 @@ def measured_peaks():
         d = json.load(open(p))
         return d.get("hbm_gbs"), d.get("bf16_tflops"), "measured"
     return 6650.0, 1590.0, "fallback"
+
+
+def measured_peaks_all():
+    """HBM GB/s and dense bf16 TF/s, burst and sustained (MEASURED_PEAKS.json,
+    else the pool's earlier measurement)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    d = json.load(open(p)) if os.path.exists(p) else {}
+    return {"hbm_gbs": d.get("hbm_gbs", 6650.0), "bf16_tflops": d.get("bf16_tflops", 1590.0),
+            "bf16_tflops_sustained": d.get("bf16_tflops_sustained", 1400.0),
+            "source": "measured" if d else "fallback"}
 
 
 def read_traffic(path):
@@ -359,17 +370,24 @@ def prefill_ops_per_token(c):
 
 
 def bench_prefill(args, world, device):
+    """The cold-prefill block (H=3072, 512 experts, I=768, top-10, shared
+    expert 3072) at each --prefill-T on the default tile-per-CTA kernel, and
+    the swap-AB kernel at the first T: ms, tok/s, TOP/s and the fraction of
+    the measured dense bf16 peak (the kernels issue f16 MMAs; the nominal
+    int8 fraction is given for context)."""
     import torch
     from titan_b200 import SparseMoeBlock, _lib
     Ts = [int(t) for t in args.prefill_T.split(",") if t.strip()]
     if not Ts:
         return {}
+    peaks = measured_peaks_all()
     c = CFG3
     torch.manual_seed(99)
     blk = SparseMoeBlock(c["H"], c["E"], c["k"], c["I"], c["Is"], device=device, weight_std=0.02)
     blk.prepare()
-    out = {}
-    for T, kernel in [(T, kk) for T in Ts for kk in (0, 1)]:
+    out = {"ops_per_token": prefill_ops_per_token(c)}
+    runs = [(T, 0) for T in Ts] + [(Ts[0], 2)]
+    for T, kernel in runs:
         o = _lib.Options()
         o.min_tokens, o.int8_prefill, o.down_int8, o.wsum_mode = 512, 1, 1, 0
         o.gemm_kernel = kernel
@@ -377,26 +395,31 @@ def bench_prefill(args, world, device):
         for _ in range(max(args.warmup, 3)):
             blk(x, options=o)
         torch.cuda.synchronize()
-        barrier(world)
-        steps = max(3, min(args.steps, 20))
+        steps = max(3, min(args.steps, 10 if T <= 16384 else 4))
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(steps):
             blk(x, options=o)
         b.record()
         torch.cuda.synchronize()
-        barrier(world)
-        ms = max_over_ranks(a.elapsed_time(b) / steps, world)
+        ms = a.elapsed_time(b) / steps
         ops = prefill_ops_per_token(c) * T
-        stages, launches = stage_profile([lambda: blk(x, options=o)], reps=2)
-        out[str(T) if kernel == 0 else f"{T}_mma_sync"] = {
-                       "gemm": "tcgen05" if kernel == 0 else "mma.sync",
-                       "ms": round(ms, 4), "tok_per_s": round(T / (ms * 1e-3), 1),
-                       "TOPs": round(ops / (ms * 1e-3) / 1e12, 2),
-                       "frac_int8_nominal_4500": round(ops / (ms * 1e-3) / 4.5e15, 4),
-                       "gpu_launches": launches,
-                       "stages_us": {k: round(v["us_per_launch"], 2) for k, v in stages.items()}}
+        tops = ops / (ms * 1e-3) / 1e12
+        stages, launches = stage_profile([lambda: blk(x, options=o)], reps=1)
+        key = str(T) if kernel == 0 else f"{T}_swap_ab_kernel"
+        out[key] = {"gemm": "tcgen05 tile-per-CTA" if kernel == 0 else "tcgen05 swap-AB persistent",
+                    "ms": round(ms, 4), "tok_per_s": round(T / (ms * 1e-3), 1),
+                    "TOPs": round(tops, 2),
+                    "frac_of_measured_bf16_peak": round(tops / peaks["bf16_tflops"], 4),
+                    "frac_int8_nominal_4500": round(tops / 4500.0, 4),
+                    "gpu_launches": launches,
+                    "stages_us": {k: round(v["us_per_launch"], 2) for k, v in stages.items()}}
+        gu = stages.get("gemm_gate_up")
+        if gu:
+            fl = 2.0 * T * c["k"] * 2 * c["I"] * c["H"]
+            out[key]["gemm_gate_up_TFLOPs"] = round(fl / (gu["us_per_launch"] * 1e-6) / 1e12, 1)
         del x
+        torch.cuda.empty_cache()
     del blk
     torch.cuda.empty_cache()
     return out
@@ -452,18 +475,25 @@ def run_ep(args, world, rank, local):
 
 
 def _run_ep(args, world, rank, local, device):
+    """Returns the measurement dict of the config-4 expert-parallel step on
+    this rank (the caller prints rank 0's)."""
     import torch
-    from titan_b200 import SparseMoeBlock, _lib
-    from titan_b200.expert_parallel import ExpertParallelMoE
+    from titan_b200 import SparseMoeBlock, _lib, ops
+    from titan_b200.expert_parallel import ExpertParallelMoE, balanced_placement
     c = CFG2
     if args.ep_tokens % world:
         raise SystemExit(f"--ep-tokens {args.ep_tokens} does not split over {world} ranks")
     T = args.ep_tokens // world
+    epr = c["E"] // world
     ex = None
     if args.ep_exchange == "peer":
         from titan_b200.expert_parallel import PeerExchange
         ex = PeerExchange(T, c["H"], c["k"], device=device)
-    layers = []
+    gen = torch.Generator(device=device).manual_seed(9000 + rank)
+    x = torch.randn(T, c["H"], generator=gen, device=device)
+    x[:, 0] = 1.0
+    x = x.to(torch.bfloat16)
+    layers, full0, pairs_r0 = [], None, []
     for l in range(args.ep_layers):
         torch.manual_seed(4321 + l)
         blk = SparseMoeBlock(c["H"], c["E"], c["k"], c["I"], c["Is"], device=device,
@@ -473,30 +503,34 @@ def _run_ep(args, world, rank, local, device):
         if args.ep_placement == "balanced":
             # expert load from a calibration batch (other tokens than the
             # timed ones), summed over the ranks
-            from titan_b200 import ops as _ops
-            from titan_b200.expert_parallel import balanced_placement
             gc = torch.Generator(device=device).manual_seed(7000 + 97 * l + rank)
             xc = torch.randn(T, c["H"], generator=gc, device=device)
             xc[:, 0] = 1.0
-            ic, _ = _ops.router_topk(xc.to(torch.bfloat16), blk.gate_weight, c["k"])
+            ic, _ = ops.router_topk(xc.to(torch.bfloat16), blk.gate_weight, c["k"])
             load = torch.bincount(ic.reshape(-1).long(), minlength=c["E"]).to(torch.int64)
             if world > 1:
                 import torch.distributed as dist
                 dist.all_reduce(load)
             placement = balanced_placement(load.cpu().tolist(), world)
-        layers.append(ExpertParallelMoE(blk, exchange=ex, placement=placement))
+        ep = ExpertParallelMoE(blk, exchange=ex, placement=placement)
+        layers.append(ep)
+        # pairs each rank's experts serve in this layer (for the GEMM roofline)
+        il, _ = ops.router_topk(x, blk.gate_weight, c["k"])
+        owner = (ep.place[il.long()].long() if ep.place is not None else il.long()) // epr
+        cnt = torch.bincount(owner.reshape(-1), minlength=world).to(torch.int64)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(cnt)
+        pairs_r0.append(int(cnt[0]))
+        if l == 0:
+            full0 = blk                       # the single-GPU block of layer 0, for ep_check
         del blk
     torch.cuda.empty_cache()
-    gen = torch.Generator(device=device).manual_seed(9000 + rank)
-    x = torch.randn(T, c["H"], generator=gen, device=device)
-    x[:, 0] = 1.0
-    x = x.to(torch.bfloat16)
     opts = _lib.Options()
     opts.min_tokens, opts.int8_prefill, opts.down_int8, opts.wsum_mode = 1, 1, 1, 0
-    # routing statistics of layer 0 over this rank's tokens
-    from titan_b200 import ops
     idx, _ = ops.router_topk(x, layers[0].gate_weight, c["k"])
-    dest = (idx.long() // (c["E"] // world))
+    dest = (idx.long() // epr) if layers[0].place is None else \
+        (layers[0].place[idx.long()].long() // epr)
     member = torch.zeros(T, world, dtype=torch.bool, device=device)
     member.scatter_(1, dest, True)
     ranks_per_token = float(member.sum(1).float().mean())
@@ -535,50 +569,107 @@ def _run_ep(args, world, rank, local, device):
         for (_, a0), (name, b0) in zip(marks, marks[1:]):
             phases[name] = phases.get(name, 0.0) + a0.elapsed_time(b0)
     phases = {k: round(1000 * v / len(layers), 1) for k, v in phases.items()}
+    # per-kernel device time of one step (events before every launch, the
+    # queue kept full behind a sleep kernel): the dominant kernel's roofline
+    barrier(world)
+    stages, launches = stage_profile([step], reps=1)
+    barrier(world)
+    I, H, Is = c["I"], c["H"], c["Is"]
+    pairs = sum(pairs_r0) / len(pairs_r0) if rank == 0 else None
+    flops = {"gemm_gate_up": (2.0 * pairs * 2 * I * H) if pairs else None,
+             "gemm_down": (2.0 * pairs * H * I) if pairs else None,
+             "gemm_shared_gate_up": 2.0 * T * 2 * Is * H,
+             "gemm_shared_down": 2.0 * T * H * Is}
+    _, _, peak_src = measured_peaks()
+    peaks = measured_peaks_all()
+    dom = max(stages.items(), key=lambda kv: kv[1]["ms_total"])
+    gemms = {k: v for k, v in stages.items() if flops.get(k)}
+    top = max(gemms.items(), key=lambda kv: kv[1]["ms_total"]) if gemms else None
+    roof = None
+    if top is not None:
+        name, st = top
+        ach = flops[name] / (st["us_per_launch"] * 1e-6) / 1e12
+        pk = peaks["bf16_tflops_sustained"]
+        traffic = read_traffic(args.traffic_file)
+        roof = {"kernel": name, "bound": "tensor", "achieved": round(ach, 1), "peak": pk,
+                "unit": "TFLOP/s", "frac": round(ach / pk, 4),
+                "peak_source": f"{peak_src} bf16 sustained (a kernel timed inside a long step)",
+                "algorithmic_flops_per_launch": flops[name],
+                "us_per_launch": round(st["us_per_launch"], 2),
+                "launches_per_step": st["launches"],
+                "dominant_of_step": dom[0],
+                "traffic": traffic.get(f"{name}_ep"),
+                "note": "f16 MMA per 64-wide group (exact int8 x int4 sums) and the "
+                        "reference's fp32 rescale; flops = 2 x routed pairs of rank 0 x N x K, "
+                        "no padding counted"}
+    # the public API end to end: the step's tokens copied in from pinned host
+    # memory, the last layer's output copied back, every step
+    xh = x.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+
+    def step_e2e():
+        xd = xh.to(device, non_blocking=True)
+        y = None
+        for ep in layers:
+            y = ep(xd, options=opts)
+        yh.copy_(y, non_blocking=True)
+
+    for _ in range(2):
+        step_e2e()
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    a.record()
+    ke = max(3, args.steps // 2)
+    for _ in range(ke):
+        step_e2e()
+    b.record()
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) * 1000 / ke
+    barrier(world)
+    ms_e2e = max_over_ranks(max(a.elapsed_time(b) / ke, wall), world)
+    e2e = {"value": round(args.ep_tokens / (ms_e2e * 1e-3), 1), "unit": "tok/s",
+           "h2d_bytes_per_step": args.ep_tokens * H * 2,
+           "d2h_bytes_per_step": args.ep_tokens * H * 2, "ms_per_step": round(ms_e2e, 4),
+           "api": "ExpertParallelMoE.forward over the layers, pinned host x in, last y out"}
+    # in-run correctness: a token subset of layer 0's expert-parallel output
+    # against the single-GPU block on the same tokens, bit for bit
+    n_chk = min(64, T)
+    y_ep = layers[0](x, options=opts)[:n_chk]
+    y_one = full0(x[:n_chk].contiguous(), options=opts)
+    diff = int((y_ep.view(torch.int16) != y_one.view(torch.int16)).sum())
+    ep_check = {"layer": 0, "tokens": n_chk, "bit_identical": diff == 0, "mismatches": diff,
+                "against": "SparseMoeBlock.forward on one GPU, same tokens and options"}
+    ok = torch.tensor([1 if diff == 0 else 0], device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    ep_check["all_ranks_bit_identical"] = bool(int(ok) == 1)
     if ex is not None:
         ex.check()                    # no device wait gave up
         ex.close()
-    if rank != 0:
-        return 0
-    line = {
-        "metric": "moe_ep_tokens_per_s", "value": round(args.ep_tokens / (ms * 1e-3), 1),
-        "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms, 4), "us_per_layer": round(1000 * ms / args.ep_layers, 2),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "int8 x int4 (tcgen05 f16 exact), f32 acc", "data": "synthetic",
-        "config": {"workload": f"config4 EP: {args.ep_layers} config-2 layers (H=2048, 512+1 "
-                               f"experts, I=512, top-10), {args.ep_tokens} tokens per step, "
-                               "Zipf(1.1) expert popularity",
-                   "tokens_per_rank": T, "experts_per_rank": c["E"] // world,
-                   "parallelism": f"ep{world}",
-                   "placement": ("experts placed by the load of a separate calibration batch "
-                                 "(balanced_placement)" if args.ep_placement == "balanced"
-                                 else "contiguous E/N per rank"),
-                   "collective": ("2 NCCL all-to-alls per layer" if ex is None else
-                                  "NVLink stores into CUDA-IPC-mapped peer buffers, epoch "
-                                  "flags, return stored by the down GEMM's epilogue, no host "
-                                  "sync"),
-                   "l2": f"inputs larger than L2: {args.ep_layers} layers of weights cycled",
-                   "timing": "CUDA events around the step, max over ranks"},
-        "phases_us_per_layer_rank0": phases,
-        "routing": {"ranks_per_token": round(ranks_per_token, 2),
-                    "top10_expert_share": round(top_share, 4)},
-        "clocks": clk.summary(),
-    }
-    print(json.dumps(line), flush=True)
-    return 0
+    del layers, full0
+    torch.cuda.empty_cache()
+    return {"ms": ms, "value": round(args.ep_tokens / (ms * 1e-3), 1), "T_rank": T,
+            "phases": phases, "roofline": roof, "gpu_launches": launches * args.steps,
+            "e2e": e2e, "ep_check": ep_check, "clocks": clk.summary(),
+            "routing": {"ranks_per_token": round(ranks_per_token, 2),
+                        "top10_expert_share": round(top_share, 4),
+                        "pairs_rank0_per_layer": round(pairs, 1) if pairs else None},
+            "stages_us": {k: round(v["us_per_launch"], 1) for k, v in stages.items()}}
 
 
 # -------------------------------------------------------------- CPU baseline
 
 def host_layer(rng, c):
-    """Host-synthesised config-2 layer for the CPU oracle: random int4 words
+    """Host-synthesised layer of shape c for the CPU oracle: random int4 words
     and scales/biases with the magnitudes N(0, 0.02) weights quantise to
     (the oracle's work does not depend on the values)."""
     from oracle import oracle as O
 
     def q(E, N, K):
-        w = rng.integers(0, 2 ** 32, size=(E, N, K // 8), dtype=np.uint64).astype(np.uint32)
+        w = rng.integers(0, 2 ** 31, size=(E, N, K // 8), dtype=np.int32).view(np.uint32)
         s = O.f32_to_bf16(rng.uniform(0.0045, 0.0065, size=(E, N, K // 64)).astype(np.float32))
         b = O.f32_to_bf16((-7.5 * O.bf16_to_f32(s) + rng.normal(0, 1e-3, size=s.shape)).astype(np.float32))
         return w, s, b
@@ -617,25 +708,90 @@ def cpu_baseline(seconds, T=HEADLINE_T, n_layers=2):
                       f"{el:.1f} s (oracle/moe_oracle.c, fp64 sums, OpenMP)"}
 
 
+def cpu_prefill_baseline(seconds, tokens=64, cfg=None, shared=True):
+    """The oracle's prefill semantics (router, int8 routed experts in the
+    reference's fp32 order, SwiGLU, weighted sum, shared expert) on a bounded
+    sample of tokens of one host-synthesised layer: tokens per second on all
+    host cores."""
+    from oracle import oracle as O
+    cfg = cfg or CFG2
+    O.set_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(0)
+    L = host_layer(rng, cfg)
+    if not shared:
+        L.Is = 0
+        L.sgu_w = L.sgu_s = L.sgu_b = L.sdn_w = L.sdn_s = L.sdn_b = L.wg = None
+    x = O.f32_to_bf16(rng.standard_normal((tokens, cfg["H"])).astype(np.float32))
+    O.moe_prefill(L, x, int8_mode=3)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.moe_prefill(L, x, int8_mode=3)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"tok_per_s": round(n * tokens / el, 2), "ms_per_call": round(1000 * el / n, 2),
+            "calls": n, "tokens_per_call": tokens, "seconds": round(el, 2),
+            "cores": O.threads()}
+
+
 # ------------------------------------------------------------------- arms
 
+def ep_config(args, world):
+    """The headline workload's config dict, printed identically by both arms."""
+    c = CFG2
+    return {"workload": f"expert-parallel prefill step: {args.ep_layers} MoE layers of the "
+                        f"80B-A3B decode shape (H={c['H']}, {c['E']} routed + 1 shared expert, "
+                        f"I={c['I']}, top-{c['k']}, int4 g64 affine), {args.ep_tokens} tokens per "
+                        "step split over the ranks, Zipf(1.1) expert popularity",
+            "layers": args.ep_layers, "tokens_per_step": args.ep_tokens,
+            "tokens_per_rank": args.ep_tokens // world, "experts_per_rank": c["E"] // world,
+            "parallelism": f"ep{world}",
+            "placement": ("experts placed by the load of a separate calibration batch "
+                          "(balanced_placement)" if args.ep_placement == "balanced"
+                          else "contiguous E/N per rank"),
+            "collective": ("2 NCCL all-to-alls per layer" if args.ep_exchange == "nccl" else
+                           "NVLink stores into CUDA-IPC-mapped peer buffers, epoch flags, the "
+                           "return stored by the down GEMM's epilogue, no host sync"),
+            "l2": f"inputs larger than L2: {args.ep_layers} layers x 906 MB of expert weights "
+                  "cycled every step",
+            "timing": "CUDA events around the steps, max over ranks"}
+
+
 def run_reference(args, world, rank):
+    """The reference algorithm on the host cores (the CPU oracle: the
+    overlay's int8 x int4 algebra in its fp32 order, MLX's rounding points):
+    each step one bounded sample of the headline workload (tokens through one
+    layer), reported per 36-layer step like the GPU arm."""
     if rank != 0:
         return 0
+    from oracle import oracle as O
+    O.set_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(0)
+    L = host_layer(rng, CFG2)
+    tok = args.ref_tokens
+    x = O.f32_to_bf16(rng.standard_normal((tok, CFG2["H"])).astype(np.float32))
+    for _ in range(max(1, min(args.warmup, 2))):
+        O.moe_prefill(L, x, int8_mode=3)
     t0 = time.perf_counter()
-    cb = cpu_baseline(max(3.0, min(args.cpu_seconds, 20.0)))
-    line = {"metric": "moe_decode_us_per_layer", "value": cb["value"], "unit": "us/layer",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(cb["value"] * args.layers / 1000, 3), "higher_is_better": False,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64-acc (int4 w, bf16 x)",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": "config2 decode T=1 (H=2048, 512+1 experts, I=512, top-10)",
-                       "layers": args.layers, "T": HEADLINE_T},
-            "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": "us/layer", "h2d_bytes_per_step": 0,
+    for _ in range(args.steps):
+        O.moe_prefill(L, x, int8_mode=3)
+    el = time.perf_counter() - t0
+    v = tok * args.steps / el / args.ep_layers
+    sample = (f"{tok} tokens through one host-synthesised layer per step, {args.steps} steps "
+              f"in {el:.1f} s on {O.threads()} threads (oracle/moe_oracle.c, OpenMP), scaled "
+              f"to the {args.ep_layers}-layer step")
+    line = {"metric": "moe_prefill_tokens_per_s", "value": round(v, 3), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1000 * el / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8 x int4, fp32 epilogue (the reference's order)", "data": "synthetic",
+            "impl": "reference", "config": ep_config(args, world),
+            "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": O.threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
-            "note": "CPU restatement of the reference block (MLX is not installable here); "
-                    f"wall {time.perf_counter() - t0:.1f} s"}
+            "note": "CPU restatement of the reference block (MLX is not installable here)"}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -645,71 +801,66 @@ def run_titan(args, world, rank, local):
     from titan_b200 import _lib
     _lib.load()
     device = torch.device("cuda", torch.cuda.current_device())
-    hbm, bf16_tf, peak_src = measured_peaks()
-    blocks = build_decode_layers(args.layers, device, seed=1234 + rank)
-    torch.cuda.synchronize()
-    clk = Clocks(local).__enter__()          # sampled over the timed regions only
-    blocks, opts, sweep, head = bench_decode(args, world, device, blocks)
-    x, ms, us, nbytes = head
-    # per-kernel profile of one headline step (48 layers)
-    stages, launches = stage_profile([lambda b=b: b(x, options=opts) for b in blocks], reps=3)
-    dom = max(stages.items(), key=lambda kv: kv[1]["ms_total"])
-    traffic = read_traffic(args.traffic_file)
-    # algorithmic bytes per launch of the dominant decode kernels
-    c = CFG2
-    uniq = sweep[str(HEADLINE_T)]["unique_experts_mean"]
-    per_launch = {
-        "gemv_gate_up": (uniq + 1) * 2 * c["I"] * (c["H"] // 2 + c["H"] // 64 * 4),
-        "gemv_down": (uniq + 1) * c["H"] * (c["I"] // 2 + c["I"] // 64 * 4),
-        "router_logits": (c["E"] + 1) * c["H"] * 2,
-        "decode_route": (c["E"] + 1) * c["H"] * 2,     # router rows; routing is on-chip
-        # the whole layer: selected + shared experts, router rows, x and y
-        "decode_layer": sweep[str(HEADLINE_T)]["bytes_per_layer"],
-    }
-    name = dom[0]
-    alg = per_launch.get(name)
-    roof = None
-    if alg:
-        ach = alg / (dom[1]["us_per_launch"] * 1e-6) / 1e9
-        roof = {"kernel": name, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm,
-                "unit": "GB/s", "frac": round(ach / hbm, 4), "peak_source": peak_src,
-                "algorithmic_bytes_per_launch": int(alg),
-                "us_per_launch": round(dom[1]["us_per_launch"], 3),
-                "traffic": traffic.get(name)}
-    # per-kernel profile at other batch sizes (one pass over the layers)
-    stages_by_T = {}
-    for Tp in (2, 8):
-        xp = torch.randn(Tp, CFG2["H"], device=device).to(torch.bfloat16)
-        st, _ = stage_profile([lambda b=b: b(xp, options=opts) for b in blocks], reps=1)
-        stages_by_T[str(Tp)] = {k: round(v["us_per_launch"], 3) for k, v in st.items()}
-    e2e = bench_e2e(blocks, opts, HEADLINE_T, max(3, args.steps // 2), args.warmup, world)
-    del blocks
-    torch.cuda.empty_cache()
-    prefill = bench_prefill(args, world, device)
-    clk.__exit__(None, None, None)
-    clocks = clk.summary()
-    cb = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_baseline(args.cpu_seconds)
+    peaks = measured_peaks_all()
+    ep = run_ep(args, world, rank, local)
+    extras, cb = {}, None
+    if world == 1 and not args.headline_only:
+        hbm = peaks["hbm_gbs"]
+        blocks = build_decode_layers(args.layers, device, seed=1234 + rank)
+        torch.cuda.synchronize()
+        clk = Clocks(local).__enter__()
+        blocks, opts, sweep, head = bench_decode(args, world, device, blocks)
+        x, ms, us, nbytes = head
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        extras["decode_config2"] = {
+            "us_per_layer_T1": round(us, 3), "sweep": sweep,
+            "roofline": {"kernel": "decode_layer (the whole layer in one launch)",
+                         "bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4),
+                         "algorithmic_bytes_per_layer": int(nbytes / args.layers),
+                         "source": "CUDA graph of one 48-layer step, CUDA events, per layer"},
+            "e2e": bench_e2e(blocks, opts, HEADLINE_T, max(3, args.steps // 2), args.warmup,
+                             world),
+            "config": "H=2048, 512 routed + 1 shared expert, I=512, top-10, int4 g64, "
+                      f"{args.layers} layers resident in HBM (43.5 GB, larger than L2)"}
+        st1, _ = stage_profile([lambda b=b: b(x, options=opts) for b in blocks], reps=2)
+        extras["decode_config2"]["stages_us_T1"] = {k: round(v["us_per_launch"], 3)
+                                                    for k, v in st1.items()}
+        del blocks
+        torch.cuda.empty_cache()
+        extras["prefill_config3"] = bench_prefill(args, world, device)
+        clk.__exit__(None, None, None)
+        extras["clocks_extras"] = clk.summary()
+        if not args.no_cpu_baseline:
+            r = cpu_prefill_baseline(args.cpu_seconds, tokens=args.ref_tokens)
+            v = r["tok_per_s"] / args.ep_layers
+            cb = {"value": round(v, 3), "unit": "tok/s", "cores": r["cores"], "kind": "port",
+                  "sample": f"{r['calls']} calls of {r['tokens_per_call']} tokens through one "
+                            f"host-synthesised layer in {r['seconds']} s (oracle, fp32 int8 "
+                            f"algebra, OpenMP), scaled to the {args.ep_layers}-layer step"}
+            c1 = dict(H=2048, E=64, k=10, I=512, Is=0)
+            r1 = cpu_prefill_baseline(min(args.cpu_seconds, 8.0), tokens=128, cfg=c1,
+                                      shared=False)
+            extras["cpu_config1"] = {"workload": "single layer T=128, H=2048, 64 experts, "
+                                                 "top-10, I=512, no shared expert",
+                                     "ms_per_layer": r1["ms_per_call"], "cores": r1["cores"],
+                                     "tok_per_s": r1["tok_per_s"]}
     if rank != 0:
         return 0
     line = {
-        "metric": "moe_decode_us_per_layer", "value": round(us, 3), "unit": "us/layer",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f16 mma / f32 acc (int4 weights, bf16 activations)", "data": "synthetic",
-        "config": {"workload": "config2 decode T=1: H=2048, 512 routed + 1 shared expert, "
-                               "I=512, top-10, int4 g64, 48 layers resident in HBM",
-                   "layers": args.layers, "T": HEADLINE_T,
-                   "l2": "inputs larger than L2: 43.5 GB of weights cycled over 48 layers",
-                   "timing": "CUDA graph of one 48-layer step, CUDA events, max over ranks",
-                   "parallelism": f"replicas x{world}"},
-        "roofline": roof, "cpu_baseline": cb, "e2e": e2e, "gpu_launches": launches * args.steps,
-        "clocks": clocks, "decode_sweep": sweep, "prefill_config3": prefill,
-        "decode_stages_us": {k: round(v["us_per_launch"], 3) for k, v in stages.items()},
-        "decode_stages_us_by_T": stages_by_T,
-        "bytes_per_layer": int(nbytes / args.layers),
+        "metric": "moe_prefill_tokens_per_s", "value": ep["value"], "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ep["ms"], 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int8 x int4 (exact per-group f16 tcgen05 MMA), f32 epilogue",
+        "data": "synthetic (seeded weights and tokens; no dataset)",
+        "config": ep_config(args, world),
+        "roofline": ep["roofline"], "cpu_baseline": cb, "e2e": ep["e2e"],
+        "gpu_launches": ep["gpu_launches"], "clocks": ep["clocks"], "ep_check": ep["ep_check"],
+        "phases_us_per_layer_rank0": ep["phases"], "routing": ep["routing"],
+        "stages_us_rank0": ep["stages_us"],
     }
+    line.update(extras)
     print(json.dumps(line), flush=True)
     return 0
 
@@ -757,8 +908,6 @@ def main():
         return run_reference(args, world, rank)
     world, rank, local = dist_setup(args)
     try:
-        if args.workload == "ep":
-            return run_ep(args, world, rank, local)
         return run_titan(args, world, rank, local)
     finally:
         if world > 1:

@@ -37,7 +37,7 @@ enum {
   TMOE_ERR_WORKSPACE = 6    /* workspace missing or smaller than required    */
 };
 
-#define TMOE_ABI_VERSION 3
+#define TMOE_ABI_VERSION 4
 
 int tmoe_abi_version(void);
 const char* tmoe_last_error(void);
@@ -64,6 +64,15 @@ int tmoe_affine_quantize(const float* w, int64_t rows, int K, uint32_t* wq, uint
  * (prepare_weights); the int8 kernel folds b + 8s itself and needs no qsum. */
 int tmoe_prepare_tables(const uint16_t* scales, const uint16_t* biases, int E, int N, int K,
                         uint16_t* scales_t, uint16_t* biases_t, void* stream);
+
+/* Power-of-two row normalisers rs [E, N] fp32 for the swap-AB grouped GEMM:
+ * rs = 2^Ew with max over the row's groups of 8|s| times rs in [2^13, 2^14),
+ * so every scaled nibble (q - 8) s rs of the row is an exact fp16 (for scales
+ * within 2^24 of the row's largest).  Part of the same one-time table build as
+ * tmoe_prepare_tables (titan/kernels/moe_gather_int8.py:227-248,
+ * engine/patches/moe-int8/kernel.py:432-446); scales / biases [E, N, K/64]. */
+int tmoe_prepare_row_scale(const uint16_t* scales, const uint16_t* biases, int E, int N, int K,
+                           float* row_scale, void* stream);
 
 /* Nibble sums qsum [E, K/64, N] uint16 — the reference table of
  * titan/kernels/moe_gather_int8.py:189-202 (titan_i8_qsum), for callers that
@@ -202,6 +211,10 @@ typedef struct tmoe_layer {
   const uint16_t* shared_gate_up_st; const uint16_t* shared_gate_up_bt; /* [H/64, 2Is] */
   const uint16_t* shared_down_st; const uint16_t* shared_down_bt;       /* [Is/64, H] */
   const uint16_t* shared_gate_w;                                 /* [H] bf16 */
+  /* Row normalisers of each projection, from tmoe_prepare_row_scale ([E, N]
+   * fp32; NULL: that projection runs on the per-group kernels). */
+  const float* gate_up_rs; const float* down_rs;
+  const float* shared_gate_up_rs; const float* shared_down_rs;
 } tmoe_layer;
 
 typedef struct tmoe_options {
@@ -213,8 +226,15 @@ typedef struct tmoe_options {
   int wsum_mode;    /* 0 clone, 1 fast */
   int int8_prefill; /* 1: int8 gate_up (the overlay installed); 0: the stock
                        bf16-activation grouped GEMMs for the prefill path */
-  int gemm_kernel;  /* prefill GEMMs: 0 = tcgen05 / TMEM (default),
-                       1 = mma.sync (the comparison baseline) */
+  int gemm_kernel;  /* routed int8 prefill GEMMs: 0 = tile-per-CTA tcgen05
+                       kernel (default), 1 = mma.sync (the comparison
+                       baseline), 2 = persistent swap-AB tcgen05 kernel
+                       (weight rows on the MMA's M side, TMA-fed; needs the
+                       row normalisers).  All three keep the int8 algebra's
+                       re-centred fp32 order bit for bit.  The
+                       bf16-activation GEMMs (stock path, shared expert) run
+                       on the swap-AB kernel whenever the layer carries its
+                       row normalisers. */
   int decode_kernel; /* decode path (T < min_tokens): 0 = the whole layer in
                         one launch where the shape allows it (T <= 4, H, I
                         and Is multiples of 512), else 1 = router, gate_up

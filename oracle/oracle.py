@@ -252,7 +252,7 @@ class Layer:
 
 
 def make_layer(H, E, k, I, Is=0, seed=0, w_std=0.02, router_std=0.02) -> Layer:
-    """Seeded synthetic layer following the BASELINE configs: router bf16
+    """Seeded synthetic layer with the benchmark workloads' distributions: router bf16
     N(0, router_std); expert weights fp32 N(0, w_std) quantised affine int4 g64
     with bf16 scales/biases; shared expert the same; shared gate bf16 N(0, 0.02)."""
     rng = np.random.default_rng(seed)

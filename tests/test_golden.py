@@ -59,7 +59,7 @@ def test_oracle_reproduces_golden_decode(oracle, golden):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("kernel", [0, 1], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("kernel", [0, 2, 1], ids=["tcgen05_tile", "tcgen05_swapab", "mma_sync"])
 def test_cuda_block_matches_golden(cuda, oracle, golden, kernel):
     from gpu_util import bf, load_block, nbf
     from titan_b200 import SparseMoeBlock, _lib

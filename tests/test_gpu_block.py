@@ -9,7 +9,7 @@ Routing indices and scores must match bit-exactly in every case.  Outputs:
     tolerance (2 bf16 ULP or 1e-2 relative, whichever is looser);
   * decode (T < min_tokens): within tolerance of the double-precision golden
     of engine/patches/decode-fusion/test_exact.py:31-50.
-At full BASELINE sizes the oracle is evaluated on a subset of tokens (every
+At full benchmark sizes the oracle is evaluated on a subset of tokens (every
 token's output depends only on its own row), plus size-independent checks.
 """
 import numpy as np
@@ -37,7 +37,8 @@ def _block(oracle, H, E, k, I, Is, seed, cuda):
 
 
 def _opts(min_tokens, int8=1, down_int8=1, wsum=0, kernel=0, decode_kernel=0):
-    """kernel 0 = tcgen05 grouped GEMMs (default), 1 = mma.sync baseline;
+    """kernel 0 = the tile-per-CTA tcgen05 grouped GEMMs (default), 1 =
+    mma.sync baseline, 2 = the persistent swap-AB tcgen05 kernel;
     decode_kernel 0 = the layer in one launch where it applies, 1 = three."""
     from titan_b200 import _lib
     o = _lib.Options()
@@ -58,7 +59,10 @@ def _launches(fn):
     return out, names
 
 
-KERNELS = pytest.mark.parametrize("kernel", [0, 1], ids=["tcgen05", "mma_sync"])
+# every prefill kernel keeps the int8 algebra's re-centred fp32 order bit for bit
+KERNELS = pytest.mark.parametrize("kernel", [0, 2, 1],
+                                  ids=["tcgen05_tile", "tcgen05_swapab", "mma_sync"])
+ALL_KERNELS = KERNELS
 
 
 @pytest.mark.parametrize("T", [1, 2, 4, 8, 32])
@@ -75,7 +79,7 @@ def test_decode_block_vs_golden(cuda, oracle, T):
 @pytest.mark.parametrize("T", [1, 2, 3, 4])
 def test_decode_single_launch_vs_three_launches(cuda, oracle, T):
     """The one-launch decode layer (grid barriers, routing in every CTA) and
-    the three-launch pipeline on BASELINE config-2 shapes: identical routing,
+    the three-launch pipeline on the 512-expert decode shape: identical routing,
     both within tolerance of the oracle, and the one-launch path really is a
     single launch."""
     from titan_b200 import SparseMoeBlock, _lib
@@ -135,7 +139,7 @@ def test_decode_single_launch_repeats_and_graph(cuda, oracle):
 
 
 def test_decode_block_full_expert_count(cuda, oracle):
-    """BASELINE config 2 shape: H=2048, 512 experts + shared, k=10, I=512."""
+    """The decode shape: H=2048, 512 experts + shared, k=10, I=512."""
     from titan_b200 import SparseMoeBlock
     torch.manual_seed(0)
     blk = SparseMoeBlock(2048, 512, 10, 512, 512, device=cuda)
@@ -149,7 +153,7 @@ def test_decode_block_full_expert_count(cuda, oracle):
 
 
 @KERNELS
-@pytest.mark.parametrize("T,H,E,k,I", [(128, 2048, 64, 10, 512),
+@pytest.mark.parametrize("T,H,E,k,I", [(128, 2048, 64, 10, 512),     # single CPU-runnable layer
                                        (300, 1024, 48, 6, 256),      # ragged T, E % 32 != 0
                                        (64, 512, 16, 4, 128)])
 def test_prefill_int8_routed_bitexact(cuda, oracle, T, H, E, k, I, kernel):
@@ -182,7 +186,7 @@ def test_prefill_int8_bitexact_tiny_scales(cuda, oracle, kernel):
     assert np.array_equal(nbf(y), ry4)
 
 
-@KERNELS
+@ALL_KERNELS
 @pytest.mark.parametrize("mode", [3, 1, 0])
 def test_prefill_modes_with_shared_expert(cuda, oracle, mode, kernel):
     """int8 both (overlay default), int8 gate_up only (SKIP_DOWN), stock bf16.
@@ -213,7 +217,7 @@ def test_modular_path_equals_fused_path(cuda, oracle):
         patch.reset_stats()
         ym = blk.forward_modular(x)
         assert patch.stats()["routed"] == 2          # gate_up and down
-        yf = blk(x)
+        yf = blk(x, options=_opts(min_tokens=64, kernel=2))
     finally:
         patch.uninstall()
     assert torch.equal(ym.view(torch.int16), yf.view(torch.int16))
@@ -229,10 +233,12 @@ def test_one_expert_takes_every_token(cuda, oracle):
     L.wr = oracle.f32_to_bf16(w)
     load_block(blk, L)
     x = oracle.f32_to_bf16(np.abs(oracle.bf16_to_f32(oracle.make_x(700, 512, seed=7))))
-    y, idx, sc = blk(bf(x), options=_opts(min_tokens=1), return_routing=True)
+    y, idx, sc = blk(bf(x), options=_opts(min_tokens=1, kernel=2), return_routing=True)
     ry, ridx, _ = oracle.moe_prefill(L, x, int8_mode=3 | 4)
     assert np.array_equal(idx.cpu().numpy(), ridx)
     assert (ridx[:, 0] == 3).all()
+    yf = blk(bf(x), options=_opts(min_tokens=1, kernel=2))
+    assert np.array_equal(nbf(yf), ry), "one expert, swap-AB kernel"
     assert np.array_equal(nbf(y), ry)
 
 
@@ -246,9 +252,64 @@ def test_empty_batch_and_determinism(cuda, oracle):
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
-@pytest.mark.parametrize("T", [4096])
+def test_prefill_swap_ab_kernel_launches(cuda, oracle):
+    """The swap-AB tcgen05 kernel (gemm_kernel 2) runs the routed experts with
+    its own h quantiser, and the shared expert always: the launches the block
+    makes, and the same bits as the tile-per-CTA kernel."""
+    blk, L = _block(oracle, 512, 16, 4, 128, 256, seed=12, cuda=cuda)
+    x = oracle.make_x(96, 512, seed=12)
+    y, names = _launches(lambda: blk(bf(x), options=_opts(min_tokens=1, kernel=2)))
+    for n in ("gemm_gate_up", "quantize_h", "gemm_down", "gemm_shared_gate_up",
+              "gemm_shared_down"):
+        assert n in names, (n, names)
+    y0, names0 = _launches(lambda: blk(bf(x), options=_opts(min_tokens=1, kernel=0)))
+    assert "quantize_h" not in names0 and "gemm_shared_gate_up" in names0
+    assert torch.equal(y.view(torch.int16), y0.view(torch.int16))
+
+
+@pytest.mark.parametrize("case,w_std,x_scale,mode", [
+    ("tiny_scales", 1e-6, 1.0, 3),          # scales near MLX's 1e-7 floor
+    ("x_large", 0.02, 1e5, 3),               # |x| past fp16's 65504
+    ("x_small", 0.02, 1e-6, 3),              # x wholly below fp16's normal range
+    ("stock_x_large", 0.02, 1e5, 0),         # bf16-activation (stock) semantics
+    ("stock_tiny_scales", 1e-6, 1e-3, 0),
+])
+def test_prefill_extreme_ranges(cuda, oracle, case, w_std, x_scale, mode):
+    """Scales and activations far outside fp16's range, through the routed
+    experts and the shared expert: the power-of-two row normalisers keep the
+    fp16 operands exact, so the int8 block stays bit-exact (routed experts)
+    and every output within the tolerance of the oracle, and finite."""
+    from titan_b200 import SparseMoeBlock
+    L = oracle.make_layer(H=512, E=16, k=4, I=128, Is=256, seed=31, w_std=w_std)
+    blk = SparseMoeBlock(512, 16, 4, 128, 256, device=cuda, init=False)
+    load_block(blk, L)
+    x = oracle.make_x(160, 512, seed=31, scale=x_scale)
+    y, idx, sc = blk(bf(x), options=_opts(min_tokens=1, int8=1 if mode else 0,
+                                          down_int8=1 if mode == 3 else 0, kernel=0),
+                     return_routing=True)
+    ry, ridx, rsc, ops = oracle.moe_prefill(L, x, int8_mode=mode, parts=True)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    yf = f32(nbf(y))
+    assert np.isfinite(yf).all(), case
+    if mode == 0:
+        # the stock (bf16-activation) path is held to the reference's own
+        # relative-RMS bar for it (tests/kernels/test_moe_gather_int8.py:28
+        # uses 0.02), here 1e-2: its bf16 h rounds where the fp32 sums do
+        assert rel_rms(yf, f32(ry)) < 1e-2, case
+    else:
+        assert_bf16_close(nbf(y), ry, what=case, operands=ops, operand_ulps=4)
+    if mode == 3:                    # the routed experts alone: bit for bit
+        L0 = oracle.make_layer(H=512, E=16, k=4, I=128, Is=0, seed=31, w_std=w_std)
+        b0 = SparseMoeBlock(512, 16, 4, 128, 0, device=cuda, init=False)
+        load_block(b0, L0)
+        y0 = b0(bf(x), options=_opts(min_tokens=1, kernel=2))
+        r0, _, _ = oracle.moe_prefill(L0, x, int8_mode=3 | 4)
+        assert np.array_equal(nbf(y0), r0), case
+
+
+@pytest.mark.parametrize("T", [4096, 16384])
 def test_prefill_full_size_config3(cuda, oracle, T):
-    """BASELINE config 3 shape (H=3072, 512 experts, I=768, shared 3072) at
+    """The cold-prefill shape (H=3072, 512 experts, I=768, shared 3072) at
     T=4096: routing bit-exact for every token against the oracle router, and
     the block output of a subset of tokens against the oracle run on those
     tokens alone."""

@@ -165,7 +165,7 @@ def test_table_cache_never_serves_another_tensors_tables(monkeypatch):
     tensor (after the old one was freed) must not return the old tables."""
     from titan_b200 import ops
     built = []
-    monkeypatch.setattr(ops, "build_tables", lambda w, s, b: built.append(w) or ops.Int8Tables(s, b))
+    monkeypatch.setattr(ops, "build_tables", lambda w, s, b: built.append(w) or ops.Int8Tables(s, b, s[..., 0].float()))
     ops.clear_tables()
     try:
         w1 = torch.zeros(2, 128, 8, dtype=torch.int32)

@@ -13,7 +13,7 @@ import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libtitan_moe.so")
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 
 class TmoeError(RuntimeError):
@@ -70,7 +70,7 @@ class Layer(C.Structure):
             "shared_gate_up_w", "shared_gate_up_s", "shared_gate_up_b",
             "shared_down_w", "shared_down_s", "shared_down_b",
             "shared_gate_up_st", "shared_gate_up_bt", "shared_down_st", "shared_down_bt",
-            "shared_gate_w")]
+            "shared_gate_w", "gate_up_rs", "down_rs", "shared_gate_up_rs", "shared_down_rs")]
 
 
 class Options(C.Structure):
@@ -125,6 +125,7 @@ _SIGS = {
     "tmoe_ep_slots": ([P, P, P, I32, I32, I32, I32, I32, P, P, P, P], I32),
     "tmoe_ep_wait": ([P, P, I32, I32, I32, P, P], I32),
     "tmoe_ep_post": ([I32, P, I32, I32, P, P, I32, P], I32),
+    "tmoe_prepare_row_scale": ([P, P, I32, I32, I32, P, P], I32),
     "tmoe_ep_post_return": ([P, I32, I32, P, P, I32, P], I32),
     "tmoe_ep_guard": ([P, I32, P, I64, P], I32),
 }

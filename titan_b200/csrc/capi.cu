@@ -62,7 +62,10 @@ struct Carve {
 
 cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
 
-int max_tiles(int R, int E) { return (R + kTileM - 1) / kTileM + E; }
+// tiles of `tile` rows over R sorted rows of E experts (a bound: one partial tile per expert)
+int tiles_for(int R, int E, int tile) { return (R + tile - 1) / tile + E; }
+// workspace capacity: enough for the smaller (swap-AB kernel) tile
+int max_tiles(int R, int E) { return tiles_for(R, E, kSwTileN); }
 
 bool bad_k(int K) { return K <= 0 || K % 64 != 0; }
 
@@ -81,7 +84,14 @@ void tmoe_set_stage_hook(tmoe_stage_fn fn, void* ctx) {
 
 int tmoe_device_status(void) {
   cudaDeviceSynchronize();
-  if (tc05_error_flag()) return fail(TMOE_ERR_TIMEOUT, "a tcgen05 kernel's bounded wait timed out");
+  const int tc = tc05_error_flag();
+  if (tc == 2)
+    return fail(TMOE_ERR_UNSUPPORTED,
+                "the per-group tcgen05 kernel's bf16-activation path met a scale or activation "
+                "outside fp16's exact range; prepare the layer's row normalisers "
+                "(tmoe_prepare_row_scale) so that the swap-AB kernel runs it");
+  if (tc || sw_error_flag())
+    return fail(TMOE_ERR_TIMEOUT, "a tcgen05 kernel's bounded wait timed out");
   if (ep_error_flag())
     return fail(TMOE_ERR_TIMEOUT, "an expert-parallel exchange wait timed out");
   if (layer_error_flag())
@@ -108,6 +118,15 @@ int tmoe_prepare_tables(const uint16_t* scales, const uint16_t* biases, int E, i
     return fail(TMOE_ERR_INVALID, "tmoe_prepare_tables: bad arguments");
   TMOE_TRY(launch_prepare_tables(scales, biases, E, N, K / 64, scales_t, biases_t, S(stream)),
            "prepare_tables");
+  return TMOE_OK;
+}
+
+int tmoe_prepare_row_scale(const uint16_t* scales, const uint16_t* biases, int E, int N, int K,
+                           float* row_scale, void* stream) {
+  if (!scales || !biases || !row_scale || E <= 0 || N <= 0 || bad_k(K))
+    return fail(TMOE_ERR_INVALID, "tmoe_prepare_row_scale: bad arguments");
+  TMOE_TRY(launch_row_scale(scales, biases, (long long)E * N, K, row_scale, S(stream)),
+           "row_scale");
   return TMOE_OK;
 }
 
@@ -163,9 +182,9 @@ int tmoe_route_sort(const int32_t* idx, int R, int E, void* ws, size_t ws_bytes,
     return fail(TMOE_ERR_INVALID, "tmoe_route_sort: bad arguments");
   if ((tile_row != nullptr) != (tile_exp != nullptr) || (tile_row && (!ntiles || maxt < 1)))
     return fail(TMOE_ERR_INVALID, "tmoe_route_sort: tile_row, tile_exp, ntiles and maxt go together");
-  if (tile_row && maxt < max_tiles(R, E))
+  if (tile_row && maxt < tiles_for(R, E, kTileM))
     return fail(TMOE_ERR_INVALID, "tmoe_route_sort: maxt %d < ceil(R/128)+E = %d", maxt,
-                max_tiles(R, E));
+                tiles_for(R, E, kTileM));
   const size_t need = route_plan_scratch_bytes(R, E);
   if (need && (!ws || ws_bytes < need))
     return fail(TMOE_ERR_WORKSPACE, "tmoe_route_sort: workspace %zu < %zu bytes", ws_bytes, need);
@@ -201,7 +220,7 @@ size_t carve_int8_gather(Carve& c, int R, int E, int K, Int8GatherWs* w) {
   t.tile_row = c.take<int32_t>(maxt);
   t.tile_exp = c.take<int32_t>(maxt);
   t.ntiles = c.take<int32_t>(1);
-  t.xq = c.take<int8_t>((size_t)R * K);
+  t.xq = c.take<int8_t>((size_t)R * K * 2);     // fp16 codes of the tcgen05 operand layout
   t.xsc = c.take<float>((size_t)R * (K / 64));
   t.xrs = c.take<float>((size_t)R * (K / 64));
   t.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(R, E));
@@ -232,7 +251,7 @@ int tmoe_gather_qmm_int8(const uint16_t* x, const uint32_t* w, const uint16_t* s
   Carve c(ws);
   Int8GatherWs b;
   carve_int8_gather(c, R, E, K, &b);
-  const int maxt = max_tiles(R, E);
+  const int maxt = tiles_for(R, E, kTileM);
   RoutePlan p{};
   p.order = b.order;
   p.inv = b.inv;
@@ -242,7 +261,8 @@ int tmoe_gather_qmm_int8(const uint16_t* x, const uint32_t* w, const uint16_t* s
   p.ntiles = b.ntiles;
   cudaStream_t s = S(stream);
   TMOE_TRY(launch_route_plan(rhs, R, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
-  TMOE_TRY(launch_quantize_rows(x, R, K, b.xq, b.xsc, b.xrs, s), "quantize_rows");
+  TMOE_TRY(launch_prep_a16(x, R, K, true, reinterpret_cast<uint16_t*>(b.xq), b.xsc, b.xrs, s),
+           "quantize_rows");
   GemmParams g{};
   g.A = b.xq;
   g.asc = b.xsc;
@@ -262,7 +282,8 @@ int tmoe_gather_qmm_int8(const uint16_t* x, const uint32_t* w, const uint16_t* s
   g.N = N;
   g.Y = y;
   g.y_rows = b.order;
-  TMOE_TRY(launch_gemm_grouped(true, kEpiStore, g, maxt, s), "gemm_int8");
+  // the per-group tcgen05 kernel: the overlay's int8 algebra bit for bit
+  TMOE_TRY(launch_gemm_tc05(true, kEpiStore, g, maxt, s), "gemm_int8");
   return TMOE_OK;
 }
 
@@ -275,9 +296,12 @@ struct Bf16GatherWs {
   uint16_t* x16p;
   float* xsum;
   void* route_scratch;
+  float* rs;        // swap-AB kernel: row normalisers, the x operand and its group scalars
+  uint16_t* xb;
+  float *xc1, *xc2;
 };
 
-size_t carve_bf16_gather(Carve& c, int R, int E, int K, Bf16GatherWs* w) {
+size_t carve_bf16_gather(Carve& c, int R, int E, int N, int K, Bf16GatherWs* w) {
   const int maxt = max_tiles(R, E);
   const int U = R < E ? R : E;
   Bf16GatherWs t;
@@ -293,6 +317,10 @@ size_t carve_bf16_gather(Carve& c, int R, int E, int K, Bf16GatherWs* w) {
   t.x16p = c.take<uint16_t>((size_t)R * K);
   t.xsum = c.take<float>((size_t)R * (K / 64));
   t.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(R, E));
+  t.rs = c.take<float>((size_t)E * N);
+  t.xb = c.take<uint16_t>((size_t)R * K);
+  t.xc1 = c.take<float>((size_t)R * (K / 64));
+  t.xc2 = c.take<float>((size_t)R * (K / 64));
   if (w) *w = t;
   return c.off;
 }
@@ -300,10 +328,9 @@ size_t carve_bf16_gather(Carve& c, int R, int E, int K, Bf16GatherWs* w) {
 }  // namespace
 
 size_t tmoe_gather_qmm_bf16_workspace_size(int R, int E, int N, int K) {
-  (void)N;
-  if (R < 0 || E <= 0 || bad_k(K)) return 0;
+  if (R < 0 || E <= 0 || N <= 0 || bad_k(K)) return 0;
   Carve c(nullptr);
-  return carve_bf16_gather(c, R, E, K, nullptr);
+  return carve_bf16_gather(c, R, E, N, K, nullptr);
 }
 
 int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* scales,
@@ -324,9 +351,11 @@ int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* s
   if (R == 0) return TMOE_OK;
   Carve c(ws);
   Bf16GatherWs b;
-  carve_bf16_gather(c, R, E, K, &b);
+  carve_bf16_gather(c, R, E, N, K, &b);
   cudaStream_t s = S(stream);
-  const int maxt = max_tiles(R, E);
+  const bool sw = !gemv && gemm_sw_supported(kEpiStore, K, N);
+  const int tile = sw ? kSwTileN : kTileM;
+  const int maxt = tiles_for(R, E, tile);
   const int U = R < E ? R : E;
   RoutePlan p{};
   p.order = b.order;
@@ -341,7 +370,7 @@ int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* s
     p.tile_exp = b.tile_exp;
     p.ntiles = b.ntiles;
   }
-  TMOE_TRY(launch_route_plan(rhs, R, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
+  TMOE_TRY(launch_route_plan(rhs, R, E, tile, maxt, p, b.route_scratch, s), "route_plan");
   const int G = K / 64;
   if (gemv) {
     StreamParams q{};
@@ -359,6 +388,31 @@ int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* s
     q.col_div = 1;
     q.outb = y;
     TMOE_TRY(launch_gemv_stream(2, q, R, s), "gemv");
+  } else if (sw) {
+    // the swap-AB tcgen05 kernel, the row normalisers computed for this call
+    TMOE_TRY(launch_row_scale(scales, biases, (long long)E * N, K, b.rs, s), "row_scale");
+    TMOE_TRY(launch_prep_rows(x, R, K, false, b.xb, b.xc1, b.xc2, nullptr, s), "prep_x");
+    SwParams g{};
+    g.B = b.xb;
+    g.c1 = b.xc1;
+    g.c2 = b.xc2;
+    g.b_rows = b.order;
+    g.b_div = 1;
+    g.W = w;
+    g.st = scales_t;
+    g.bt = biases_t;
+    g.rscale = b.rs;
+    g.E = E;
+    g.K = K;
+    g.Nw = N;
+    g.tile_row = b.tile_row;
+    g.tile_exp = b.tile_exp;
+    g.ntiles = b.ntiles;
+    g.offsets = b.offsets;
+    g.maxt = maxt;
+    g.Y = y;
+    g.y_rows = b.order;
+    TMOE_TRY(launch_gemm_sw(kEpiStore, g, s), "gemm_f16");
   } else {
     TMOE_TRY(launch_prep_x(x, R, K, b.x16p, b.xsum, G, 1, s), "prep_x");
     GemmParams g{};
@@ -537,6 +591,127 @@ int tmoe_weighted_sum(const uint16_t* ys, const int32_t* inv_order, const uint16
   return TMOE_OK;
 }
 
+// ------------------------------------------------ swap-AB expert GEMMs
+// gate_up with the fused SwiGLU, then down, on gemm_sw: the activations and
+// h quantised once each (prep_rows), the weights widened in shared memory.
+
+namespace {
+
+struct FastProj {                    // one expert projection pair
+  const uint32_t* guw;
+  const uint16_t *gust, *gubt;
+  const float* gurs;
+  const uint32_t* dnw;
+  const uint16_t *dnst, *dnbt;
+  const float* dnrs;
+  int E, H, I;                       // gate_up [E][2I][H], down [E][H][I]
+};
+
+bool fast_ok(const FastProj& f) {
+  return f.gurs && f.dnrs && f.gust && f.gubt && f.dnst && f.dnbt &&
+         gemm_sw_supported(kEpiSwigluH16, f.H, 2 * f.I) && gemm_sw_supported(kEpiStore, f.I, f.H);
+}
+
+FastProj routed_proj(const tmoe_layer* L) {
+  return {L->gate_up_w, L->gate_up_st, L->gate_up_bt, L->gate_up_rs,
+          L->down_w,    L->down_st,    L->down_bt,    L->down_rs,
+          L->num_experts, L->hidden, L->moe_inter};
+}
+
+FastProj shared_proj(const tmoe_layer* L) {
+  return {L->shared_gate_up_w, L->shared_gate_up_st, L->shared_gate_up_bt, L->shared_gate_up_rs,
+          L->shared_down_w,    L->shared_down_st,    L->shared_down_bt,    L->shared_down_rs,
+          1, L->hidden, L->shared_inter};
+}
+
+struct FastWs {
+  uint16_t* xb;        // activation operand rows [xrows][H] (codes, or x * 2^-Et)
+  float *xc1, *xc2;    // [xrows][H/64]: group scale (or 2^Et) and exact group sum
+  uint16_t* h;         // bf16 h [P][I], sorted rows
+  uint16_t* hb;        // h operand rows [P][I]
+  float *hc1, *hc2;    // [P][I/64]
+};
+
+void carve_fast(Carve& c, int xrows, int P, int H, int I, FastWs* w) {
+  FastWs t;
+  t.xb = c.take<uint16_t>((size_t)xrows * H);
+  t.xc1 = c.take<float>((size_t)xrows * (H / 64));
+  t.xc2 = c.take<float>((size_t)xrows * (H / 64));
+  t.h = c.take<uint16_t>((size_t)P * I);
+  t.hb = c.take<uint16_t>((size_t)P * I);
+  t.hc1 = c.take<float>((size_t)P * (I / 64));
+  t.hc2 = c.take<float>((size_t)P * (I / 64));
+  if (w) *w = t;
+}
+
+struct FastRoute {                   // routed rows in expert order (route plan tiles of kSwTileN)
+  const int32_t *tile_row, *tile_exp, *ntiles, *offsets;
+  int maxt;
+  const int32_t* b_rows;             // gate_up activation row of sorted row r:
+  int b_div;                         //   b_rows[r] / b_div, or b_map[b_rows[r]]
+  const int32_t* b_map;
+};
+
+// names: fold of x, gate_up GEMM, fold of h, down GEMM (stage-hook labels).
+int run_fast(const FastProj& f, const uint16_t* x, int xrows, int prows, bool q_gu, bool q_dn,
+             const FastRoute& rt, const FastWs& w, uint16_t* Y, const int32_t* y_rows,
+             uint16_t* const* y_ptr, cudaStream_t s, const char* const names[4]) {
+  TMOE_TRY(launch_prep_rows(x, xrows, f.H, q_gu, w.xb, w.xc1, w.xc2, nullptr, s), names[0]);
+  SwParams g{};
+  g.B = w.xb;
+  g.c1 = w.xc1;
+  g.c2 = w.xc2;
+  g.b_rows = rt.b_rows;
+  g.b_div = rt.b_div > 0 ? rt.b_div : 1;
+  g.b_map = rt.b_map;
+  g.W = f.guw;
+  g.st = f.gust;
+  g.bt = f.gubt;
+  g.rscale = f.gurs;
+  g.E = f.E;
+  g.K = f.H;
+  g.Nw = 2 * f.I;
+  g.bias_bf16 = q_gu ? 1 : 0;
+  g.tile_row = rt.tile_row;
+  g.tile_exp = rt.tile_exp;
+  g.ntiles = rt.ntiles;
+  g.offsets = rt.offsets;
+  g.maxt = rt.maxt;
+  g.H = w.h;
+  TMOE_TRY(launch_gemm_sw(kEpiSwigluH16, g, s), names[1]);
+  // rows past offsets[E] (skipped slots) were not written and are not read
+  TMOE_TRY(launch_prep_rows(w.h, prows, f.I, q_dn, w.hb, w.hc1, w.hc2, rt.offsets + f.E, s),
+           names[2]);
+  SwParams d{};
+  d.B = w.hb;
+  d.c1 = w.hc1;
+  d.c2 = w.hc2;
+  d.W = f.dnw;
+  d.st = f.dnst;
+  d.bt = f.dnbt;
+  d.rscale = f.dnrs;
+  d.E = f.E;
+  d.K = f.I;
+  d.Nw = f.H;
+  d.bias_bf16 = q_dn ? 1 : 0;
+  d.tile_row = rt.tile_row;
+  d.tile_exp = rt.tile_exp;
+  d.ntiles = rt.ntiles;
+  d.offsets = rt.offsets;
+  d.maxt = rt.maxt;
+  d.Y = Y;
+  d.y_rows = y_rows;
+  d.y_ptr = y_ptr;
+  TMOE_TRY(launch_gemm_sw(kEpiStore, d, s), names[3]);
+  return TMOE_OK;
+}
+
+const char* const kRoutedNames[4] = {"quantize_rows", "gemm_gate_up", "quantize_h", "gemm_down"};
+const char* const kSharedNames[4] = {"prep_x", "gemm_shared_gate_up", "prep_h_shared",
+                                     "gemm_shared_down"};
+
+}  // namespace
+
 // ---------------------------------------------------------------- whole block
 
 namespace {
@@ -566,13 +741,24 @@ struct BlockWs {
   int32_t *s_tile_row, *s_tile_exp, *s_ntiles, *s_offsets;
   uint16_t *sx16p, *sh16p, *ys_sh;  // sx16p/sxsum: fp16 operand copy of x (F16 GEMMs)
   float *sxsum, *shrs;
+  FastWs fr, fs;                    // swap-AB path: routed experts, shared expert
 };
 
 int opt_min_tokens(const tmoe_options* o) { return (o && o->min_tokens > 0) ? o->min_tokens : 512; }
 int opt_down_int8(const tmoe_options* o) { return o ? (o->down_int8 != 0) : 1; }
 int opt_wsum(const tmoe_options* o) { return o ? o->wsum_mode : 0; }
 int opt_int8(const tmoe_options* o) { return o ? (o->int8_prefill != 0) : 1; }
-int opt_tc05(const tmoe_options* o) { return o ? (o->gemm_kernel == 0) : 1; }
+int opt_gemm(const tmoe_options* o) { return o ? o->gemm_kernel : 0; }
+// the tile-per-CTA tcgen05 kernel (else mma.sync) where the swap-AB one is not used
+int opt_tc05(const tmoe_options* o) { return opt_gemm(o) != 1; }
+// routed experts on the swap-AB kernel: when asked for (gemm_kernel 2), and
+// for the stock (bf16-activation) semantics whenever the layer carries its
+// row normalisers (the power-of-two normalisers keep x and the scales exact
+// in fp16 at any magnitude)
+bool fast_routed(const tmoe_layer* L, const tmoe_options* o) {
+  return fast_ok(routed_proj(L)) && (opt_gemm(o) == 2 || !opt_int8(o));
+}
+bool fast_shared(const tmoe_layer* L) { return L->shared_inter > 0 && fast_ok(shared_proj(L)); }
 int opt_layer(const tmoe_options* o) { return o ? (o->decode_kernel == 0) : 1; }
 
 size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt, BlockWs* out) {
@@ -620,34 +806,43 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
     b.tile_exp = c.take<int32_t>(maxt);
     b.ntiles = c.take<int32_t>(1);
     const bool tc = opt_tc05(opt);
-    if (i8) {  // int8 codes: one byte each for mma.sync, fp16 for tcgen05
-      b.xq = c.take<int8_t>((size_t)T * H * (tc ? 2 : 1));
-      b.xsc = c.take<float>((size_t)T * G);
-      b.xrs = c.take<float>((size_t)T * G);
+    const bool fr = fast_routed(L, opt), fs = fast_shared(L);
+    if (fr) {
+      carve_fast(c, T, R, H, I, &b.fr);
+    } else {
+      if (i8) {  // int8 codes: one byte each for mma.sync, fp16 for tcgen05
+        b.xq = c.take<int8_t>((size_t)T * H * (tc ? 2 : 1));
+        b.xsc = c.take<float>((size_t)T * G);
+        b.xrs = c.take<float>((size_t)T * G);
+      }
+      if (d8) {
+        if (tc)
+          b.h16p = c.take<uint16_t>((size_t)R * I);
+        else
+          b.hq = c.take<int8_t>((size_t)R * I);
+        b.hsc = c.take<float>((size_t)R * (I / 64));
+      } else {
+        b.h16p = c.take<uint16_t>((size_t)R * I);
+      }
+      b.hrs = c.take<float>((size_t)R * (I / 64));
     }
-    if (!i8 || Is > 0) {
+    if ((!fr && !i8) || (Is > 0 && !fs)) {
       b.sx16p = c.take<uint16_t>((size_t)T * H);
       b.sxsum = c.take<float>((size_t)T * G);
     }
-    if (d8) {
-      if (tc)
-        b.h16p = c.take<uint16_t>((size_t)R * I);
-      else
-        b.hq = c.take<int8_t>((size_t)R * I);
-      b.hsc = c.take<float>((size_t)R * (I / 64));
-    } else {
-      b.h16p = c.take<uint16_t>((size_t)R * I);
-    }
-    b.hrs = c.take<float>((size_t)R * (I / 64));
     b.ys = c.take<uint16_t>((size_t)R * H);
     if (Is > 0) {
-      const int st = (T + kTileM - 1) / kTileM;
+      const int st = (T + kSwTileN - 1) / kSwTileN;
       b.s_tile_row = c.take<int32_t>(st);
       b.s_tile_exp = c.take<int32_t>(st);
       b.s_ntiles = c.take<int32_t>(1);
       b.s_offsets = c.take<int32_t>(2);
-      b.sh16p = c.take<uint16_t>((size_t)T * Is);
-      b.shrs = c.take<float>((size_t)T * (Is / 64));
+      if (fs) {
+        carve_fast(c, T, T, H, Is, &b.fs);
+      } else {
+        b.sh16p = c.take<uint16_t>((size_t)T * Is);
+        b.shrs = c.take<float>((size_t)T * (Is / 64));
+      }
       b.ys_sh = c.take<uint16_t>((size_t)T * H);
     }
   }
@@ -843,7 +1038,9 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   p.tile_row = b.tile_row;
   p.tile_exp = b.tile_exp;
   p.ntiles = b.ntiles;
-  TMOE_TRY(launch_route_plan(idx, R, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
+  const bool fr = fast_routed(L, opt), fs = fast_shared(L);
+  const int rtile = fr ? kSwTileN : kTileM, rmaxt = tiles_for(R, E, rtile);
+  TMOE_TRY(launch_route_plan(idx, R, E, rtile, rmaxt, p, b.route_scratch, s), "route_plan");
   const bool i8 = opt_int8(opt);
   const bool d8 = i8 && opt_down_int8(opt);
   const bool tc = opt_tc05(opt);
@@ -851,94 +1048,112 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     return tc ? launch_gemm_tc05(int8, epi, P, ntiles_max, s)
               : launch_gemm_grouped(int8, epi, P, ntiles_max, s);
   };
-  if (tc) {
-    if (i8)
-      TMOE_TRY(launch_prep_a16(x, T, H, true, reinterpret_cast<uint16_t*>(b.xq), b.xsc, b.xrs, s),
-               "quantize_rows");
-    if (!i8 || Is > 0)
+  if ((!fr && !i8) || (Is > 0 && !fs)) {      // fp16 copy of x for the per-group kernels
+    if (tc)
       TMOE_TRY(launch_prep_a16(x, T, H, false, b.sx16p, nullptr, b.sxsum, s), "prep_x");
-  } else {
-    if (i8) TMOE_TRY(launch_quantize_rows(x, T, H, b.xq, b.xsc, b.xrs, s), "quantize_rows");
-    if (!i8 || Is > 0) TMOE_TRY(launch_prep_x(x, T, H, b.sx16p, b.sxsum, G, 1, s), "prep_x");
+    else
+      TMOE_TRY(launch_prep_x(x, T, H, b.sx16p, b.sxsum, G, 1, s), "prep_x");
   }
-  GemmParams g{};
-  g.A = i8 ? static_cast<const void*>(b.xq) : static_cast<const void*>(b.sx16p);
-  g.asc = b.xsc;
-  g.ars = i8 ? b.xrs : b.sxsum;
-  g.s_r = G;
-  g.s_g = 1;
-  g.a_rows = b.order;
-  g.a_div = k;
-  g.W = L->gate_up_w;
-  g.st = L->gate_up_st;
-  g.bt = L->gate_up_bt;
-  g.tile_row = b.tile_row;
-  g.tile_exp = b.tile_exp;
-  g.ntiles = b.ntiles;
-  g.offsets = b.offsets;
-  g.K = H;
-  g.N = 2 * I;
-  g.hq = b.hq;
-  g.hsc = b.hsc;
-  g.hrs = b.hrs;
-  g.Rpad_h = R;
-  g.h16p = b.h16p;
-  TMOE_TRY(gemm(i8, d8 ? kEpiSwigluQ8 : kEpiSwigluH16, g, maxt), "gemm_gate_up");
-  GemmParams dn{};
-  dn.A = (d8 && !tc) ? static_cast<const void*>(b.hq) : static_cast<const void*>(b.h16p);
-  dn.asc = b.hsc;
-  dn.ars = b.hrs;
-  dn.s_r = 1;
-  dn.s_g = R;
-  dn.W = L->down_w;
-  dn.st = L->down_st;
-  dn.bt = L->down_bt;
-  dn.tile_row = b.tile_row;
-  dn.tile_exp = b.tile_exp;
-  dn.ntiles = b.ntiles;
-  dn.offsets = b.offsets;
-  dn.K = I;
-  dn.N = H;
-  dn.Y = b.ys;
-  TMOE_TRY(gemm(d8, kEpiStore, dn, maxt), "gemm_down");
+  if (fr) {
+    const FastRoute rt{b.tile_row, b.tile_exp, b.ntiles, b.offsets, rmaxt, b.order, k, nullptr};
+    if (int rc = run_fast(routed_proj(L), x, T, R, i8, d8, rt, b.fr, b.ys, nullptr, nullptr, s,
+                          kRoutedNames))
+      return rc;
+  } else {
+    if (i8) {
+      if (tc)
+        TMOE_TRY(launch_prep_a16(x, T, H, true, reinterpret_cast<uint16_t*>(b.xq), b.xsc, b.xrs, s),
+                 "quantize_rows");
+      else
+        TMOE_TRY(launch_quantize_rows(x, T, H, b.xq, b.xsc, b.xrs, s), "quantize_rows");
+    }
+    GemmParams g{};
+    g.A = i8 ? static_cast<const void*>(b.xq) : static_cast<const void*>(b.sx16p);
+    g.asc = b.xsc;
+    g.ars = i8 ? b.xrs : b.sxsum;
+    g.s_r = G;
+    g.s_g = 1;
+    g.a_rows = b.order;
+    g.a_div = k;
+    g.W = L->gate_up_w;
+    g.st = L->gate_up_st;
+    g.bt = L->gate_up_bt;
+    g.tile_row = b.tile_row;
+    g.tile_exp = b.tile_exp;
+    g.ntiles = b.ntiles;
+    g.offsets = b.offsets;
+    g.K = H;
+    g.N = 2 * I;
+    g.hq = b.hq;
+    g.hsc = b.hsc;
+    g.hrs = b.hrs;
+    g.Rpad_h = R;
+    g.h16p = b.h16p;
+    TMOE_TRY(gemm(i8, d8 ? kEpiSwigluQ8 : kEpiSwigluH16, g, rmaxt), "gemm_gate_up");
+    GemmParams dn{};
+    dn.A = (d8 && !tc) ? static_cast<const void*>(b.hq) : static_cast<const void*>(b.h16p);
+    dn.asc = b.hsc;
+    dn.ars = b.hrs;
+    dn.s_r = 1;
+    dn.s_g = R;
+    dn.W = L->down_w;
+    dn.st = L->down_st;
+    dn.bt = L->down_bt;
+    dn.tile_row = b.tile_row;
+    dn.tile_exp = b.tile_exp;
+    dn.ntiles = b.ntiles;
+    dn.offsets = b.offsets;
+    dn.K = I;
+    dn.N = H;
+    dn.Y = b.ys;
+    TMOE_TRY(gemm(d8, kEpiStore, dn, rmaxt), "gemm_down");
+  }
   if (Is > 0) {
-    const int st = (T + kTileM - 1) / kTileM;
-    TMOE_TRY(launch_dense_tiles(T, kTileM, b.s_tile_row, b.s_tile_exp, b.s_ntiles, b.s_offsets, s),
+    const int stile = fs ? kSwTileN : kTileM, st = (T + stile - 1) / stile;
+    TMOE_TRY(launch_dense_tiles(T, stile, b.s_tile_row, b.s_tile_exp, b.s_ntiles, b.s_offsets, s),
              "dense_tiles");
-    GemmParams sg{};
-    sg.A = b.sx16p;
-    sg.ars = b.sxsum;
-    sg.s_r = G;
-    sg.s_g = 1;
-    sg.W = L->shared_gate_up_w;
-    sg.st = L->shared_gate_up_st;
-    sg.bt = L->shared_gate_up_bt;
-    sg.tile_row = b.s_tile_row;
-    sg.tile_exp = b.s_tile_exp;
-    sg.ntiles = b.s_ntiles;
-    sg.offsets = b.s_offsets;
-    sg.K = H;
-    sg.N = 2 * Is;
-    sg.hrs = b.shrs;
-    sg.Rpad_h = T;
-    sg.h16p = b.sh16p;
-    TMOE_TRY(gemm(false, kEpiSwigluH16, sg, st), "gemm_shared_gate_up");
-    GemmParams sd{};
-    sd.A = b.sh16p;
-    sd.ars = b.shrs;
-    sd.s_r = 1;
-    sd.s_g = T;
-    sd.W = L->shared_down_w;
-    sd.st = L->shared_down_st;
-    sd.bt = L->shared_down_bt;
-    sd.tile_row = b.s_tile_row;
-    sd.tile_exp = b.s_tile_exp;
-    sd.ntiles = b.s_ntiles;
-    sd.offsets = b.s_offsets;
-    sd.K = Is;
-    sd.N = H;
-    sd.Y = b.ys_sh;
-    TMOE_TRY(gemm(false, kEpiStore, sd, st), "gemm_shared_down");
+    if (fs) {
+      const FastRoute rs{b.s_tile_row, b.s_tile_exp, b.s_ntiles, b.s_offsets, st, nullptr, 1,
+                         nullptr};
+      if (int rc = run_fast(shared_proj(L), x, T, T, false, false, rs, b.fs, b.ys_sh, nullptr,
+                            nullptr, s, kSharedNames))
+        return rc;
+    } else {
+      GemmParams sg{};
+      sg.A = b.sx16p;
+      sg.ars = b.sxsum;
+      sg.s_r = G;
+      sg.s_g = 1;
+      sg.W = L->shared_gate_up_w;
+      sg.st = L->shared_gate_up_st;
+      sg.bt = L->shared_gate_up_bt;
+      sg.tile_row = b.s_tile_row;
+      sg.tile_exp = b.s_tile_exp;
+      sg.ntiles = b.s_ntiles;
+      sg.offsets = b.s_offsets;
+      sg.K = H;
+      sg.N = 2 * Is;
+      sg.hrs = b.shrs;
+      sg.Rpad_h = T;
+      sg.h16p = b.sh16p;
+      TMOE_TRY(gemm(false, kEpiSwigluH16, sg, st), "gemm_shared_gate_up");
+      GemmParams sd{};
+      sd.A = b.sh16p;
+      sd.ars = b.shrs;
+      sd.s_r = 1;
+      sd.s_g = T;
+      sd.W = L->shared_down_w;
+      sd.st = L->shared_down_st;
+      sd.bt = L->shared_down_bt;
+      sd.tile_row = b.s_tile_row;
+      sd.tile_exp = b.s_tile_exp;
+      sd.ntiles = b.s_ntiles;
+      sd.offsets = b.s_offsets;
+      sd.K = Is;
+      sd.N = H;
+      sd.Y = b.ys_sh;
+      TMOE_TRY(gemm(false, kEpiStore, sd, st), "gemm_shared_down");
+    }
   }
   TMOE_TRY(launch_wsum(b.ys, b.inv, scores, T, k, H, opt_wsum(opt), Is > 0 ? b.ys_sh : nullptr,
                        b.gate_logit, y, s),
@@ -963,6 +1178,7 @@ struct ExpertsWs {
   float *xsc, *xrs, *hsc, *hrs;
   uint16_t *x16p, *h16p;
   float* xsum;
+  FastWs fr;
 };
 
 size_t carve_experts(Carve& c, const tmoe_layer* L, int R, int P, const tmoe_options* opt,
@@ -978,6 +1194,11 @@ size_t carve_experts(Carve& c, const tmoe_layer* L, int R, int P, const tmoe_opt
   b.tile_exp = c.take<int32_t>(maxt);
   b.ntiles = c.take<int32_t>(1);
   b.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(P, E));
+  if (fast_routed(L, opt)) {
+    carve_fast(c, R, P, H, I, &b.fr);
+    if (out) *out = b;
+    return c.off;
+  }
   if (i8) {
     b.xq = c.take<int8_t>((size_t)R * H * (tc ? 2 : 1));
     b.xsc = c.take<float>((size_t)R * G);
@@ -1034,7 +1255,9 @@ int moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pa
   Carve c(ws);
   ExpertsWs b;
   carve_experts(c, L, R, npairs, opt, &b);
-  const int P = npairs, maxt = max_tiles(P, E);
+  const int P = npairs;
+  const bool fastr = fast_routed(L, opt);
+  const int maxt = tiles_for(P, E, fastr ? kSwTileN : kTileM);
   RoutePlan p{};
   p.order = b.order;
   p.inv = b.inv;
@@ -1042,8 +1265,16 @@ int moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pa
   p.tile_row = b.tile_row;
   p.tile_exp = b.tile_exp;
   p.ntiles = b.ntiles;
-  TMOE_TRY(launch_route_plan(pair_exp, P, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
+  TMOE_TRY(launch_route_plan(pair_exp, P, E, fastr ? kSwTileN : kTileM, maxt, p, b.route_scratch,
+                             s),
+           "route_plan");
   const bool i8 = opt_int8(opt), d8 = i8 && opt_down_int8(opt), tc = opt_tc05(opt);
+  if (fastr) {
+    const FastRoute rt{b.tile_row, b.tile_exp, b.ntiles, b.offsets, maxt, b.order,
+                       slot_k > 0 ? slot_k : 1, slot_k > 0 ? nullptr : pair_row};
+    return run_fast(routed_proj(L), x, R, P, i8, d8, rt, b.fr, y_pairs, b.order, y_ptr, s,
+                    kRoutedNames);
+  }
   auto gemm = [&](bool int8, int epi, const GemmParams& Pm) {
     return tc ? launch_gemm_tc05(int8, epi, Pm, maxt, s) : launch_gemm_grouped(int8, epi, Pm, maxt, s);
   };
@@ -1182,6 +1413,15 @@ int tmoe_moe_local(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_opt
            "router_logits");
   TMOE_TRY(launch_router_topk(b.logits, T, E, k, idx, scores, nullptr, s), "router_topk");
   if (Is == 0) return TMOE_OK;
+  if (fast_shared(L)) {
+    const int st = (T + kSwTileN - 1) / kSwTileN;
+    TMOE_TRY(launch_dense_tiles(T, kSwTileN, b.s_tile_row, b.s_tile_exp, b.s_ntiles, b.s_offsets,
+                                s),
+             "dense_tiles");
+    const FastRoute rs{b.s_tile_row, b.s_tile_exp, b.s_ntiles, b.s_offsets, st, nullptr, 1, nullptr};
+    return run_fast(shared_proj(L), x, T, T, false, false, rs, b.fs, shared_out, nullptr, nullptr,
+                    s, kSharedNames);
+  }
   if (opt_tc05(&o))
     TMOE_TRY(launch_prep_a16(x, T, H, false, b.sx16p, nullptr, b.sxsum, s), "prep_x");
   else

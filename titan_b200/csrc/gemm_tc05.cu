@@ -35,7 +35,7 @@
 // Every mbarrier wait is bounded: on timeout the thread records an error in
 // g_tc05_error, raises a CTA-wide abort flag and every role leaves its loop;
 // TMEM is released before the kernel returns.
-#include "common.cuh"
+#include "tc05.cuh"
 #include "tmoe_internal.h"
 
 namespace tmoe {
@@ -63,36 +63,9 @@ constexpr int SMEM = XCH_OFF + BM * 36 * 4 + 1024;
 static_assert(SMEM <= 232448, "shared memory per CTA");
 constexpr int NTHREADS = 512;
 constexpr int NPROD = 224;                       // warps 1-7
-constexpr uint32_t kSpinLimit = 1u << 22;   // bound of every wait (polls)
-constexpr uint32_t kFastPolls = 1u << 12;   // polls before backing off
-
-TMOE_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-TMOE_DEV void mbar_init(uint32_t a, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count));
-}
-TMOE_DEV void mbar_arrive(uint32_t a) {
-  asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(a) : "memory");
-}
-TMOE_DEV bool mbar_try(uint32_t a, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(a), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait; false (with the abort flag raised) on timeout or abort.
+// Bounded wait recording into this kernel's error flag.
 TMOE_DEV bool mbar_wait(uint32_t a, uint32_t parity, volatile int* abort_flag) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try(a, parity)) return true;
-    if (*abort_flag) return false;
-    if (i >= kFastPolls) __nanosleep(64);
-  }
-  *abort_flag = 1;
-  atomicExch(&g_tc05_error, 1);
-  return false;
+  return tc::mbar_wait(a, parity, abort_flag, &g_tc05_error);
 }
 
 // Named barrier over the producer warps that also ANDs a predicate.
@@ -106,70 +79,13 @@ TMOE_DEV bool producers_and(bool v) {
   return r != 0;
 }
 
-TMOE_DEV uint64_t sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)64 << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
 // kind::f16, f16 x f16 -> f32, K-major A and B, M = 128, N = 128.
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) |
                             ((uint32_t)(BM >> 4) << 24);
 
 TMOE_DEV void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+  tc::mma_f16(tmem_d, adesc, bdesc, kIdesc, accumulate);
 }
-TMOE_DEV void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
-}
-TMOE_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-TMOE_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-TMOE_DEV void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-TMOE_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// 8 nibbles (elements 0..7 of a chunk) -> 4 half2 in the pair order
-// (0,4),(1,5),(2,6),(3,7): the fp16 operand layout of every A and B chunk.
-// 0x6400|q is 1024 + q; pairs 1 and 3 are taken 4 bits up (1024 + 16q) and
-// re-centred by one HFMA2 (x/16 - 72); every step is exact.
-TMOE_DEV uint4 widen8(uint32_t w, bool scale, __half2 s2) {
-  const __half2 off = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
-  const __half2 sixteenth = __halves2half2(__ushort_as_half(0x2c00), __ushort_as_half(0x2c00));
-  const __half2 m72 = __halves2half2(__ushort_as_half(0xd480), __ushort_as_half(0xd480));
-  const uint32_t w8 = w >> 8;
-  uint32_t v[4] = {(w & 0x000f000fu) | 0x64006400u, (w & 0x00f000f0u) | 0x64006400u,
-                   (w8 & 0x000f000fu) | 0x64006400u, (w8 & 0x00f000f0u) | 0x64006400u};
-  __half2 h[4];
-  h[0] = __hsub2(*reinterpret_cast<__half2*>(&v[0]), off);
-  h[1] = __hfma2(*reinterpret_cast<__half2*>(&v[1]), sixteenth, m72);
-  h[2] = __hsub2(*reinterpret_cast<__half2*>(&v[2]), off);
-  h[3] = __hfma2(*reinterpret_cast<__half2*>(&v[3]), sixteenth, m72);
-  uint32_t o[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if (scale) h[i] = __hmul2(h[i], s2);
-    o[i] = *reinterpret_cast<uint32_t*>(&h[i]);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-// position of element k within its 8-element chunk in the operand layout
-TMOE_DEV int p8(int k) { return (k & ~7) | (((k & 3) << 1) | ((k >> 2) & 1)); }
 
 }  // namespace tc
 
@@ -272,7 +188,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
     // of the tile is 0 or inside [2^-14, 2^12): then the MMA returns D * s
     // exactly (|D| <= 2^16, so D * s needs at most 24 bits).  One flag per CTA.
     bool safe = true;
-    if (I8) {
+    {
       for (int i = pt; i < G * 16; i += NPROD) {
         const int g = i >> 4, cc = i & 15;
         const uint4 v = *reinterpret_cast<const uint4*>(ste + (size_t)g * P.N + wrow(cc * 8));
@@ -285,8 +201,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
         }
       }
     }
-    const bool prescale = I8 ? producers_and(safe) : producers_and(true);
+    const bool prescale = producers_and(safe);
     if (pt == 0) *prescale_flag = prescale ? 1 : 0;
+    // STOCK accumulates every group in TMEM, so B must carry the scale: a
+    // tile whose scales fall outside fp16's exact range is reported (error 2,
+    // tmoe_device_status) — the swap-AB kernel with row normalisers has
+    // no such limit.
+    if (!I8 && !prescale && pt == 0) atomicExch(&g_tc05_error, 2);
     const bool scale_b = !I8 || prescale;
 
     // Per-thread copy plan, fixed across groups (addresses advance per group).
@@ -606,6 +527,13 @@ __global__ void __launch_bounds__(256) prep_a16_kernel(const uint16_t* __restric
   const uint32_t pr = *reinterpret_cast<const uint32_t*>(x + (size_t)m * K + g * kGroup + 2 * lane);
   float a = bf2f((uint16_t)(pr & 0xffffu)), b = bf2f((uint16_t)(pr >> 16));
   const float sum = warp_butterfly_sum(__fadd_rn(a, b));
+  if (!QUANT) {
+    // x itself becomes the fp16 operand: it overflows past 65504, and a group
+    // lying wholly below fp16's normal range keeps too few bits
+    const float gm = warp_max(fmaxf(fabsf(a), fabsf(b)));
+    if (lane == 0 && (gm >= 65504.0f || (gm > 0.0f && gm < 6.103515625e-05f)))
+      atomicExch(&g_tc05_error, 2);
+  }
   if (QUANT) {
     const float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
     const float sc = __fdiv_rn(fmaxf(amax, 1e-30f), 127.0f);

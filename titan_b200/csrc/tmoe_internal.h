@@ -121,6 +121,51 @@ cudaError_t launch_prep_a16(const uint16_t* x, int R, int K, bool quant, uint16_
                             float* xrs, cudaStream_t s);
 int tc05_error_flag();
 
+// Persistent swap-AB grouped GEMM (gemm_sw.cu): weight rows on the MMA's M
+// side (two 128-row tiles per work item), up to kSwTileN routed rows of one
+// expert on N; one exact MMA per 64-wide group and the reference's per-group
+// fp32 FMAs in the epilogue.
+constexpr int kSwTileN = 64;       // routed rows per work item (route plan tile size)
+struct SwParams {
+  const uint16_t* B;       // activation operand rows [brows][K] fp16, each 8-element chunk
+                           // in (0,4,1,5,2,6,3,7) order: int8 codes, or x * 2^-Et (stock)
+  const float* c1;         // [brows][K/64]: the group's activation scale xsc, or 2^Et
+  const float* c2;         // [brows][K/64]: exact group sum of the unquantised row
+  const int32_t* b_rows;   // optional: sorted row r reads B row b_rows[r] / b_div,
+  int b_div;               // or b_map[b_rows[r]] when b_map is set
+  const int32_t* b_map;
+  const uint32_t* W;       // [E][Nw][K/8] packed int4
+  const uint16_t* st;      // [E][G][Nw] bf16 scales (transposed)
+  const uint16_t* bt;      // [E][G][Nw] bf16 biases (transposed)
+  const float* rscale;     // [E][Nw] 2^Ew: the weight row's scale normaliser
+  int E, K, Nw;
+  int bias_bf16;           // bias bf16(b + 8s) (int8 algebra) or fp32 b + 8s (stock)
+  const int32_t* tile_row;
+  const int32_t* tile_exp;
+  const int32_t* ntiles;
+  const int32_t* offsets;  // [E+1]
+  int maxt;
+  uint16_t* Y;             // store: bf16 rows of Nw
+  const int32_t* y_rows;   // optional: sorted row r is stored at Y row y_rows[r]
+  uint16_t* const* y_ptr;  // optional: Y row i is stored at y_ptr[i] (any device's memory)
+  uint16_t* H;             // SwiGLU: bf16 h [R][Nw/2] in sorted row order
+};
+// epi: kEpiStore or kEpiSwigluH16 (bf16 h).  False: the shape is outside this
+// kernel (Nw % 256, K % 256 or 64) and the caller uses the per-group kernel.
+bool gemm_sw_supported(int epi, int K, int Nw);
+cudaError_t launch_gemm_sw(int epi, const SwParams& P, cudaStream_t s);
+// Activation operand rows for gemm_sw, one warp per row: quant = the
+// reference's per-(row, 64-group) quantiser (codes xu - 128 as fp16, c1 =
+// amax/127, c2 = the exact group sum); else x * 2^-Et with one power of two
+// per row (amax * 2^-Et in [2^8, 2^9)), c1 = 2^Et, c2 = the group sums.
+// rows_limit (optional, device): rows at or past *rows_limit are left alone.
+cudaError_t launch_prep_rows(const uint16_t* x, int R, int K, bool quant, uint16_t* out,
+                             float* c1, float* c2, const int32_t* rows_limit, cudaStream_t s);
+// rscale[e][n] = 2^Ew with max_g 8|s| * 2^Ew in [2^13, 2^14).
+cudaError_t launch_row_scale(const uint16_t* scales, const uint16_t* biases, long long rows, int K,
+                             float* rscale, cudaStream_t s);
+int sw_error_flag();
+
 // Single-launch decode layer (decode_layer.cu), T <= kLayerMaxT tokens.
 struct LayerArgs {
   const uint16_t* x;                                   // [T][H] bf16

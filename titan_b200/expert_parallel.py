@@ -470,6 +470,8 @@ class ExpertParallelMoE(torch.nn.Module):
             L.down_w, L.down_s, L.down_b = (t.data_ptr() for t in self.dn)
             L.gate_up_st, L.gate_up_bt = self.tables[0].scales_t.data_ptr(), self.tables[0].biases_t.data_ptr()
             L.down_st, L.down_bt = self.tables[1].scales_t.data_ptr(), self.tables[1].biases_t.data_ptr()
+            L.gate_up_rs = self.tables[0].row_scale.data_ptr()
+            L.down_rs = self.tables[1].row_scale.data_ptr()
             self._layer = L
         return self._layer
 
@@ -491,6 +493,8 @@ class ExpertParallelMoE(torch.nn.Module):
                 L.shared_down_b = se.down_proj.biases.data_ptr()
                 L.shared_gate_up_st, L.shared_gate_up_bt = t[0].scales_t.data_ptr(), t[0].biases_t.data_ptr()
                 L.shared_down_st, L.shared_down_bt = t[1].scales_t.data_ptr(), t[1].biases_t.data_ptr()
+                L.shared_gate_up_rs = t[0].row_scale.data_ptr()
+                L.shared_down_rs = t[1].row_scale.data_ptr()
                 L.shared_gate_w = self.shared_gate.data_ptr()
             self._local = L
         return self._local

@@ -104,6 +104,7 @@ class SparseMoeBlock(nn.Module):
         t = self._tables
         L.gate_up_st, L.gate_up_bt = t[0].scales_t.data_ptr(), t[0].biases_t.data_ptr()
         L.down_st, L.down_bt = t[1].scales_t.data_ptr(), t[1].biases_t.data_ptr()
+        L.gate_up_rs, L.down_rs = t[0].row_scale.data_ptr(), t[1].row_scale.data_ptr()
         if self.shared_expert is not None:
             se = self.shared_expert
             L.shared_gate_up_w = se.gate_up_proj.weight.data_ptr()
@@ -115,6 +116,8 @@ class SparseMoeBlock(nn.Module):
             L.shared_gate_up_st, L.shared_gate_up_bt = (t[2].scales_t.data_ptr(),
                                                         t[2].biases_t.data_ptr())
             L.shared_down_st, L.shared_down_bt = t[3].scales_t.data_ptr(), t[3].biases_t.data_ptr()
+            L.shared_gate_up_rs, L.shared_down_rs = (t[2].row_scale.data_ptr(),
+                                                     t[3].row_scale.data_ptr())
             L.shared_gate_w = self.shared_expert_gate_weight.data_ptr()
         self._layer = L
         return L

@@ -145,15 +145,31 @@ class Int8Tables:
 
     scales_t: torch.Tensor   # [E, G, N] bf16
     biases_t: torch.Tensor   # [E, G, N] bf16 (raw biases; b + 8s is folded in-kernel)
+    row_scale: torch.Tensor  # [E, N] fp32 power-of-two row normalisers (swap-AB GEMM)
 
     @property
     def nbytes(self) -> int:
-        return self.scales_t.numel() * 2 + self.biases_t.numel() * 2
+        return self.scales_t.numel() * 2 + self.biases_t.numel() * 2 + self.row_scale.numel() * 4
+
+
+def row_scale(scales: torch.Tensor, biases: torch.Tensor) -> torch.Tensor:
+    """[E, N, G] scales / biases -> [E, N] fp32 row normalisers 2^Ew of the
+    swap-AB grouped GEMM (tmoe_prepare_row_scale)."""
+    scales = _bf16(scales, "scales")
+    biases = _bf16(biases, "biases")
+    squeeze = scales.dim() == 2
+    if squeeze:
+        scales, biases = scales[None], biases[None]
+    E, N, G = scales.shape
+    rs = torch.empty(E, N, dtype=torch.float32, device=scales.device)
+    _lib.call("tmoe_prepare_row_scale", _p(scales), _p(biases), E, N, G * GROUP, _p(rs),
+              stream_ptr(scales.device))
+    return rs[0] if squeeze else rs
 
 
 def build_tables(wq, scales, biases) -> Int8Tables:
     st, bt = prepare_tables(scales, biases)
-    return Int8Tables(st, bt)
+    return Int8Tables(st, bt, row_scale(scales, biases))
 
 
 _TABLES: dict = {}

@@ -49,7 +49,7 @@ class QuantizedSwitchLinear(nn.Module):
         """``init``: draw fp32 weights and quantise them on the GPU, a chunk
         of experts at a time — uniform(-1/sqrt(in), 1/sqrt(in)) as the
         reference's constructor (switch_layers.py:41-51), or N(0, weight_std)
-        when given (the BASELINE configs use N(0, 0.02))."""
+        when given (the benchmark workloads use N(0, 0.02))."""
         super().__init__()
         if bias:
             raise Unsupported("QuantizedSwitchLinear with bias is not part of the MoE block")
