@@ -59,6 +59,9 @@ def parse():
                     help="run a small untimed case for an ncu capture and exit")
     ap.add_argument("--gemm-kernel", type=int, default=0,
                     help="prefill grouped GEMMs: 0 tcgen05 (default), 1 mma.sync baseline")
+    ap.add_argument("--spec-streams", type=int, default=64, help="config 5: streams per step")
+    ap.add_argument("--spec-draft", type=int, default=3, help="config 5: draft tokens per stream")
+    ap.add_argument("--spec-layers", type=int, default=48, help="config 5: layers per step")
     ap.add_argument("--headline-only", action="store_true",
                     help="only the expert-parallel headline (no decode / prefill / CPU extras)")
     ap.add_argument("--ref-tokens", type=int, default=64,
@@ -474,6 +477,28 @@ def run_ep(args, world, rank, local):
             dist.destroy_process_group()
 
 
+def run_spec_group(args, world, rank, local):
+    """run_spec inside a process group (a one-rank group at N=1)."""
+    import torch
+    import torch.distributed as dist
+    device = torch.device("cuda", torch.cuda.current_device())
+    own_group = not dist.is_initialized()
+    if own_group:
+        import socket
+        so = socket.socket()
+        so.bind(("127.0.0.1", 0))
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(so.getsockname()[1])
+        so.close()
+        dist.init_process_group("nccl", rank=0, world_size=1,
+                                timeout=datetime.timedelta(seconds=300))
+    try:
+        return run_spec(args, world, rank, local, device)
+    finally:
+        if own_group:
+            dist.destroy_process_group()
+
+
 def _run_ep(args, world, rank, local, device):
     """Returns the measurement dict of the config-4 expert-parallel step on
     this rank (the caller prints rank 0's)."""
@@ -660,6 +685,133 @@ def _run_ep(args, world, rank, local, device):
             "stages_us": {k: round(v["us_per_launch"], 1) for k, v in stages.items()}}
 
 
+def spec_tokens(streams, draft, H, E, k, shared=7, s=1.2, seed=0):
+    """Tokens of a batched speculative-decode verify step with prescribed
+    routing: `streams` streams of 1 + `draft` tokens; expert popularity
+    follows Zipf(s) over a seeded ranking; the tokens of a stream share
+    `shared` of their k experts (drawn per stream) and draw the rest per
+    token.  With the one-hot router of spec_router (logit of expert e =
+    x[:, e]) the chosen experts get distinct logits in [3, 3 + k/8) and every
+    other logit stays below 2, so the top-k sets are known exactly (no bf16
+    ties at the boundary).  Returns x [streams, 1 + draft, H] fp32 and the
+    sets [streams * (1 + draft), k] (ascending)."""
+    rng = np.random.default_rng(seed)
+    Tq = 1 + draft
+    rank = rng.permutation(E)
+    p = 1.0 / np.arange(1, E + 1) ** s
+    p /= p.sum()
+    x = rng.standard_normal((streams * Tq, H)).astype(np.float32)
+    x[:, :E] = np.clip(rng.normal(0.0, 0.4, size=(streams * Tq, E)), -1.5, 1.5)
+    sets = np.zeros((streams * Tq, k), np.int64)
+    for st in range(streams):
+        base = rank[rng.choice(E, size=shared, replace=False, p=p)]
+        for j in range(Tq):
+            t = st * Tq + j
+            q = p.copy()
+            q[np.isin(rank, base)] = 0.0
+            q /= q.sum()
+            own = rank[rng.choice(E, size=k - shared, replace=False, p=q)]
+            chosen = np.concatenate([base, own])
+            lv = 3.0 + 0.125 * rng.permutation(k)          # distinct, exact in bf16
+            x[t, chosen] = lv
+            sets[t] = np.sort(chosen)
+    return x.reshape(streams, Tq, H), sets
+
+
+def spec_router_(blk):
+    """One-hot router: the logit of expert e is x[:, e] exactly."""
+    import torch
+    E, H = blk.gate_weight.shape
+    w = torch.zeros(E, H, device=blk.gate_weight.device)
+    w[torch.arange(E), torch.arange(E)] = 1.0
+    with torch.no_grad():
+        blk.gate_weight.copy_(w.to(torch.bfloat16))
+
+
+def run_spec(args, world, rank, local, device):
+    """Batched speculative decode: 64 streams x (1 + 3 draft) = 256 tokens per
+    verify step through `spec_layers` layers of the decode shape, the experts
+    sharded over the N ranks (the streams split over the ranks), verify
+    semantics (the reference's unsorted stock gathers).  Every step checks
+    each rank's top-k sets against the prescribed ones bit for bit; after the
+    timing, layer 0's expert-parallel output of the rank's tokens against the
+    single-GPU block (the combine)."""
+    import torch
+    from titan_b200 import SparseMoeBlock, _lib, ops
+    from titan_b200.expert_parallel import ExpertParallelMoE, PeerExchange
+    c = CFG2
+    S, D = args.spec_streams, args.spec_draft
+    Tq = 1 + D
+    if S % world:
+        raise SystemExit(f"--spec-streams {S} does not split over {world} ranks")
+    xs, sets = spec_tokens(S, D, c["H"], c["E"], c["k"], seed=77)
+    sl = slice(rank * (S // world), (rank + 1) * (S // world))
+    xr = torch.from_numpy(xs[sl]).to(device).to(torch.bfloat16).contiguous()
+    want = torch.from_numpy(sets.reshape(S, Tq, -1)[sl].reshape(-1, c["k"])).to(device)
+    T = xr.shape[0] * Tq
+    ex = PeerExchange(T, c["H"], c["k"], device=device)
+    layers, full0 = [], None
+    for l in range(args.spec_layers):
+        torch.manual_seed(5000 + l)
+        blk = SparseMoeBlock(c["H"], c["E"], c["k"], c["I"], c["Is"], device=device,
+                             weight_std=0.02)
+        spec_router_(blk)
+        layers.append(ExpertParallelMoE(blk, exchange=ex))
+        if l == 0:
+            full0 = blk
+        del blk
+    torch.cuda.empty_cache()
+    opts = SparseMoeBlock.verify_options()
+    xf = xr.reshape(T, c["H"])
+    bad_routing = 0
+
+    def step(check=False):
+        nonlocal bad_routing
+        for ep in layers:
+            ep(xf, options=opts)
+        if check:
+            idx, _ = ops.router_topk(xf, layers[0].gate_weight, c["k"])
+            got = torch.sort(idx.long(), dim=1).values
+            bad_routing += int((got != want).any(dim=1).sum())
+
+    torch.cuda.synchronize()
+    barrier(world)
+    for _ in range(max(args.warmup, 3)):
+        step(check=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
+    for _ in range(args.steps):          # the per-step checks, outside the timed region
+        step(check=True)
+    y_ep = layers[0](xf, options=opts)
+    y_one = full0(xf, options=opts)
+    mism = int((y_ep.view(torch.int16) != y_one.view(torch.int16)).sum())
+    flags = torch.tensor([bad_routing, mism], device=device, dtype=torch.int64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(flags)
+    ex.check()
+    ex.close()
+    del layers, full0
+    torch.cuda.empty_cache()
+    return {"workload": f"batched speculative decode: {S} streams x (1 + {D} draft) = {S * Tq} "
+                        f"tokens per verify step, {args.spec_layers} layers of the decode shape, "
+                        "Zipf(1.2) expert popularity, the tokens of a stream share 7 of their 10 "
+                        "experts, verify semantics (unsorted stock gathers, token-major combine)",
+            "ms_per_step": round(ms, 4), "us_per_layer": round(1000 * ms / args.spec_layers, 2),
+            "tok_per_s": round(S * Tq / (ms * 1e-3), 1),
+            "topk_mismatched_tokens_all_steps": int(flags[0]),
+            "combine_mismatches_vs_single_gpu": int(flags[1]),
+            "checked_steps": args.steps + max(args.warmup, 3), "parallelism": f"ep{world}"}
+
+
 # -------------------------------------------------------------- CPU baseline
 
 def host_layer(rng, c):
@@ -804,6 +956,8 @@ def run_titan(args, world, rank, local):
     peaks = measured_peaks_all()
     ep = run_ep(args, world, rank, local)
     extras, cb = {}, None
+    if not args.headline_only:
+        extras["spec_decode_config5"] = run_spec_group(args, world, rank, local)
     if world == 1 and not args.headline_only:
         hbm = peaks["hbm_gbs"]
         blocks = build_decode_layers(args.layers, device, seed=1234 + rank)

@@ -164,10 +164,10 @@ __global__ void ep_wait_kernel(const unsigned long long* flags, int W, int epoch
 
 // One thread per rank d: (epoch, counts[d]) into this rank's slot of d's
 // flag row `which`.  The return's rows were stored into the sources' ret rows
-// by the down GEMM's epilogue (GemmParams::y_ptr), an earlier launch on the
-// stream: a kernel's stores, peer stores included, are performed at system
-// scope when it completes (the completion is what makes them visible to the
-// host), so the flag, stored after that, cannot overtake them.
+// by the down GEMM's epilogue (GemmParams::y_ptr / SwParams::y_ptr), an
+// earlier launch on the stream, whose storing threads each end with a
+// system-scope fence; the flag, stored after that launch completed and after
+// this thread's own system-scope fence, cannot overtake them.
 __global__ void ep_post_kernel(EpPostArgs a) {
   const int d = threadIdx.x;
   if (d >= a.world) return;

@@ -306,6 +306,7 @@ __global__ void __launch_bounds__(256) gemm_grouped_kernel(GemmParams P) {
           *reinterpret_cast<uint32_t*>(yrow + col) = v;
         }
       }
+    if (P.y_ptr) __threadfence_system();   // peer stores before the kernel ends
   } else {
     // Fused SwiGLU + per-(row, 64-group) statistics of h.
     float* psum = reinterpret_cast<float*>(smem);          // [128][33]

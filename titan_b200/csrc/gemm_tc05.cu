@@ -419,6 +419,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
           pk.w = (uint32_t)f2bf(acc[8 * v + 6]) | ((uint32_t)f2bf(acc[8 * v + 7]) << 16);
           dst[v] = pk;
         }
+        // stores into other GPUs' memory (the expert-parallel return) are
+        // performed at system scope before this kernel ends, ahead of the
+        // flag the next launch posts
+        if (P.y_ptr) __threadfence_system();
       }
     } else {
       // SwiGLU of the 32 (gate, up) pairs this thread holds; h columns

@@ -153,6 +153,58 @@ class SparseMoeBlock(nn.Module):
         y = y.reshape(shape)
         return (y, idx, sc) if return_routing else y
 
+    # ------------------------------------------------------- verify layout
+    @staticmethod
+    def verify_options() -> _lib.Options:
+        """Options of the target-verify semantics: the reference runs the
+        verify step's experts through unsorted gathers
+        (qwen3_5_moe/language.py:16-41, sorted_indices=False), which the int8
+        overlay does not claim (engine/patches/moe-int8/patch.py:78-102
+        routes only sorted calls), so they are the stock bf16-activation
+        gathers at every size; here the grouped GEMMs at every T."""
+        o = _lib.Options()
+        o.min_tokens, o.down_int8, o.wsum_mode, o.int8_prefill = 1, 0, 0, 0
+        o.gemm_kernel, o.decode_kernel = 0, 0
+        return o
+
+    def forward_verify(self, x: torch.Tensor, return_routing: bool = False):
+        """The speculative-decode verify step on x [B, T, H] (B streams of T =
+        1 + draft tokens): every token of every stream routed and combined at
+        once, the expert outputs token-major (the layout of
+        _target_verify_switch_glu) and the weighted sum without an unsort
+        permutation (round3/small-items REPORT.md:7-12).  y [B, T, H]."""
+        if x.dim() != 3:
+            raise _lib.InvalidArgument("forward_verify takes x [B, T, H]")
+        return self.forward(x, options=self.verify_options(), return_routing=return_routing)
+
+    def forward_verify_modular(self, x: torch.Tensor):
+        """The verify step op by op: router, the unsorted SwitchGLU (stock
+        gathers), the token-major weighted sum, the gated shared expert."""
+        if x.dim() != 3:
+            raise _lib.InvalidArgument("forward_verify_modular takes x [B, T, H]")
+        B, T, H = x.shape
+        xf = x.reshape(B * T, H).contiguous()
+        inds, scores = ops.router_topk(xf, self.gate_weight, self.top_k)
+        sm = self.switch_mlp
+        xe = xf.unsqueeze(-2)
+        gu = ops.gather_qmm(xe.expand(-1, self.top_k, -1).reshape(-1, 1, H),
+                            sm.gate_up_proj.weight, sm.gate_up_proj.scales,
+                            sm.gate_up_proj.biases,
+                            rhs_indices=inds.reshape(-1), sorted_indices=False)
+        g, u = gu.reshape(-1, 2 * self.moe_inter).chunk(2, dim=-1)
+        h = ops.swiglu(u.contiguous(), g.contiguous())
+        yk = ops.gather_qmm(h.unsqueeze(-2), sm.down_proj.weight, sm.down_proj.scales,
+                            sm.down_proj.biases, rhs_indices=inds.reshape(-1),
+                            sorted_indices=False)
+        y = ops.weighted_sum(yk.reshape(B * T, self.top_k, H), None, scores, (B * T, H))
+        if self.shared_expert is not None:
+            sh = self.shared_expert(xf)
+            gl = (xf.float() @ self.shared_expert_gate_weight.float().t())
+            sg = torch.sigmoid(gl.to(torch.bfloat16).float()).to(torch.bfloat16)
+            sh = (sg.float() * sh.float()).to(torch.bfloat16)
+            y = (y.float() + sh.float()).to(torch.bfloat16)
+        return y.reshape(B, T, H)
+
     def forward_modular(self, x: torch.Tensor):
         """The reference block op by op (qwen3_5_moe/language.py:60-91)."""
         shape = x.shape
