@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--traffic-file", default=os.path.join(ROOT, "profiles", "traffic.txt"))
-    ap.add_argument("--profile", choices=("decode", "prefill"), default=None,
+    ap.add_argument("--profile", choices=("decode", "prefill", "ep"), default=None,
                     help="run a small untimed case for an ncu capture and exit")
     ap.add_argument("--gemm-kernel", type=int, default=0,
                     help="prefill grouped GEMMs: 0 tcgen05 (default), 1 mma.sync baseline")
@@ -1021,8 +1021,10 @@ def run_titan(args, world, rank, local):
 
 def run_profile_case(args):
     """A small untimed case of one path, for ncu captures (bench numbers are
-    never taken from it): decode = 2 config-2 layers at T=1, 3 steps;
-    prefill = one config-3 block at the first --prefill-T, 2 calls."""
+    never taken from it): decode = 2 decode-shape layers at T=1, 3 steps;
+    prefill = one cold-prefill block at the first --prefill-T, 2 calls;
+    ep = one decode-shape layer with the Zipf(1.1) router on --ep-tokens
+    tokens on one GPU (the grouped GEMMs of the headline step at N=1), 2 calls."""
     import torch
     from titan_b200 import SparseMoeBlock, _lib
     device = torch.device("cuda", 0)
@@ -1033,6 +1035,22 @@ def run_profile_case(args):
         for _ in range(3):
             for b in blocks:
                 b(x, options=opts)
+    elif args.profile == "ep":
+        c = CFG2
+        torch.manual_seed(4321)
+        blk = SparseMoeBlock(c["H"], c["E"], c["k"], c["I"], c["Is"], device=device,
+                             weight_std=0.02)
+        zipf_router_(blk, torch.Generator().manual_seed(777))
+        blk.prepare()
+        o = _lib.Options()
+        o.min_tokens, o.int8_prefill, o.down_int8, o.wsum_mode = 1, 1, 1, 0
+        o.gemm_kernel = args.gemm_kernel
+        g = torch.Generator(device=device).manual_seed(9000)
+        x = torch.randn(args.ep_tokens, c["H"], generator=g, device=device)
+        x[:, 0] = 1.0
+        x = x.to(torch.bfloat16)
+        for _ in range(2):
+            blk(x, options=o)
     else:
         c = CFG3
         T = int(args.prefill_T.split(",")[0])

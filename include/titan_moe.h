@@ -259,6 +259,36 @@ int tmoe_moe_forward(const tmoe_layer* layer, const uint16_t* x, int T, const tm
                      void* ws, size_t ws_bytes, uint16_t* y, int32_t* idx_out,
                      uint16_t* scores_out, void* stream);
 
+/* ------------------------------------------------ the decoder sub-layer */
+
+/* RMSNorm with weight: out = bf16((x * r) * w), r = 1 / sqrt(mean(x^2) + eps)
+ * in fp32 (the post-attention norm feeding the MoE block,
+ * titan/adapters/mlx/vendor/mlx_vlm/models/qwen3_5_moe/language.py:103-107,137,
+ * nn.RMSNorm).  x, out [T, H] bf16; weight [H] bf16. */
+int tmoe_rmsnorm(const uint16_t* x, const uint16_t* weight, int T, int H, float eps, uint16_t* out,
+                 void* stream);
+
+/* Write a branch output back into the residual stream.  nstreams = 0: the
+ * decoder layer's residual add out = bf16(residual + branch) [T, H]
+ * (qwen3_5_moe/language.py:137).  nstreams = n > 0: the hyper-connection
+ * inject into an n-wide stream, out[t, j] = bf16(residual[t, j] +
+ * bf16(branch[t] * weights[t, j])), residual / out [T, n, H], weights [T, n]
+ * bf16 (qwen4_exp/language.py:3198-3218, _hyper_inject). */
+int tmoe_residual_inject(const uint16_t* branch, const uint16_t* residual, const uint16_t* weights,
+                         int T, int H, int nstreams, uint16_t* out, void* stream);
+
+/* The MoE sub-layer of a decoder layer in one call: the post-attention
+ * RMSNorm of h, the block (tmoe_moe_forward), and the write-back:
+ * nstreams = 0: out = h + block(norm(h)) (qwen3_5_moe/language.py:136-137);
+ * nstreams = n: out = inject(residual [T, n, H], block(norm(h)), weights
+ * [T, n]) (qwen4_exp/language.py:3338-3343).  The workspace follows
+ * tmoe_moe_forward's rules (zero-filled once when allocated). */
+size_t tmoe_moe_sublayer_workspace_size(const tmoe_layer* layer, int T, const tmoe_options* opt);
+int tmoe_moe_sublayer(const tmoe_layer* layer, const uint16_t* norm_weight, float eps,
+                      const uint16_t* h, int T, const uint16_t* residual,
+                      const uint16_t* inject_weights, int nstreams, const tmoe_options* opt,
+                      void* ws, size_t ws_bytes, uint16_t* out, void* stream);
+
 /* Expert parallelism (no reference counterpart: the reference runs one
  * device).  Experts are sharded e // (E / W) over W ranks; these two calls are
  * the two halves of Qwen3_5MoeSparseMoeBlock.__call__ (language.py:74-91)

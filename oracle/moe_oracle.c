@@ -704,3 +704,43 @@ void orc_moe_decode(const orc_moe_desc* d, const uint16_t* x, int32_t* idx_out,
     if (scores_out) memcpy(scores_out, sc, sizeof(uint16_t) * (size_t)T * k);
     free(idx); free(sc);
 }
+
+/* ------------------------------------------- the steps either side of the block
+ * RMSNorm (qwen3_5_moe/language.py:103-107, 137): lane partials over
+ * e = 32c + l (fma, c ascending), the xor butterfly; ms = sum / H;
+ * r = 1 / sqrt(ms + eps); out = bf16((x * r) * w).  Residual write-back:
+ * n = 0: out = bf16(branch + residual); n > 0 (hyper-connection inject,
+ * qwen4_exp/language.py:3198-3218): out[t, j] = bf16(residual[t, j] +
+ * bf16(branch[t] * w[t, j])). */
+void orc_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps, uint16_t* out) {
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < T; ++t) {
+        const uint16_t* xr = x + (size_t)t * H;
+        float part[32];
+        for (int l = 0; l < 32; ++l) {
+            float s = 0.0f;
+            for (int e = l; e < H; e += 32) {
+                float v = bf2f(xr[e]);
+                s = fmaf(v, v, s);
+            }
+            part[l] = s;
+        }
+        float s = butterfly32(part);
+        float ms = s / (float)H;
+        float r = 1.0f / sqrtf(ms + eps);
+        for (int e = 0; e < H; ++e) out[(size_t)t * H + e] = f2bf((bf2f(xr[e]) * r) * bf2f(w[e]));
+    }
+}
+
+void orc_inject(const uint16_t* branch, const uint16_t* res, const uint16_t* wts, int T, int H,
+                int n, uint16_t* out) {
+    int ns = n > 0 ? n : 1;
+    for (int t = 0; t < T; ++t)
+        for (int j = 0; j < ns; ++j)
+            for (int c = 0; c < H; ++c) {
+                size_t i = ((size_t)t * ns + j) * H + c;
+                float b = bf2f(branch[(size_t)t * H + c]);
+                float p = n > 0 ? bf2f(f2bf(b * bf2f(wts[(size_t)t * n + j]))) : b;
+                out[i] = f2bf(p + bf2f(res[i]));
+            }
+}

@@ -50,6 +50,8 @@ def lib():
             "orc_moe_prefill": ([P, P, i32, P, P, P], None),
             "orc_set_parts_out": ([P, P, P], None),
             "orc_moe_decode": ([P, P, P, P, P], None),
+            "orc_rmsnorm": ([P, P, i32, i32, C.c_float, P], None),
+            "orc_inject": ([P, P, P, i32, i32, i32, P], None),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -318,3 +320,24 @@ def moe_decode(layer: Layer, x):
     sc = np.zeros((T, layer.k), np.uint16)
     lib().orc_moe_decode(C.byref(d), _p(np.ascontiguousarray(x)), _p(idx), _p(sc), _p(y))
     return y, idx, sc
+
+
+def rmsnorm(x, w, eps=1e-6):
+    """RMSNorm of bf16 rows x [T, H] with weight w [H] (canonical order)."""
+    T, H = x.shape
+    out = np.zeros((T, H), np.uint16)
+    lib().orc_rmsnorm(_p(np.ascontiguousarray(x)), _p(np.ascontiguousarray(w)), T, H,
+                      float(eps), _p(out))
+    return out
+
+
+def inject(branch, residual, weights=None):
+    """Residual write-back: n = 0 (weights None) bf16(branch + residual) [T, H];
+    else the hyper-connection inject into residual [T, n, H] with weights [T, n]."""
+    T, H = branch.shape
+    n = 0 if weights is None else weights.shape[1]
+    out = np.zeros(residual.shape, np.uint16)
+    lib().orc_inject(_p(np.ascontiguousarray(branch)), _p(np.ascontiguousarray(residual)),
+                     _p(None if weights is None else np.ascontiguousarray(weights)), T, H, n,
+                     _p(out))
+    return out

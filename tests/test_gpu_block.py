@@ -138,6 +138,53 @@ def test_decode_single_launch_repeats_and_graph(cuda, oracle):
     assert _lib.load().tmoe_device_status() == 0
 
 
+@pytest.mark.parametrize("T", [2, 4, 8])
+def test_decode_full_expert_count_small_batches(cuda, oracle, T):
+    """The 512-expert decode shape at T = 2, 4 (one launch) and 8 (three
+    launches) against the oracle: routing and scores bit-exact, output within
+    tolerance of the fp32 golden."""
+    from titan_b200 import SparseMoeBlock
+    torch.manual_seed(60 + T)
+    blk = SparseMoeBlock(2048, 512, 10, 512, 512, device=cuda)
+    L = layer_from_block(oracle, blk)
+    x = oracle.make_x(T, 2048, seed=600 + T)
+    y, idx, sc = blk(bf(x), options=_opts(512), return_routing=True)
+    ry, ridx, rsc = oracle.moe_decode(L, x)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    assert np.array_equal(nbf(sc), rsc)
+    assert_bf16_close(nbf(y), ry, what=f"decode E=512 T={T}")
+
+
+def test_zipf_routing_subset_matches_oracle(cuda, oracle):
+    """The expert-parallel workload's Zipf(1.1) router (one column of the
+    router carries -1.1 log(rank), x[:, 0] = 1): the router's top-k over a
+    batch of 8192 tokens bit-exact for every token, the skew as intended, and
+    the whole block on a token subset against the oracle."""
+    import bench
+    from titan_b200 import SparseMoeBlock, ops
+    torch.manual_seed(4321)
+    blk = SparseMoeBlock(2048, 512, 10, 512, 512, device=cuda, weight_std=0.02)
+    bench.zipf_router_(blk, torch.Generator().manual_seed(777))
+    L = layer_from_block(oracle, blk)
+    g = torch.Generator(device=cuda).manual_seed(9000)
+    xt = torch.randn(8192, 2048, generator=g, device=cuda)
+    xt[:, 0] = 1.0
+    xt = xt.to(torch.bfloat16)
+    idx, sc = ops.router_topk(xt, blk.gate_weight, 10)
+    x = nbf(xt)
+    ridx, rsc, _, _ = oracle.router(x, L.wr, 10)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    assert np.array_equal(nbf(sc), rsc)
+    counts = np.bincount(ridx.reshape(-1), minlength=512)
+    top10 = np.sort(counts)[::-1][:10].sum() / counts.sum()
+    assert top10 > 0.3                                   # heavily skewed, as Zipf(1.1) is
+    sub = np.r_[0:6, 4096:4102, 8186:8192]
+    xs = np.ascontiguousarray(x[sub])
+    y = blk(bf(xs), options=_opts(min_tokens=1))
+    ry, _, _, ops_ = oracle.moe_prefill(L, xs, int8_mode=3, parts=True)
+    assert_bf16_close(nbf(y), ry, what="Zipf subset", operands=ops_)
+
+
 def test_decode_block_full_expert_count(cuda, oracle):
     """The decode shape: H=2048, 512 experts + shared, k=10, I=512."""
     from titan_b200 import SparseMoeBlock
@@ -330,3 +377,47 @@ def test_prefill_full_size_config3(cuda, oracle, T):
     yf = f32(nbf(y))
     assert np.isfinite(yf).all()
     assert 0.001 < float(np.sqrt((yf ** 2).mean())) < 10.0
+
+
+def _decode_range_child(q):
+    try:
+        import torch
+        from titan_b200 import SparseMoeBlock, _lib
+        torch.cuda.set_device(0)
+        torch.manual_seed(3)
+        blk = SparseMoeBlock(2048, 64, 10, 512, 512, device="cuda")
+        lib = _lib.load()
+        xn = torch.randn(2, 2048, device="cuda").to(torch.bfloat16)
+        dec = _opts(512)
+        blk(xn, options=dec)
+        blk(xn, options=_opts(512, decode_kernel=1))
+        torch.cuda.synchronize()
+        st0 = int(lib.tmoe_device_status())
+        xl = (torch.randn(2, 2048, device="cuda") * 1e5).to(torch.bfloat16)
+        yp = blk(xl, options=_opts(1))                       # grouped GEMMs: range-safe
+        torch.cuda.synchronize()
+        st1 = int(lib.tmoe_device_status())
+        finite = bool(torch.isfinite(yp.float()).all())
+        blk(xl, options=dec)                                 # decode: flagged
+        torch.cuda.synchronize()
+        st2 = int(lib.tmoe_device_status())
+        q.put((st0, st1, finite, st2, None))
+    except Exception as exc:
+        q.put((None, None, None, None, repr(exc)))
+
+
+def test_decode_out_of_range_activations_are_reported():
+    """Decode stages bf16 x as fp16: a group past fp16's range is reported by
+    tmoe_device_status as Unsupported (2) instead of passing silently, while
+    the grouped-GEMM path takes the same tokens exactly.  In a child process:
+    the report is sticky for the life of the library."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_decode_range_child, args=(q,))
+    p.start()
+    st0, st1, finite, st2, err = q.get(timeout=300)
+    p.join(timeout=60)
+    assert err is None, err
+    assert st0 == 0 and st1 == 0 and finite
+    assert st2 == 2

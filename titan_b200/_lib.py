@@ -126,6 +126,10 @@ _SIGS = {
     "tmoe_ep_wait": ([P, P, I32, I32, I32, P, P], I32),
     "tmoe_ep_post": ([I32, P, I32, I32, P, P, I32, P], I32),
     "tmoe_prepare_row_scale": ([P, P, I32, I32, I32, P, P], I32),
+    "tmoe_rmsnorm": ([P, P, I32, I32, C.c_float, P, P], I32),
+    "tmoe_residual_inject": ([P, P, P, I32, I32, I32, P, P], I32),
+    "tmoe_moe_sublayer_workspace_size": ([P, I32, P], SZ),
+    "tmoe_moe_sublayer": ([P, P, C.c_float, P, I32, P, P, I32, P, P, SZ, P, P], I32),
     "tmoe_ep_post_return": ([P, I32, I32, P, P, I32, P], I32),
     "tmoe_ep_guard": ([P, I32, P, I64, P], I32),
 }

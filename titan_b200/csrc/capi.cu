@@ -94,7 +94,13 @@ int tmoe_device_status(void) {
     return fail(TMOE_ERR_TIMEOUT, "a tcgen05 kernel's bounded wait timed out");
   if (ep_error_flag())
     return fail(TMOE_ERR_TIMEOUT, "an expert-parallel exchange wait timed out");
-  if (layer_error_flag())
+  const int le = layer_error_flag();
+  if (le == 2 || decode_range_flag())
+    return fail(TMOE_ERR_UNSUPPORTED,
+                "a decode-path activation group lay outside fp16's exact range (|x| >= 65504, "
+                "or the whole group below 2^-14); run such tokens through the grouped-GEMM "
+                "path (options.min_tokens <= T), which normalises x by a power of two");
+  if (le)
     return fail(TMOE_ERR_TIMEOUT, "a grid barrier of the single-launch decode layer timed out");
   return TMOE_OK;
 }
@@ -1158,6 +1164,61 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   TMOE_TRY(launch_wsum(b.ys, b.inv, scores, T, k, H, opt_wsum(opt), Is > 0 ? b.ys_sh : nullptr,
                        b.gate_logit, y, s),
            "weighted_sum");
+  return TMOE_OK;
+}
+
+// ------------------------------------------------------- decoder sub-layer
+
+int tmoe_rmsnorm(const uint16_t* x, const uint16_t* weight, int T, int H, float eps, uint16_t* out,
+                 void* stream) {
+  if (!x || !weight || !out || T < 0 || H <= 0 || !(eps >= 0.0f))
+    return fail(TMOE_ERR_INVALID, "tmoe_rmsnorm: bad arguments");
+  TMOE_TRY(launch_rmsnorm(x, weight, T, H, eps, out, S(stream)), "rmsnorm");
+  return TMOE_OK;
+}
+
+int tmoe_residual_inject(const uint16_t* branch, const uint16_t* residual, const uint16_t* weights,
+                         int T, int H, int nstreams, uint16_t* out, void* stream) {
+  if (!branch || !residual || !out || T < 0 || H <= 0 || nstreams < 0 || nstreams > 64 ||
+      (nstreams > 0 && !weights))
+    return fail(TMOE_ERR_INVALID, "tmoe_residual_inject: bad arguments");
+  TMOE_TRY(launch_inject(branch, residual, weights, T, H, nstreams, out, S(stream)), "inject");
+  return TMOE_OK;
+}
+
+size_t tmoe_moe_sublayer_workspace_size(const tmoe_layer* L, int T, const tmoe_options* opt) {
+  if (!L || T < 0) return 0;
+  Carve c(nullptr);
+  c.take<uint16_t>((size_t)T * L->hidden);     // normed x
+  c.take<uint16_t>((size_t)T * L->hidden);     // the block's output
+  c.off = (c.off + 255) & ~size_t(255);
+  return c.off + tmoe_moe_workspace_size(L, T, opt);
+}
+
+int tmoe_moe_sublayer(const tmoe_layer* L, const uint16_t* norm_weight, float eps,
+                      const uint16_t* h, int T, const uint16_t* residual,
+                      const uint16_t* inject_weights, int nstreams, const tmoe_options* opt,
+                      void* ws, size_t ws_bytes, uint16_t* out, void* stream) {
+  if (!L || !norm_weight || T < 0 || nstreams < 0 || nstreams > 64 ||
+      (T > 0 && (!h || !out || (nstreams > 0 && (!residual || !inject_weights)))))
+    return fail(TMOE_ERR_INVALID, "tmoe_moe_sublayer: bad arguments");
+  if (int rc = check_layer(L, T, opt)) return rc;
+  if (T == 0) return TMOE_OK;
+  const size_t need = tmoe_moe_sublayer_workspace_size(L, T, opt);
+  if (!ws || ws_bytes < need)
+    return fail(TMOE_ERR_WORKSPACE, "tmoe_moe_sublayer: workspace %zu < %zu bytes", ws_bytes, need);
+  const int H = L->hidden;
+  Carve c(ws);
+  uint16_t* xn = c.take<uint16_t>((size_t)T * H);
+  uint16_t* y = c.take<uint16_t>((size_t)T * H);
+  c.off = (c.off + 255) & ~size_t(255);
+  void* bws = static_cast<uint8_t*>(ws) + c.off;
+  cudaStream_t s = S(stream);
+  TMOE_TRY(launch_rmsnorm(h, norm_weight, T, H, eps, xn, s), "rmsnorm");
+  if (int rc = tmoe_moe_forward(L, xn, T, opt, bws, ws_bytes - c.off, y, nullptr, nullptr, stream))
+    return rc;
+  TMOE_TRY(launch_inject(y, nstreams > 0 ? residual : h, inject_weights, T, H, nstreams, out, s),
+           "inject");
   return TMOE_OK;
 }
 

@@ -34,6 +34,12 @@ TMOE_DEV uint16_t f2bf(float f) {
 
 TMOE_DEV float bfround(float f) { return bf2f(f2bf(f)); }
 
+// A group of activations whose largest magnitude is gmax is exact as fp16
+// values: below fp16's overflow and not wholly below its normal range.
+TMOE_DEV bool fp16_group_ok(float gmax) {
+  return gmax < 65504.0f && !(gmax > 0.0f && gmax < 6.103515625e-05f);
+}
+
 // e^x, the canonical sequence (see file header).
 TMOE_DEV float cexp(float x) {
   if (x != x) return x;

@@ -32,6 +32,14 @@
 
 namespace tmoe {
 
+__device__ int g_decode_range = 0;   // bf16 x outside fp16's exact range (sticky)
+
+int decode_range_flag() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_decode_range, sizeof(int));
+  return v;
+}
+
 namespace {
 
 constexpr int kSlabRows = 32;   // weight rows per CTA (two m16 tiles)
@@ -109,7 +117,7 @@ TMOE_DEV void convert_columns(const GemvPlan& L, uint8_t* wsm, int nc, int kq, i
     const uint8_t* raw = wsm + L.raw_off + c * L.rstride;
     for (int b0 = 0; b0 < nblk; b0 += 32) {
       const int b = b0 + lane;
-      float sum = 0.0f;
+      float sum = 0.0f, bmax = 0.0f;
       if (b < nblk) {
         float v[16];
         if (MODE == 1) {
@@ -130,6 +138,7 @@ TMOE_DEV void convert_columns(const GemvPlan& L, uint8_t* wsm, int nc, int kq, i
           for (int q = 0; q < 8; ++q) {
             v[2 * q] = bf2f((uint16_t)(w8[q] & 0xffffu));
             v[2 * q + 1] = bf2f((uint16_t)(w8[q] >> 16));
+            bmax = fmaxf(bmax, fmaxf(fabsf(v[2 * q]), fabsf(v[2 * q + 1])));
           }
         }
         uint16_t hv[16], lv[16];
@@ -162,7 +171,13 @@ TMOE_DEV void convert_columns(const GemvPlan& L, uint8_t* wsm, int nc, int kq, i
       // four consecutive blocks make one 64-group
       sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
       sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
-      if (b < nblk && (lane & 3) == 0) xs[b >> 2] = sum;
+      bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
+      bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
+      if (b < nblk && (lane & 3) == 0) {
+        xs[b >> 2] = sum;
+        // bf16 x is staged as one fp16 value: exact only inside fp16's range
+        if (MODE != 1 && !fp16_group_ok(bmax)) atomicExch(&g_decode_range, 1);
+      }
     }
   }
 }

@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
     const int nblk = T * (H / 16);
     for (int base = 0; base < nblk; base += kLThreads) {
       const int b = base + tid;
-      float sum = 0.0f;
+      float sum = 0.0f, bmax = 0.0f;
       if (b < nblk) {
         const int tt = b / (H / 16), bb = b % (H / 16);
         const uint4* src = reinterpret_cast<const uint4*>(A.x + (size_t)tt * H + bb * 16);
@@ -410,6 +410,7 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float v0 = bf2f((uint16_t)(w8[q] & 0xffffu)), v1 = bf2f((uint16_t)(w8[q] >> 16));
+          bmax = fmaxf(bmax, fmaxf(fabsf(v0), fabsf(v1)));
           const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
           hv[f16p_pos(2 * q)] = __half_as_ushort(h0);
           hv[f16p_pos(2 * q + 1)] = __half_as_ushort(h1);
@@ -424,7 +425,13 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
       }
       sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
       sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
-      if (b < nblk && (b & 3) == 0) xs[(b / (H / 16)) * G + (b % (H / 16)) / 4] = sum;
+      bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
+      bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
+      if (b < nblk && (b & 3) == 0) {
+        xs[(b / (H / 16)) * G + (b % (H / 16)) / 4] = sum;
+        // x is staged as fp16: exact only inside fp16's normal range
+        if (c == 0 && !fp16_group_ok(bmax)) atomicExch(&g_layer_error, 2);
+      }
     }
   }
   __syncthreads();
@@ -787,7 +794,9 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
   }
   cp_async_wait_n<0>();
   __syncthreads();
-  // weighted sum in slot order + the gated shared expert, per output slab
+  // weighted sum in slot order + the gated shared expert, per output slab; a
+  // CTA whose wait gave up writes NaN, so its slabs cannot pass for a result
+  const bool failed = *(volatile int*)&s_abort != 0;
   for (int js = 0; js < W.nslab_c; ++js) {
     const int slab = c + js * nct;
     const float* rs = res + (size_t)js * (R + T) * 16;
@@ -796,7 +805,7 @@ __global__ void __launch_bounds__(kLThreads, 1) decode_layer_kernel(LayerArgs A)
       float a = 0.0f;
       for (int j = 0; j < k; ++j) a = __fmaf_rn(s_score[tt * k + j], rs[(tt * k + j) * 16 + r], a);
       if (Is > 0) a = __fmaf_rn(s_gate[tt], rs[(R + tt) * 16 + r], a);
-      A.y[(size_t)tt * H + slab * 16 + r] = f2bf(a);
+      A.y[(size_t)tt * H + slab * 16 + r] = failed ? (uint16_t)0x7fc0u : f2bf(a);
     }
   }
 }
@@ -830,7 +839,21 @@ cudaError_t launch_decode_layer(const LayerArgs& a, int ns, cudaStream_t s) {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kLThreads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;   // the CTAs could not all be resident
-    return launch_pdl(kernel, dim3(nct), dim3(kLThreads), smem, s, a);
+    // cooperative: the driver guarantees every CTA is resident at once (the
+    // CTAs wait for each other's data) or refuses the launch
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nct);
+    cfg.blockDim = dim3(kLThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kernel, a);
   };
   if (ns == 4) err = go(decode_layer_kernel<4>);
   else if (ns == 3) err = go(decode_layer_kernel<3>);

@@ -198,6 +198,7 @@ int decode_layer_ctas();
 size_t decode_layer_smem(int T, int H, int E, int k, int I, int Is, int nct, int ns);
 cudaError_t launch_decode_layer(const LayerArgs& a, int ns, cudaStream_t s);
 int layer_error_flag();
+int decode_range_flag();
 
 // Expert-parallel exchanges over peer memory (ep_p2p.cu).
 struct EpDispatchArgs {
@@ -253,6 +254,12 @@ cudaError_t launch_dense_tiles(int R, int tile_m, int32_t* tile_row, int32_t* ti
 cudaError_t ensure_smem_attr(const void* func, int bytes);
 // SMs of the current device, cached per device; thread-safe.
 int device_sm_count();
+
+// The decoder-layer steps either side of the block (norm.cu).
+cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps,
+                           uint16_t* out, cudaStream_t s);
+cudaError_t launch_inject(const uint16_t* branch, const uint16_t* hyper, const uint16_t* wts, int T,
+                          int H, int n, uint16_t* out, cudaStream_t s);
 
 // Records `msg` as this thread's tmoe_last_error() text and returns `code`.
 int record_error(int code, const char* msg);

@@ -153,6 +153,43 @@ class SparseMoeBlock(nn.Module):
         y = y.reshape(shape)
         return (y, idx, sc) if return_routing else y
 
+    # --------------------------------------------------- decoder sub-layer
+    def forward_sublayer(self, h: torch.Tensor, norm_weight: torch.Tensor, eps: float = 1e-6,
+                         residual: torch.Tensor | None = None,
+                         inject_weights: torch.Tensor | None = None,
+                         options: _lib.Options | None = None) -> torch.Tensor:
+        """The MoE half of a decoder layer in one C-ABI call
+        (tmoe_moe_sublayer): out = h + block(rmsnorm(h))
+        (qwen3_5_moe/language.py:136-137), or with inject_weights [T, n] the
+        hyper-connection inject of block(rmsnorm(h)) into residual [T, n, H]
+        (qwen4_exp/language.py:3338-3343)."""
+        H = self.hidden
+        hf = h.reshape(-1, H)
+        if hf.dtype != torch.bfloat16:
+            raise _lib.InvalidArgument("forward_sublayer takes bf16 activations")
+        hf = hf.contiguous()
+        T = hf.shape[0]
+        n = 0 if inject_weights is None else inject_weights.shape[-1]
+        if n and residual is None:
+            raise _lib.InvalidArgument("the hyper-connection inject needs the residual stream")
+        out = torch.empty((T, n, H) if n else (T, H), dtype=torch.bfloat16, device=hf.device)
+        if T == 0:
+            return out
+        L = self.layer_struct()
+        opt = options if options is not None else patch.block_options()
+        lib = _lib.load()
+        nb = lib.tmoe_moe_sublayer_workspace_size(C.byref(L), T, C.byref(opt))
+        ws = ops.workspace(nb, hf.device, "moe_sublayer")
+        nw = norm_weight.to(torch.bfloat16).contiguous()
+        res = residual.to(torch.bfloat16).contiguous() if n else None
+        wts = inject_weights.to(torch.bfloat16).reshape(T, n).contiguous() if n else None
+        _lib.check(lib.tmoe_moe_sublayer(C.byref(L), nw.data_ptr(), float(eps), hf.data_ptr(), T,
+                                         res.data_ptr() if n else None,
+                                         wts.data_ptr() if n else None, n, C.byref(opt),
+                                         ws.data_ptr(), ws.numel(), out.data_ptr(),
+                                         ops.stream_ptr(hf.device)), "tmoe_moe_sublayer")
+        return out
+
     # ------------------------------------------------------- verify layout
     @staticmethod
     def verify_options() -> _lib.Options:

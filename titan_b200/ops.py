@@ -422,3 +422,32 @@ def down_wsum(h, weight, scales, biases, idx, scores, group_size=GROUP):
               _p(_bf16(biases, "biases")), _p(idx), _p(sc), T, k, E, I, D, _p(ws), ws.numel(), _p(y),
               stream_ptr(h.device))
     return y
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """nn.RMSNorm (qwen3_5_moe/language.py:103-107): bf16 rows x [..., H]."""
+    _need_cuda(x, weight)
+    H = x.shape[-1]
+    xf = _bf16(x, "x").reshape(-1, H).contiguous()
+    w = _bf16(weight, "weight").contiguous()
+    out = torch.empty_like(xf)
+    _lib.call("tmoe_rmsnorm", _p(xf), _p(w), xf.shape[0], H, float(eps), _p(out),
+              stream_ptr(x.device))
+    return out.reshape(x.shape)
+
+
+def residual_inject(branch: torch.Tensor, residual: torch.Tensor,
+                    weights: torch.Tensor | None = None) -> torch.Tensor:
+    """The write-back of a branch: branch + residual, or with weights [T, n]
+    the hyper-connection inject into residual [T, n, H]
+    (qwen4_exp/language.py:3198-3218)."""
+    _need_cuda(branch, residual)
+    H = branch.shape[-1]
+    b = _bf16(branch, "branch").reshape(-1, H).contiguous()
+    r = _bf16(residual, "residual").contiguous()
+    n = 0 if weights is None else weights.shape[-1]
+    w = None if weights is None else _bf16(weights, "weights").reshape(-1, n).contiguous()
+    out = torch.empty_like(r)
+    _lib.call("tmoe_residual_inject", _p(b), _p(r), _p(w), b.shape[0], H, n, _p(out),
+              stream_ptr(branch.device))
+    return out
