@@ -227,8 +227,8 @@ size_t carve_int8_gather(Carve& c, int R, int E, int K, Int8GatherWs* w) {
   t.tile_exp = c.take<int32_t>(maxt);
   t.ntiles = c.take<int32_t>(1);
   t.xq = c.take<int8_t>((size_t)R * K * 2);     // fp16 codes of the tcgen05 operand layout
-  t.xsc = c.take<float>((size_t)R * (K / 64));
-  t.xrs = c.take<float>((size_t)R * (K / 64));
+  t.xsc = c.take<float>((size_t)R * tc05_srow(K / 64));
+  t.xrs = c.take<float>((size_t)R * tc05_srow(K / 64));
   t.route_scratch = c.take<uint8_t>(route_plan_scratch_bytes(R, E));
   if (w) *w = t;
   return c.off;
@@ -267,17 +267,29 @@ int tmoe_gather_qmm_int8(const uint16_t* x, const uint32_t* w, const uint16_t* s
   p.ntiles = b.ntiles;
   cudaStream_t s = S(stream);
   TMOE_TRY(launch_route_plan(rhs, R, E, kTileM, maxt, p, b.route_scratch, s), "route_plan");
-  TMOE_TRY(launch_prep_a16(x, R, K, true, reinterpret_cast<uint16_t*>(b.xq), b.xsc, b.xrs, s),
-           "quantize_rows");
+  const bool tc = gemm_tc05_supported(K, N);
   GemmParams g{};
-  g.A = b.xq;
+  if (tc) {
+    // expert-sorted operand rows: row r quantises x row order[r]
+    const int gs = tc05_srow(K / 64);
+    TMOE_TRY(launch_prep_a16_rows(x, R, K, true, b.order, nullptr, 1, gs,
+                                  reinterpret_cast<uint16_t*>(b.xq), b.xsc, b.xrs, s),
+             "quantize_rows");
+    g.A = b.xq;
+    g.s_r = gs;
+    g.a_nrows = R;
+  } else {
+    TMOE_TRY(launch_quantize_rows(x, R, K, b.xq, b.xsc, b.xrs, s), "quantize_rows");
+    g.A = b.xq;
+    g.s_r = K / 64;
+    g.a_rows = b.order;
+    g.a_div = 1;
+  }
   g.asc = b.xsc;
   g.ars = b.xrs;
-  g.s_r = K / 64;
   g.s_g = 1;
-  g.a_rows = b.order;
-  g.a_div = 1;
   g.W = w;
+  g.E = E;
   g.st = scales_t;
   g.bt = biases_t;
   g.tile_row = b.tile_row;
@@ -288,8 +300,12 @@ int tmoe_gather_qmm_int8(const uint16_t* x, const uint32_t* w, const uint16_t* s
   g.N = N;
   g.Y = y;
   g.y_rows = b.order;
-  // the per-group tcgen05 kernel: the overlay's int8 algebra bit for bit
-  TMOE_TRY(launch_gemm_tc05(true, kEpiStore, g, maxt, s), "gemm_int8");
+  // the per-group tcgen05 kernel (mma.sync for K > 3072 or N % 128 != 0): the
+  // overlay's int8 algebra bit for bit
+  if (tc)
+    TMOE_TRY(launch_gemm_tc05(true, kEpiStore, g, maxt, s), "gemm_int8");
+  else
+    TMOE_TRY(launch_gemm_grouped(true, kEpiStore, g, maxt, s), "gemm_int8");
   return TMOE_OK;
 }
 
@@ -429,6 +445,7 @@ int tmoe_gather_qmm_bf16(const uint16_t* x, const uint32_t* w, const uint16_t* s
     g.a_rows = b.order;
     g.a_div = 1;
     g.W = w;
+    g.E = E;
     g.st = scales_t;
     g.bt = biases_t;
     g.tile_row = b.tile_row;
@@ -757,6 +774,14 @@ int opt_int8(const tmoe_options* o) { return o ? (o->int8_prefill != 0) : 1; }
 int opt_gemm(const tmoe_options* o) { return o ? o->gemm_kernel : 0; }
 // the tile-per-CTA tcgen05 kernel (else mma.sync) where the swap-AB one is not used
 int opt_tc05(const tmoe_options* o) { return opt_gemm(o) != 1; }
+// The per-group tcgen05 kernel runs every grouped GEMM of the layer when it is
+// selected and takes all of the layer's shapes (K <= 3072, N % 128 == 0);
+// otherwise the mma.sync kernel does.
+bool tc05_layer(const tmoe_layer* L, const tmoe_options* o) {
+  const int H = L->hidden, I = L->moe_inter, Is = L->shared_inter;
+  return opt_tc05(o) && gemm_tc05_supported(H, 2 * I) && gemm_tc05_supported(I, H) &&
+         (Is == 0 || (gemm_tc05_supported(H, 2 * Is) && gemm_tc05_supported(Is, H)));
+}
 // routed experts on the swap-AB kernel: when asked for (gemm_kernel 2), and
 // for the stock (bf16-activation) semantics whenever the layer carries its
 // row normalisers (the power-of-two normalisers keep x and the scales exact
@@ -811,13 +836,18 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
     b.tile_row = c.take<int32_t>(maxt);
     b.tile_exp = c.take<int32_t>(maxt);
     b.ntiles = c.take<int32_t>(1);
-    const bool tc = opt_tc05(opt);
+    const bool tc = tc05_layer(L, opt);
     const bool fr = fast_routed(L, opt), fs = fast_shared(L);
+    const int gs = tc ? tc05_srow(G) : G, gi = tc ? tc05_srow(I / 64) : I / 64;
     if (fr) {
       carve_fast(c, T, R, H, I, &b.fr);
     } else {
-      if (i8) {  // int8 codes: one byte each for mma.sync, fp16 for tcgen05
-        b.xq = c.take<int8_t>((size_t)T * H * (tc ? 2 : 1));
+      if (tc) {  // tcgen05: expert-sorted fp16 rows (int8 codes or x) + row scalars
+        b.xq = c.take<int8_t>((size_t)R * H * 2);
+        b.xsc = c.take<float>((size_t)R * gs);
+        b.xrs = c.take<float>((size_t)R * gs);
+      } else if (i8) {  // mma.sync: int8 codes per token
+        b.xq = c.take<int8_t>((size_t)T * H);
         b.xsc = c.take<float>((size_t)T * G);
         b.xrs = c.take<float>((size_t)T * G);
       }
@@ -826,15 +856,15 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
           b.h16p = c.take<uint16_t>((size_t)R * I);
         else
           b.hq = c.take<int8_t>((size_t)R * I);
-        b.hsc = c.take<float>((size_t)R * (I / 64));
+        b.hsc = c.take<float>((size_t)R * gi);
       } else {
         b.h16p = c.take<uint16_t>((size_t)R * I);
       }
-      b.hrs = c.take<float>((size_t)R * (I / 64));
+      b.hrs = c.take<float>((size_t)R * gi);
     }
-    if ((!fr && !i8) || (Is > 0 && !fs)) {
+    if ((!fr && !i8 && !tc) || (Is > 0 && !fs)) {
       b.sx16p = c.take<uint16_t>((size_t)T * H);
-      b.sxsum = c.take<float>((size_t)T * G);
+      b.sxsum = c.take<float>((size_t)T * gs);
     }
     b.ys = c.take<uint16_t>((size_t)R * H);
     if (Is > 0) {
@@ -847,7 +877,7 @@ size_t carve_block(Carve& c, const tmoe_layer* L, int T, const tmoe_options* opt
         carve_fast(c, T, T, H, Is, &b.fs);
       } else {
         b.sh16p = c.take<uint16_t>((size_t)T * Is);
-        b.shrs = c.take<float>((size_t)T * (Is / 64));
+        b.shrs = c.take<float>((size_t)T * (tc ? tc05_srow(Is / 64) : Is / 64));
       }
       b.ys_sh = c.take<uint16_t>((size_t)T * H);
     }
@@ -1049,14 +1079,17 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   TMOE_TRY(launch_route_plan(idx, R, E, rtile, rmaxt, p, b.route_scratch, s), "route_plan");
   const bool i8 = opt_int8(opt);
   const bool d8 = i8 && opt_down_int8(opt);
-  const bool tc = opt_tc05(opt);
+  const bool tc = tc05_layer(L, opt);
+  const int gs = tc ? tc05_srow(G) : G, gi = tc ? tc05_srow(I / 64) : I / 64;
   auto gemm = [&](bool int8, int epi, const GemmParams& P, int ntiles_max) {
     return tc ? launch_gemm_tc05(int8, epi, P, ntiles_max, s)
               : launch_gemm_grouped(int8, epi, P, ntiles_max, s);
   };
-  if ((!fr && !i8) || (Is > 0 && !fs)) {      // fp16 copy of x for the per-group kernels
+  if ((!fr && !i8 && !tc) || (Is > 0 && !fs)) {   // fp16 copy of x (token order)
     if (tc)
-      TMOE_TRY(launch_prep_a16(x, T, H, false, b.sx16p, nullptr, b.sxsum, s), "prep_x");
+      TMOE_TRY(launch_prep_a16_rows(x, T, H, false, nullptr, nullptr, 1, gs, b.sx16p, nullptr,
+                                    b.sxsum, s),
+               "prep_x");
     else
       TMOE_TRY(launch_prep_x(x, T, H, b.sx16p, b.sxsum, G, 1, s), "prep_x");
   }
@@ -1066,22 +1099,31 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
                           kRoutedNames))
       return rc;
   } else {
-    if (i8) {
-      if (tc)
-        TMOE_TRY(launch_prep_a16(x, T, H, true, reinterpret_cast<uint16_t*>(b.xq), b.xsc, b.xrs, s),
-                 "quantize_rows");
-      else
-        TMOE_TRY(launch_quantize_rows(x, T, H, b.xq, b.xsc, b.xrs, s), "quantize_rows");
-    }
     GemmParams g{};
-    g.A = i8 ? static_cast<const void*>(b.xq) : static_cast<const void*>(b.sx16p);
-    g.asc = b.xsc;
-    g.ars = i8 ? b.xrs : b.sxsum;
-    g.s_r = G;
+    if (tc) {
+      // the expert-sorted operand rows: int8 codes (or x) of token order[r] / k
+      TMOE_TRY(launch_prep_a16_rows(x, R, H, i8, b.order, nullptr, k, gs,
+                                    reinterpret_cast<uint16_t*>(b.xq), i8 ? b.xsc : nullptr, b.xrs,
+                                    s),
+               i8 ? "quantize_rows" : "prep_x");
+      g.A = b.xq;
+      g.asc = i8 ? b.xsc : nullptr;
+      g.ars = b.xrs;
+      g.s_r = gs;
+      g.a_nrows = R;
+      g.h_srow = gi;
+    } else {
+      if (i8) TMOE_TRY(launch_quantize_rows(x, T, H, b.xq, b.xsc, b.xrs, s), "quantize_rows");
+      g.A = i8 ? static_cast<const void*>(b.xq) : static_cast<const void*>(b.sx16p);
+      g.asc = b.xsc;
+      g.ars = i8 ? b.xrs : b.sxsum;
+      g.s_r = G;
+      g.a_rows = b.order;
+      g.a_div = k;
+    }
     g.s_g = 1;
-    g.a_rows = b.order;
-    g.a_div = k;
     g.W = L->gate_up_w;
+    g.E = E;
     g.st = L->gate_up_st;
     g.bt = L->gate_up_bt;
     g.tile_row = b.tile_row;
@@ -1100,9 +1142,11 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     dn.A = (d8 && !tc) ? static_cast<const void*>(b.hq) : static_cast<const void*>(b.h16p);
     dn.asc = b.hsc;
     dn.ars = b.hrs;
-    dn.s_r = 1;
-    dn.s_g = R;
+    dn.s_r = tc ? gi : 1;      // tcgen05: row-major h scalars; mma.sync: [group][row]
+    dn.s_g = tc ? 1 : R;
+    dn.a_nrows = R;
     dn.W = L->down_w;
+    dn.E = E;
     dn.st = L->down_st;
     dn.bt = L->down_bt;
     dn.tile_row = b.tile_row;
@@ -1126,11 +1170,14 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
         return rc;
     } else {
       GemmParams sg{};
+      const int gsh = tc ? tc05_srow(Is / 64) : Is / 64;
       sg.A = b.sx16p;
       sg.ars = b.sxsum;
-      sg.s_r = G;
+      sg.s_r = gs;
       sg.s_g = 1;
+      sg.a_nrows = T;
       sg.W = L->shared_gate_up_w;
+      sg.E = 1;
       sg.st = L->shared_gate_up_st;
       sg.bt = L->shared_gate_up_bt;
       sg.tile_row = b.s_tile_row;
@@ -1141,14 +1188,17 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
       sg.N = 2 * Is;
       sg.hrs = b.shrs;
       sg.Rpad_h = T;
+      sg.h_srow = gsh;
       sg.h16p = b.sh16p;
       TMOE_TRY(gemm(false, kEpiSwigluH16, sg, st), "gemm_shared_gate_up");
       GemmParams sd{};
       sd.A = b.sh16p;
       sd.ars = b.shrs;
-      sd.s_r = 1;
-      sd.s_g = T;
+      sd.s_r = tc ? gsh : 1;
+      sd.s_g = tc ? 1 : T;
+      sd.a_nrows = T;
       sd.W = L->shared_down_w;
+      sd.E = 1;
       sd.st = L->shared_down_st;
       sd.bt = L->shared_down_bt;
       sd.tile_row = b.s_tile_row;
@@ -1246,7 +1296,8 @@ size_t carve_experts(Carve& c, const tmoe_layer* L, int R, int P, const tmoe_opt
                      ExpertsWs* out) {
   const int H = L->hidden, E = L->num_experts, I = L->moe_inter, G = H / 64;
   const int maxt = max_tiles(P, E);
-  const bool i8 = opt_int8(opt), d8 = i8 && opt_down_int8(opt), tc = opt_tc05(opt);
+  const bool i8 = opt_int8(opt), d8 = i8 && opt_down_int8(opt), tc = tc05_layer(L, opt);
+  const int gs = tc ? tc05_srow(G) : G, gi = tc ? tc05_srow(I / 64) : I / 64;
   ExpertsWs b{};
   b.order = c.take<int32_t>(P);
   b.inv = c.take<int32_t>(P);
@@ -1260,8 +1311,12 @@ size_t carve_experts(Carve& c, const tmoe_layer* L, int R, int P, const tmoe_opt
     if (out) *out = b;
     return c.off;
   }
-  if (i8) {
-    b.xq = c.take<int8_t>((size_t)R * H * (tc ? 2 : 1));
+  if (tc) {  // expert-sorted fp16 rows, one per pair (int8 codes or x) + row scalars
+    b.xq = c.take<int8_t>((size_t)P * H * 2);
+    b.xsc = c.take<float>((size_t)P * gs);
+    b.xrs = c.take<float>((size_t)P * gs);
+  } else if (i8) {
+    b.xq = c.take<int8_t>((size_t)R * H);
     b.xsc = c.take<float>((size_t)R * G);
     b.xrs = c.take<float>((size_t)R * G);
   } else {
@@ -1272,8 +1327,8 @@ size_t carve_experts(Carve& c, const tmoe_layer* L, int R, int P, const tmoe_opt
     b.hq = c.take<int8_t>((size_t)P * I);
   else
     b.h16p = c.take<uint16_t>((size_t)P * I);
-  if (d8) b.hsc = c.take<float>((size_t)P * (I / 64));
-  b.hrs = c.take<float>((size_t)P * (I / 64));
+  if (d8) b.hsc = c.take<float>((size_t)P * gi);
+  b.hrs = c.take<float>((size_t)P * gi);
   if (out) *out = b;
   return c.off;
 }
@@ -1329,7 +1384,8 @@ int moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pa
   TMOE_TRY(launch_route_plan(pair_exp, P, E, fastr ? kSwTileN : kTileM, maxt, p, b.route_scratch,
                              s),
            "route_plan");
-  const bool i8 = opt_int8(opt), d8 = i8 && opt_down_int8(opt), tc = opt_tc05(opt);
+  const bool i8 = opt_int8(opt), d8 = i8 && opt_down_int8(opt), tc = tc05_layer(L, opt);
+  const int gs = tc ? tc05_srow(G) : G, gi = tc ? tc05_srow(I / 64) : I / 64;
   if (fastr) {
     const FastRoute rt{b.tile_row, b.tile_exp, b.ntiles, b.offsets, maxt, b.order,
                        slot_k > 0 ? slot_k : 1, slot_k > 0 ? nullptr : pair_row};
@@ -1339,28 +1395,35 @@ int moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pa
   auto gemm = [&](bool int8, int epi, const GemmParams& Pm) {
     return tc ? launch_gemm_tc05(int8, epi, Pm, maxt, s) : launch_gemm_grouped(int8, epi, Pm, maxt, s);
   };
+  GemmParams g{};
   if (tc) {
-    if (i8)
-      TMOE_TRY(launch_prep_a16(x, R, H, true, reinterpret_cast<uint16_t*>(b.xq), b.xsc, b.xrs, s),
-               "quantize_rows");
-    else
-      TMOE_TRY(launch_prep_a16(x, R, H, false, b.x16p, nullptr, b.xsum, s), "prep_x");
+    // one expert-sorted operand row per pair: sorted position -> pair -> row
+    TMOE_TRY(launch_prep_a16_rows(x, P, H, i8, b.order, slot_k > 0 ? nullptr : pair_row,
+                                  slot_k > 0 ? slot_k : 1, gs, reinterpret_cast<uint16_t*>(b.xq),
+                                  i8 ? b.xsc : nullptr, b.xrs, s),
+             i8 ? "quantize_rows" : "prep_x");
+    g.A = b.xq;
+    g.asc = i8 ? b.xsc : nullptr;
+    g.ars = b.xrs;
+    g.s_r = gs;
+    g.a_nrows = P;
+    g.h_srow = gi;
   } else {
     if (i8)
       TMOE_TRY(launch_quantize_rows(x, R, H, b.xq, b.xsc, b.xrs, s), "quantize_rows");
     else
       TMOE_TRY(launch_prep_x(x, R, H, b.x16p, b.xsum, G, 1, s), "prep_x");
+    g.A = i8 ? static_cast<const void*>(b.xq) : static_cast<const void*>(b.x16p);
+    g.asc = b.xsc;
+    g.ars = i8 ? b.xrs : b.xsum;
+    g.s_r = G;
+    g.a_rows = b.order;          // sorted position -> pair
+    g.a_map = slot_k > 0 ? nullptr : pair_row;   // pair -> received row
+    g.a_div = slot_k > 0 ? slot_k : 1;
   }
-  GemmParams g{};
-  g.A = i8 ? static_cast<const void*>(b.xq) : static_cast<const void*>(b.x16p);
-  g.asc = b.xsc;
-  g.ars = i8 ? b.xrs : b.xsum;
-  g.s_r = G;
   g.s_g = 1;
-  g.a_rows = b.order;          // sorted position -> pair
-  g.a_map = slot_k > 0 ? nullptr : pair_row;   // pair -> received row
-  g.a_div = slot_k > 0 ? slot_k : 1;
   g.W = L->gate_up_w;
+  g.E = E;
   g.st = L->gate_up_st;
   g.bt = L->gate_up_bt;
   g.tile_row = b.tile_row;
@@ -1379,9 +1442,11 @@ int moe_experts(const tmoe_layer* L, const uint16_t* x, int R, const int32_t* pa
   dn.A = (d8 && !tc) ? static_cast<const void*>(b.hq) : static_cast<const void*>(b.h16p);
   dn.asc = b.hsc;
   dn.ars = b.hrs;
-  dn.s_r = 1;
-  dn.s_g = P;
+  dn.s_r = tc ? gi : 1;      // tcgen05: row-major h scalars; mma.sync: [group][row]
+  dn.s_g = tc ? 1 : P;
+  dn.a_nrows = P;
   dn.W = L->down_w;
+  dn.E = E;
   dn.st = L->down_st;
   dn.bt = L->down_bt;
   dn.tile_row = b.tile_row;
@@ -1483,13 +1548,17 @@ int tmoe_moe_local(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_opt
     return run_fast(shared_proj(L), x, T, T, false, false, rs, b.fs, shared_out, nullptr, nullptr,
                     s, kSharedNames);
   }
-  if (opt_tc05(&o))
-    TMOE_TRY(launch_prep_a16(x, T, H, false, b.sx16p, nullptr, b.sxsum, s), "prep_x");
+  const bool tc = tc05_layer(L, &o);
+  const int gs = tc ? tc05_srow(G) : G, gsh = tc ? tc05_srow(Is / 64) : Is / 64;
+  if (tc)
+    TMOE_TRY(launch_prep_a16_rows(x, T, H, false, nullptr, nullptr, 1, gs, b.sx16p, nullptr,
+                                  b.sxsum, s),
+             "prep_x");
   else
     TMOE_TRY(launch_prep_x(x, T, H, b.sx16p, b.sxsum, G, 1, s), "prep_x");
   auto gemm = [&](int epi, const GemmParams& P, int ntiles_max) {
-    return opt_tc05(&o) ? launch_gemm_tc05(false, epi, P, ntiles_max, s)
-                        : launch_gemm_grouped(false, epi, P, ntiles_max, s);
+    return tc ? launch_gemm_tc05(false, epi, P, ntiles_max, s)
+              : launch_gemm_grouped(false, epi, P, ntiles_max, s);
   };
   const int st = (T + kTileM - 1) / kTileM;
   TMOE_TRY(launch_dense_tiles(T, kTileM, b.s_tile_row, b.s_tile_exp, b.s_ntiles, b.s_offsets, s),
@@ -1497,9 +1566,11 @@ int tmoe_moe_local(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_opt
   GemmParams sg{};
   sg.A = b.sx16p;
   sg.ars = b.sxsum;
-  sg.s_r = G;
+  sg.s_r = gs;
   sg.s_g = 1;
+  sg.a_nrows = T;
   sg.W = L->shared_gate_up_w;
+  sg.E = 1;
   sg.st = L->shared_gate_up_st;
   sg.bt = L->shared_gate_up_bt;
   sg.tile_row = b.s_tile_row;
@@ -1510,14 +1581,17 @@ int tmoe_moe_local(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_opt
   sg.N = 2 * Is;
   sg.hrs = b.shrs;
   sg.Rpad_h = T;
+  sg.h_srow = gsh;
   sg.h16p = b.sh16p;
   TMOE_TRY(gemm(kEpiSwigluH16, sg, st), "gemm_shared_gate_up");
   GemmParams sd{};
   sd.A = b.sh16p;
   sd.ars = b.shrs;
-  sd.s_r = 1;
-  sd.s_g = T;
+  sd.s_r = tc ? gsh : 1;
+  sd.s_g = tc ? 1 : T;
+  sd.a_nrows = T;
   sd.W = L->shared_down_w;
+  sd.E = 1;
   sd.st = L->shared_down_st;
   sd.bt = L->shared_down_bt;
   sd.tile_row = b.s_tile_row;

@@ -4,14 +4,17 @@
 // One CTA computes a 128-row x 128-column tile of one expert over the K
 // dimension, one 64-wide quantisation group per pipeline stage.  Roles
 // (512 threads):
-//   warp 0      allocates TMEM, issues tcgen05.mma (one elected lane) and
+//   warp 0      loader, LAG groups ahead: TMA loads (no multicast) of the
+//               packed int4 weight rows and of the group's scale / bias
+//               segments; cp.async copies of the gathered A rows (through
+//               a_rows) into the 128B-swizzled K-major layout and of the row
+//               scalars;
+//   warp 1      allocates TMEM, issues tcgen05.mma (one elected lane) and
 //               commits stage / accumulator barriers;
-//   warps 1-7   producers: cp.async copies of the A rows (gathered through
-//               a_rows), the packed int4 B rows and the scalars, LAG groups
-//               ahead; then widen the current group's B rows into fp16, both
-//               operands in the 128B-swizzled K-major layout that the MMA
-//               descriptors address;
-//   warps 8-15  epilogue: two warps per TMEM lane quadrant, 64 columns each.
+//   warps 2-7   converters: widen the group's packed rows into fp16 B (same
+//               swizzled layout) and write the fp32 column scalars;
+//   warps 8-15  epilogue: two warps per TMEM lane quadrant, 64 columns each;
+//               the per-group rescale issues as packed f32x2 FMAs.
 //
 // Two arithmetic modes, both on kind::f16 with fp32 accumulation:
 //   INT8  — the reference's int8 x int4 algebra: A holds the activation codes
@@ -45,36 +48,49 @@ __device__ int g_tc05_error = 0;
 namespace tc {
 
 constexpr int BM = 128, BN = 128;
-constexpr int NST = 5;                            // pipeline stages
-constexpr int LAG = 3;                            // groups in flight ahead of the widening
-constexpr int A_BYTES = BM * 128;                 // 64 fp16 per row per group
+constexpr int NA = 4;                             // activation tiles (one group each)
+constexpr int NB = 3;                             // widened weight tiles (one group each)
+constexpr int NQ = 2;                             // packed stages (4 groups each)
+constexpr int kMaxG = 48;                         // K <= 3072: scale / bias tables held whole
+constexpr int A_BYTES = BM * 128;                 // 128 rows x 64 fp16, 128B-swizzled
 constexpr int B_BYTES = BN * 128;
-constexpr int SC_BYTES = (2 * BM + 2 * BN) * 4;   // xsc, xrs, s, bv (fp32)
-constexpr int RAWB_BYTES = BN * 32;               // packed int4 rows of the group
-constexpr int RAWT_BYTES = 2 * BN * 2;            // bf16 scales and biases of the group
-constexpr int STAGE = 39936;                      // A + B + SC + RAWB + RAWT rounded to 1 KB
-static_assert(A_BYTES + B_BYTES + SC_BYTES + RAWB_BYTES + RAWT_BYTES <= STAGE &&
-                  STAGE % 1024 == 0, "stage layout");
-static_assert(LAG < NST, "the producer refills a stage the MMA finished two groups ago");
-constexpr int BAR_OFF = NST * STAGE;
-constexpr int AROW_OFF = BAR_OFF + 256;           // source row of each tile row
-constexpr int XCH_OFF = AROW_OFF + BM * 4;
-constexpr int SMEM = XCH_OFF + BM * 36 * 4 + 1024;
+constexpr int CS_BYTES = 2 * BN * 4;              // column s and b + 8s (fp32) of a group
+constexpr int QW_BYTES = 4 * 32 * 128;            // 4 segments x [32 rows][4 groups x 32 B], SW128
+constexpr int QS_BYTES = BM * 16;                 // one row scalar x [128 rows][4 groups]
+constexpr int Q_BYTES = QW_BYTES + 2 * QS_BYTES;  // + xsc, xrs
+constexpr int A_OFF = 0;
+constexpr int B_OFF = A_OFF + NA * A_BYTES;
+constexpr int Q_OFF = B_OFF + NB * B_BYTES;
+constexpr int CS_OFF = Q_OFF + NQ * Q_BYTES;
+constexpr int TB_OFF = CS_OFF + NB * CS_BYTES;    // 8 table boxes [G][32] bf16 (s x 4, b x 4)
+constexpr int TB_BYTES = 8 * 64 * kMaxG;
+constexpr int XCH_OFF = TB_OFF + TB_BYTES;
+constexpr int BAR_OFF = XCH_OFF + BM * 36 * 4;
+constexpr int SMEM = BAR_OFF + 512 + 1024;        // + alignment slack
+static_assert(A_OFF % 1024 == 0 && B_OFF % 1024 == 0 && Q_OFF % 1024 == 0 && Q_BYTES % 1024 == 0 &&
+                  CS_OFF % 128 == 0 && TB_OFF % 128 == 0 && BAR_OFF % 8 == 0,
+              "TMA / UMMA tiles 1024-byte aligned, other TMA destinations 128-byte aligned");
 static_assert(SMEM <= 232448, "shared memory per CTA");
 constexpr int NTHREADS = 512;
-constexpr int NPROD = 224;                       // warps 1-7
+constexpr int NCONV = 192;                        // converter warps 2-7
+// barrier indices (uint64 each) at BAR_OFF
+constexpr int B_AF = 0, B_AE = B_AF + NA, B_BF = B_AE + NA, B_BE = B_BF + NB, B_QF = B_BE + NB,
+              B_QE = B_QF + NQ, B_TF = B_QE + NQ, B_TE = B_TF + 2, B_TBL = B_TE + 2,
+              B_DRAIN = B_TBL + 1, B_SLOT = B_DRAIN + 1, B_ABORT = B_SLOT + 1,
+              B_PRESCALE = B_ABORT + 1;
+static_assert((B_PRESCALE + 1) * 8 <= 512, "barrier area");
 // Bounded wait recording into this kernel's error flag.
 TMOE_DEV bool mbar_wait(uint32_t a, uint32_t parity, volatile int* abort_flag) {
   return tc::mbar_wait(a, parity, abort_flag, &g_tc05_error);
 }
 
-// Named barrier over the producer warps that also ANDs a predicate.
-TMOE_DEV bool producers_and(bool v) {
+// Named barrier over the converter warps that also ANDs a predicate.
+TMOE_DEV bool converters_and(bool v) {
   uint32_t r;
   asm volatile(
       "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, 2, %2, p; selp.u32 %0, 1, 0, q; }"
       : "=r"(r)
-      : "r"((uint32_t)v), "n"(NPROD)
+      : "r"((uint32_t)v), "n"(NCONV)
       : "memory");
   return r != 0;
 }
@@ -91,8 +107,18 @@ TMOE_DEV void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t 
 
 using namespace tc;
 
+struct Tc05Maps {
+  CUtensorMap a;    // [rows][K] fp16 operand, box 64 x 128, 128B swizzle
+  CUtensorMap xs;   // [rows][srow] fp32 row scales, box 4 x 128
+  CUtensorMap xr;   // [rows][srow] fp32 row sums, box 4 x 128
+  CUtensorMap w;    // [E*N][K/8] packed int4 words, box 32 x 32, 128B swizzle
+  CUtensorMap s;    // [E*G][N] bf16 scales, box 32 x G
+  CUtensorMap b;    // [E*G][N] bf16 biases, box 32 x G
+};
+
 template <bool I8, int EPI>
-__global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gemm_tc05_kernel(const __grid_constant__ GemmParams P, const __grid_constant__ Tc05Maps M) {
   extern __shared__ uint8_t smem_raw[];
   const int tile = blockIdx.y;
   if (tile >= P.ntiles[0]) return;
@@ -103,30 +129,40 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
   constexpr bool SW = EPI != kEpiStore;
   const int Ih = P.N / 2;
   const int n0 = blockIdx.x * (SW ? 64 : BN);
+  const int TBS = (64 * G + 127) & ~127;      // bytes per table box, 128-byte aligned
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NST);
-  const uint32_t tfull0 = smem_u32(bars + 3 * NST), tempty0 = smem_u32(bars + 3 * NST + 2);
-  const uint32_t drain = smem_u32(bars + 3 * NST + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * NST + 5);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * NST + 6);
-  int* prescale_flag = reinterpret_cast<int*>(bars + 3 * NST + 7);
+  auto bar = [&](int i) -> uint32_t { return smem_u32(bars + i); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_SLOT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + B_ABORT);
+  int* prescale_flag = reinterpret_cast<int*>(bars + B_PRESCALE);
   float* xch = reinterpret_cast<float*>(smem + XCH_OFF);           // [128][36]
 
   if (tid == 0) {
-    for (int s = 0; s < NST; ++s) {
-      mbar_init(full0 + 8 * s, NPROD);
-      mbar_init(empty0 + 8 * s, 9);         // the MMA commit + the 8 epilogue warps
+    for (int i = 0; i < NA; ++i) {
+      mbar_init(bar(B_AF + i), 1);          // the loader's expect_tx + the tile's bytes
+      mbar_init(bar(B_AE + i), 1);          // MMA commit
+    }
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(bar(B_BF + i), NCONV / 32); // one arrival per converter warp
+      mbar_init(bar(B_BE + i), 9);          // MMA commit + the 8 epilogue warps
+    }
+    for (int i = 0; i < NQ; ++i) {
+      mbar_init(bar(B_QF + i), 1);
+      mbar_init(bar(B_QE + i), NCONV / 32 + 8);   // converters (packed rows), epilogue (row scalars)
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(tfull0 + 8 * b, 1);
-      mbar_init(tempty0 + 8 * b, 8);
+      mbar_init(bar(B_TF + b), 1);
+      mbar_init(bar(B_TE + b), 8);
     }
-    mbar_init(drain, 1);
+    mbar_init(bar(B_TBL), 1);
+    mbar_init(bar(B_DRAIN), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&M.a);
+    tma_prefetch_desc(&M.w);
   }
-  if (warp == 0) {
+  if (warp == 1) {
     const uint32_t ncols = I8 ? 2 * BN : BN;
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)), "r"(ncols));
@@ -137,197 +173,204 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // weight row of B-tile row c: the SwiGLU tiles interleave 32-row segments
+  // (gate lo, up lo, gate hi, up hi) so that each epilogue half holds matching
+  // gate and up columns
   auto wrow = [&](int c) -> int {
     if (!SW) return n0 + c;
-    const int q = c >> 5;                 // 0: gate lo, 1: up lo, 2: gate hi, 3: up hi
+    const int q = c >> 5;
     const int j = c & 31;
     return ((q & 1) ? Ih : 0) + n0 + ((q >> 1) << 5) + j;
   };
+  const int nq = (G + 3) >> 2;                // packed stages of this tile
 
   if (warp == 0) {
+    // ---------------------------------------------------------------- loader
+    // One thread issues every copy, all TMA (no multicast): the tables once,
+    // then per group the 16 KB activation tile and per 4 groups the packed
+    // weight rows (4 x 4 KB) and the row scalars (2 x 2 KB).  Coordinates:
+    // x of every box is a multiple of 16 bytes; rows past the operand's end
+    // read zeros.
+    if (lane == 0) {
+      const uint32_t tbl = bar(B_TBL);
+      mbar_expect_tx(tbl, 8u * 64u * (uint32_t)G);
+      for (int seg = 0; seg < 4; ++seg) {
+        const int wr = wrow(seg * 32);
+        tma_load_2d(smem_u32(smem + TB_OFF + seg * TBS), &M.s, wr, e * G, tbl);
+        tma_load_2d(smem_u32(smem + TB_OFF + (4 + seg) * TBS), &M.b, wr, e * G, tbl);
+      }
+      const uint32_t qtx = (uint32_t)QW_BYTES + (I8 ? 2u : 1u) * (uint32_t)QS_BYTES;
+      int issued_a = 0, issued_q = 0;
+      bool ok = true;
+      for (int g = 0; g < G && ok; ++g) {
+        if ((g & 3) == 0) {
+          const int q = g >> 2, sq = q % NQ;
+          if (!(ok = mbar_wait(bar(B_QE + sq), ((q / NQ) & 1) ^ 1, abort_flag))) break;
+          const uint32_t qb = bar(B_QF + sq);
+          uint8_t* qs = smem + Q_OFF + sq * Q_BYTES;
+          mbar_expect_tx(qb, qtx);
+          for (int seg = 0; seg < 4; ++seg)
+            tma_load_2d(smem_u32(qs + seg * 4096), &M.w, q * 32, e * P.N + wrow(seg * 32), qb);
+          if (I8) tma_load_2d(smem_u32(qs + QW_BYTES), &M.xs, q * 4, row0, qb);
+          tma_load_2d(smem_u32(qs + QW_BYTES + QS_BYTES), &M.xr, q * 4, row0, qb);
+          issued_q = q + 1;
+        }
+        const int sa = g % NA;
+        if (!(ok = mbar_wait(bar(B_AE + sa), ((g / NA) & 1) ^ 1, abort_flag))) break;
+        mbar_expect_tx(bar(B_AF + sa), A_BYTES);
+        tma_load_2d(smem_u32(smem + A_OFF + sa * A_BYTES), &M.a, g * 64, row0, bar(B_AF + sa));
+        issued_a = g + 1;
+      }
+      // copies still in flight (after an abort) land before the CTA exits
+      auto drain_wait = [&](uint32_t b, uint32_t par) {
+        for (uint32_t i = 0; i < kSpinLimit && !mbar_try(b, par); ++i) __nanosleep(128);
+      };
+      drain_wait(tbl, 0);
+      for (int g = issued_a > NA ? issued_a - NA : 0; g < issued_a; ++g)
+        drain_wait(bar(B_AF + g % NA), (g / NA) & 1);
+      for (int q = issued_q > NQ ? issued_q - NQ : 0; q < issued_q; ++q)
+        drain_wait(bar(B_QF + q % NQ), (q / NQ) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       for (int g = 0; g < G; ++g) {
-        const int s = g % NST;
-        const uint32_t ph = (g / NST) & 1;
-        if (!mbar_wait(full0 + 8 * s, ph, abort_flag)) break;
+        const int sa = g % NA, sb = g % NB;
+        if (!mbar_wait(bar(B_AF + sa), (g / NA) & 1, abort_flag)) break;
+        if (!mbar_wait(bar(B_BF + sb), (g / NB) & 1, abort_flag)) break;
         const int b = I8 ? (g & 1) : 0;
-        if (I8 && !mbar_wait(tempty0 + 8 * b, ((g >> 1) & 1) ^ 1, abort_flag)) break;
+        if (I8 && !mbar_wait(bar(B_TE + b), ((g >> 1) & 1) ^ 1, abort_flag)) break;
         tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + s * STAGE);
-        const uint32_t b_base = a_base + A_BYTES;
+        const uint32_t a_base = smem_u32(smem + A_OFF + sa * A_BYTES);
+        const uint32_t b_base = smem_u32(smem + B_OFF + sb * B_BYTES);
         const uint32_t d = tmem + (uint32_t)(b * BN);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_f16(d, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32),
                   (kk > 0 || (!I8 && g > 0)) ? 1u : 0u);
-        mma_commit(empty0 + 8 * s);
-        if (I8) mma_commit(tfull0 + 8 * b);
+        mma_commit(bar(B_AE + sa));
+        mma_commit(bar(B_BE + sb));
+        if (I8) mma_commit(bar(B_TF + b));
       }
-      if (!I8) mma_commit(tfull0);
+      if (!I8) mma_commit(bar(B_TF));
     }
     __syncwarp();
   } else if (warp < 8) {
-    // --------------------------------------------------------------- producers
-    // Copies for group g + LAG are issued (cp.async: A rows, packed B rows,
-    // row scalars, column tables) before group g is widened, so LAG groups of
-    // loads are in flight behind the one being converted.
-    const int pt = tid - 32;
-    const size_t KW = (size_t)(P.K / 8);
-    const uint32_t* We = P.W + (size_t)e * P.N * KW;
-    const uint16_t* ste = P.st + (size_t)e * G * P.N;
-    const uint16_t* bte = P.bt + (size_t)e * G * P.N;
-    const uint16_t* A = static_cast<const uint16_t*>(P.A);
-    int* arow_s = reinterpret_cast<int*>(smem + AROW_OFF);
-    for (int r = pt; r < BM; r += NPROD) {
-      int rr = row0 + r;
-      if (rr >= rowend) rr = row0;           // rows past the expert's end: any valid row
-      arow_s[r] = !P.a_rows ? rr : (P.a_map ? P.a_map[P.a_rows[rr]] : P.a_rows[rr] / P.a_div);
-    }
-    // INT8: B can carry the scale, (q - 8) * s exact in fp16, when every scale
-    // of the tile is 0 or inside [2^-14, 2^12): then the MMA returns D * s
-    // exactly (|D| <= 2^16, so D * s needs at most 24 bits).  One flag per CTA.
-    bool safe = true;
-    {
-      for (int i = pt; i < G * 16; i += NPROD) {
-        const int g = i >> 4, cc = i & 15;
-        const uint4 v = *reinterpret_cast<const uint4*>(ste + (size_t)g * P.N + wrow(cc * 8));
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    // ------------------------------------------------------------- converters
+    // Widen group g's packed rows into the fp16 B operand (128B-swizzled
+    // K-major) and write the group's fp32 column scalars.  Work item
+    // i = (tile row i / 8, word i % 8): a warp covers 4 rows x 8 words per
+    // step; both the swizzled packed stage and the B tile are read / written
+    // without bank conflicts.  The six items of a thread are loaded before any
+    // is widened.
+    const int ct = tid - 64;
+    if (!mbar_wait(bar(B_TBL), 0, abort_flag)) {
+      converters_and(false);
+    } else {
+      const uint8_t* tb = smem + TB_OFF;
+      auto tab = [&](int which, int g, int c) -> uint16_t {   // which: 0 = s, 1 = b
+        return *reinterpret_cast<const uint16_t*>(tb + (which * 4 + (c >> 5)) * TBS + g * 64 +
+                                                  (c & 31) * 2);
+      };
+      // INT8: B can carry the scale, (q - 8) * s exact in fp16, when every
+      // scale of the tile is 0 or inside [2^-14, 2^12): then the MMA returns
+      // D * s exactly (|D| <= 2^16, so D * s needs at most 24 bits).
+      bool safe = true;
+      for (int i = ct; i < G * BN; i += NCONV) {
+        const uint32_t bv = tab(0, i >> 7, i & 127);
+        const uint32_t ex = (bv >> 7) & 0xffu;
+        safe = safe && (((bv & 0x7fffu) == 0u) || (ex >= 113u && ex <= 138u));
+      }
+      const bool prescale = converters_and(safe);
+      if (ct == 0) *prescale_flag = prescale ? 1 : 0;
+      // STOCK accumulates every group in TMEM, so B must carry the scale: a
+      // tile whose scales fall outside fp16's exact range is reported (error
+      // 2, tmoe_device_status) — the swap-AB kernel with row normalisers has
+      // no such limit.
+      if (!I8 && !prescale && ct == 0) atomicExch(&g_tc05_error, 2);
+      const bool scale_b = !I8 || prescale;
+      constexpr int NIT = (BN * 8 + NCONV - 1) / NCONV;
+      for (int g = 0; g < G; ++g) {
+        const int q = g >> 2, sq = q % NQ, sb = g % NB;
+        if (!mbar_wait(bar(B_QF + sq), (q / NQ) & 1, abort_flag)) break;
+        if (!mbar_wait(bar(B_BE + sb), ((g / NB) & 1) ^ 1, abort_flag)) break;
+        const uint8_t* qs = smem + Q_OFF + sq * Q_BYTES;
+        uint8_t* sB = smem + B_OFF + sb * B_BYTES;
+        const int gg = g & 3;
+        uint32_t wv[NIT];
+        __half sh[NIT];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t b = (w[j >> 1] >> (16 * (j & 1))) & 0xffffu;
-          const uint32_t ex = (b >> 7) & 0xffu;
-          safe = safe && (((b & 0x7fffu) == 0u) || (ex >= 113u && ex <= 138u));
+        for (int k = 0; k < NIT; ++k) {
+          const int i = ct + k * NCONV;
+          if (i < BN * 8) {
+            const int r = i >> 3, c = i & 7;
+            wv[k] = *reinterpret_cast<const uint32_t*>(
+                qs + (r >> 5) * 4096 + (r & 31) * 128 + (((2 * gg + (c >> 2)) ^ (r & 7)) << 4) +
+                (c & 3) * 4);
+            sh[k] = __float2half_rn(bf2f(tab(0, g, r)));
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < NIT; ++k) {
+          const int i = ct + k * NCONV;
+          if (i < BN * 8) {
+            const int r = i >> 3, c = i & 7;
+            *reinterpret_cast<uint4*>(sB + r * 128 + ((c ^ (r & 7)) << 4)) =
+                widen8(wv[k], scale_b, __halves2half2(sh[k], sh[k]));
+          }
+        }
+        // column scalars: s and the folded bias b + 8s
+        if (ct < BN) {
+          const float sv = bf2f(tab(0, g, ct));
+          const float bb = __fadd_rn(bf2f(tab(1, g, ct)), __fmul_rn(8.0f, sv));
+          float* cs = reinterpret_cast<float*>(smem + CS_OFF + sb * CS_BYTES);
+          cs[ct] = sv;
+          cs[BN + ct] = I8 ? bfround(bb) : bb;
+        }
+        // each writer makes its stores visible to the async proxy; one
+        // arrival per warp
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar(B_BF + sb));
+          if (gg == 3 || g == G - 1) mbar_arrive(bar(B_QE + sq));
         }
       }
     }
-    const bool prescale = producers_and(safe);
-    if (pt == 0) *prescale_flag = prescale ? 1 : 0;
-    // STOCK accumulates every group in TMEM, so B must carry the scale: a
-    // tile whose scales fall outside fp16's exact range is reported (error 2,
-    // tmoe_device_status) — the swap-AB kernel with row normalisers has
-    // no such limit.
-    if (!I8 && !prescale && pt == 0) atomicExch(&g_tc05_error, 2);
-    const bool scale_b = !I8 || prescale;
-
-    // Per-thread copy plan, fixed across groups (addresses advance per group).
-    constexpr int NA = (BM * 8 + NPROD - 1) / NPROD;
-    constexpr int NB = (BN * 2 + NPROD - 1) / NPROD;
-    constexpr int NS = (2 * BM + NPROD - 1) / NPROD;
-    const uint16_t* a_src[NA];
-    uint32_t a_dst[NA];
-#pragma unroll
-    for (int j = 0; j < NA; ++j) {
-      const int i = min(pt + j * NPROD, BM * 8 - 1);
-      const int r = i >> 3, c = i & 7;
-      a_src[j] = A + (size_t)arow_s[r] * P.K + c * 8;
-      a_dst[j] = r * 128 + ((c ^ (r & 7)) << 4);
-    }
-    const uint32_t* b_src[NB];
-#pragma unroll
-    for (int j = 0; j < NB; ++j) {
-      const int i = min(pt + j * NPROD, BN * 2 - 1);
-      b_src[j] = We + (size_t)wrow(i >> 1) * KW + (i & 1) * 4;
-    }
-    const float* s_src[NS];
-#pragma unroll
-    for (int j = 0; j < NS; ++j) {
-      const int i = min(pt + j * NPROD, 2 * BM - 1);
-      const float* arr = (i < BM) ? P.asc : P.ars;
-      s_src[j] = (arr ? arr : P.ars) + (size_t)arow_s[i & (BM - 1)] * P.s_r;
-    }
-    const uint16_t* t_src = (pt < 32) ? ((pt >> 4) ? bte : ste) + wrow((pt & 15) * 8) : ste;
-
-    auto issue = [&](int g) {
-      uint8_t* sA = smem + (g % NST) * STAGE;
-      float* sc = reinterpret_cast<float*>(sA + A_BYTES + B_BYTES);
-      uint8_t* raw = reinterpret_cast<uint8_t*>(sc) + SC_BYTES;
-      uint8_t* rawt = raw + RAWB_BYTES;
-#pragma unroll
-      for (int j = 0; j < NA; ++j)
-        if (pt + j * NPROD < BM * 8) cp_async16(sA + a_dst[j], a_src[j] + g * 64);
-#pragma unroll
-      for (int j = 0; j < NB; ++j)
-        if (pt + j * NPROD < BN * 2) cp_async16_l2pf(raw + (pt + j * NPROD) * 16, b_src[j] + g * 8);
-#pragma unroll
-      for (int j = 0; j < NS; ++j) {
-        const int i = pt + j * NPROD;
-        if (i < 2 * BM && (I8 || i >= BM)) cp_async4(sc + i, s_src[j] + (size_t)g * P.s_g);
-      }
-      if (pt < 32) cp_async16(rawt + pt * 16, t_src + (size_t)g * P.N);
-    };
-    auto stage_free = [&](int g) -> bool {
-      const int s = g % NST;
-      const uint32_t ph = ((g / NST) & 1) ^ 1;
-      return mbar_wait(empty0 + 8 * s, ph, abort_flag);
-    };
-
-    for (int g = 0; g < LAG; ++g) {   // the first NST stages start free; one
-      if (g < G) issue(g);             // commit group per group index keeps the
-      cp_async_commit();               // wait_group<LAG> count exact when G < LAG
-    }
-    for (int g = 0; g < G; ++g) {
-      const int gi = g + LAG;
-      bool ok = true;
-      if (gi < G) {
-        ok = stage_free(gi);
-        if (ok) issue(gi);
-      }
-      cp_async_commit();
-      cp_async_wait<LAG>();                    // this thread's copies of group g landed
-      if (!producers_and(ok && !*abort_flag)) break;   // ... and every producer's
-      const int s = g % NST;
-      uint8_t* sB = smem + s * STAGE + A_BYTES;
-      float* sc = reinterpret_cast<float*>(sB + B_BYTES);
-      const uint8_t* raw = reinterpret_cast<const uint8_t*>(sc) + SC_BYTES;
-      const uint16_t* rawt = reinterpret_cast<const uint16_t*>(raw + RAWB_BYTES);
-      // B: 128 rows x 2 half-rows (4 packed words each) -> 8 fp16 chunks
-      for (int i = pt; i < BN * 2; i += NPROD) {
-        const int r = i >> 1, hh = i & 1;
-        const uint4 w4 = *reinterpret_cast<const uint4*>(raw + r * 32 + hh * 16);
-        const __half sh = __float2half_rn(bf2f(rawt[r]));
-        const __half2 s2 = __halves2half2(sh, sh);
-        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = hh * 4 + j;
-          *reinterpret_cast<uint4*>(sB + r * 128 + ((c ^ (r & 7)) << 4)) = widen8(ws[j], scale_b, s2);
-        }
-      }
-      // column scalars: s and the folded bias b + 8s
-      for (int c = pt; c < BN; c += NPROD) {
-        const float sv = bf2f(rawt[c]);
-        const float bb = __fadd_rn(bf2f(rawt[BN + c]), __fmul_rn(8.0f, sv));
-        sc[2 * BM + c] = sv;
-        sc[2 * BM + BN + c] = I8 ? bfround(bb) : bb;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(full0 + 8 * s);
-    }
-    cp_async_wait<0>();
   } else {
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;                      // TMEM lane quadrant
     const int half = (warp - 8) >> 2;            // column half
     const int lr = q * 32 + lane;                // tile row of this thread
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    float acc[64];
+    // accumulators as column pairs: the per-group rescale issues as packed
+    // f32x2 FMAs (each component rounds exactly as a scalar fma.rn)
+    float2 acc2[32];
 #pragma unroll
-    for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
+    for (int c = 0; c < 32; ++c) acc2[c] = make_float2(0.0f, 0.0f);
+    auto acc = [&](int c) -> float { return (c & 1) ? acc2[c >> 1].y : acc2[c >> 1].x; };
     bool ok = true;
     bool prescaled = false;
     for (int g = 0; g < G && ok; ++g) {
-      const int s = g % NST;
-      const uint32_t ph = (g / NST) & 1;
-      if (!mbar_wait(full0 + 8 * s, ph, abort_flag)) { ok = false; break; }
+      const int qd = g >> 2, sq = qd % NQ, sb = g % NB, gg = g & 3;
+      // row scalars of the packed stage (TMA), column scalars of the group
+      // (converters)
+      if (!mbar_wait(bar(B_QF + sq), (qd / NQ) & 1, abort_flag) ||
+          !mbar_wait(bar(B_BF + sb), (g / NB) & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
       if (g == 0) prescaled = *reinterpret_cast<volatile int*>(prescale_flag) != 0;
-      const float* sc = reinterpret_cast<const float*>(smem + s * STAGE + A_BYTES + B_BYTES);
-      const float xs = sc[lr], xr = sc[BM + lr];
-      const float* cs = sc + 2 * BM + 64 * half;
-      const float* cb = sc + 2 * BM + BN + 64 * half;
+      const float* qsc = reinterpret_cast<const float*>(smem + Q_OFF + sq * Q_BYTES + QW_BYTES);
+      const float xs = I8 ? qsc[lr * 4 + gg] : 0.0f;
+      const float xr = qsc[BM * 4 + lr * 4 + gg];
+      const float* csb = reinterpret_cast<const float*>(smem + CS_OFF + sb * CS_BYTES);
+      const float* cs = csb + 64 * half;
+      const float* cb = csb + BN + 64 * half;
       if (I8) {
         const int b = g & 1;
-        if (!mbar_wait(tfull0 + 8 * b, (g >> 1) & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(bar(B_TF + b), (g >> 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t ta = tmem + lane_addr + (uint32_t)(b * BN + 64 * half);
 #pragma unroll
@@ -339,54 +382,56 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
           if (hh == 1) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty0 + 8 * b);
+            if (lane == 0) mbar_arrive(bar(B_TE + b));
           }
           // column scalars read 4 at a time (16-byte aligned in the stage)
           const float4* cb4 = reinterpret_cast<const float4*>(cb + 32 * hh);
           const float4* cs4 = reinterpret_cast<const float4*>(cs + 32 * hh);
+          const float2 xs2 = make_float2(xs, xs), xr2 = make_float2(xr, xr);
+          float2* a2 = acc2 + 16 * hh;
           if (prescaled) {                     // d = D * s already (exact)
 #pragma unroll
             for (int c4 = 0; c4 < 8; ++c4) {
               const float4 b4 = cb4[c4];
-              const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int c = 4 * c4 + q;
-                acc[32 * hh + c] = __fmaf_rn(d[c], xs, acc[32 * hh + c]);
-                acc[32 * hh + c] = __fmaf_rn(xr, bv[q], acc[32 * hh + c]);
-              }
+              a2[2 * c4] = __ffma2_rn(make_float2(d[4 * c4], d[4 * c4 + 1]), xs2, a2[2 * c4]);
+              a2[2 * c4] = __ffma2_rn(xr2, make_float2(b4.x, b4.y), a2[2 * c4]);
+              a2[2 * c4 + 1] =
+                  __ffma2_rn(make_float2(d[4 * c4 + 2], d[4 * c4 + 3]), xs2, a2[2 * c4 + 1]);
+              a2[2 * c4 + 1] = __ffma2_rn(xr2, make_float2(b4.z, b4.w), a2[2 * c4 + 1]);
             }
           } else {
 #pragma unroll
             for (int c4 = 0; c4 < 8; ++c4) {
               const float4 b4 = cb4[c4], s4 = cs4[c4];
-              const float bv[4] = {b4.x, b4.y, b4.z, b4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int c = 4 * c4 + q;
-                const float t1 = __fmul_rn(d[c], sv[q]);
-                acc[32 * hh + c] = __fmaf_rn(t1, xs, acc[32 * hh + c]);
-                acc[32 * hh + c] = __fmaf_rn(xr, bv[q], acc[32 * hh + c]);
-              }
+              const float2 t0 =
+                  __fmul2_rn(make_float2(d[4 * c4], d[4 * c4 + 1]), make_float2(s4.x, s4.y));
+              const float2 t1 =
+                  __fmul2_rn(make_float2(d[4 * c4 + 2], d[4 * c4 + 3]), make_float2(s4.z, s4.w));
+              a2[2 * c4] = __ffma2_rn(t0, xs2, a2[2 * c4]);
+              a2[2 * c4] = __ffma2_rn(xr2, make_float2(b4.x, b4.y), a2[2 * c4]);
+              a2[2 * c4 + 1] = __ffma2_rn(t1, xs2, a2[2 * c4 + 1]);
+              a2[2 * c4 + 1] = __ffma2_rn(xr2, make_float2(b4.z, b4.w), a2[2 * c4 + 1]);
             }
           }
         }
       } else {
         const float4* cb4 = reinterpret_cast<const float4*>(cb);
+        const float2 xr2 = make_float2(xr, xr);
 #pragma unroll
         for (int c4 = 0; c4 < 16; ++c4) {
           const float4 b4 = cb4[c4];
-          acc[4 * c4] = __fmaf_rn(xr, b4.x, acc[4 * c4]);
-          acc[4 * c4 + 1] = __fmaf_rn(xr, b4.y, acc[4 * c4 + 1]);
-          acc[4 * c4 + 2] = __fmaf_rn(xr, b4.z, acc[4 * c4 + 2]);
-          acc[4 * c4 + 3] = __fmaf_rn(xr, b4.w, acc[4 * c4 + 3]);
+          acc2[2 * c4] = __ffma2_rn(xr2, make_float2(b4.x, b4.y), acc2[2 * c4]);
+          acc2[2 * c4 + 1] = __ffma2_rn(xr2, make_float2(b4.z, b4.w), acc2[2 * c4 + 1]);
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8 * s);
+      if (lane == 0) {
+        mbar_arrive(bar(B_BE + sb));
+        if (gg == 3 || g == G - 1) mbar_arrive(bar(B_QE + sq));
+      }
     }
     if (!I8 && ok) {
-      if (mbar_wait(tfull0, 0, abort_flag)) {
+      if (mbar_wait(bar(B_TF), 0, abort_flag)) {
         tc_fence_after();
         const uint32_t ta = tmem + lane_addr + (uint32_t)(64 * half);
 #pragma unroll
@@ -396,7 +441,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
           tmem_ld16(ta + 32 * hh + 16, d + 16);
           tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 32; ++c) acc[32 * hh + c] = __fadd_rn(d[c], acc[32 * hh + c]);
+          for (int c = 0; c < 16; ++c)
+            acc2[16 * hh + c] = make_float2(__fadd_rn(d[2 * c], acc2[16 * hh + c].x),
+                                            __fadd_rn(d[2 * c + 1], acc2[16 * hh + c].y));
         }
         tc_fence_before();
       } else {
@@ -413,10 +460,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           uint4 pk;
-          pk.x = (uint32_t)f2bf(acc[8 * v + 0]) | ((uint32_t)f2bf(acc[8 * v + 1]) << 16);
-          pk.y = (uint32_t)f2bf(acc[8 * v + 2]) | ((uint32_t)f2bf(acc[8 * v + 3]) << 16);
-          pk.z = (uint32_t)f2bf(acc[8 * v + 4]) | ((uint32_t)f2bf(acc[8 * v + 5]) << 16);
-          pk.w = (uint32_t)f2bf(acc[8 * v + 6]) | ((uint32_t)f2bf(acc[8 * v + 7]) << 16);
+          pk.x = (uint32_t)f2bf(acc(8 * v + 0)) | ((uint32_t)f2bf(acc(8 * v + 1)) << 16);
+          pk.y = (uint32_t)f2bf(acc(8 * v + 2)) | ((uint32_t)f2bf(acc(8 * v + 3)) << 16);
+          pk.z = (uint32_t)f2bf(acc(8 * v + 4)) | ((uint32_t)f2bf(acc(8 * v + 5)) << 16);
+          pk.w = (uint32_t)f2bf(acc(8 * v + 6)) | ((uint32_t)f2bf(acc(8 * v + 7)) << 16);
           dst[v] = pk;
         }
         // stores into other GPUs' memory (the expert-parallel return) are
@@ -432,7 +479,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
       float am = 0.0f;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        h[j] = swiglu_bf16(bfround(acc[j]), bfround(acc[32 + j]));
+        h[j] = swiglu_bf16(bfround(acc(j)), bfround(acc(32 + j)));
         am = fmaxf(am, fabsf(h[j]));
       }
 #pragma unroll
@@ -444,7 +491,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
       const float scl = __fdiv_rn(fmaxf(amax, 1e-30f), 127.0f);
       const float inv = __fdiv_rn(1.0f, scl);
       if (live) {
-        const size_t o = (size_t)blockIdx.x * P.Rpad_h + row;
+        const size_t o = (size_t)row * P.h_srow + blockIdx.x;   // row-major, padded stride
         if (half == 0) {
           if (EPI == kEpiSwigluQ8) P.hsc[o] = scl;
           P.hrs[o] = sum;
@@ -478,12 +525,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     if (*abort_flag) {
       // let any issued MMA drain before the columns are released (bounded)
       if (lane == 0) {
-        mma_commit(drain);
-        for (uint32_t i = 0; i < kSpinLimit && !mbar_try(drain, 0); ++i) __nanosleep(128);
+        mma_commit(bar(B_DRAIN));
+        for (uint32_t i = 0; i < kSpinLimit && !mbar_try(bar(B_DRAIN), 0); ++i) __nanosleep(128);
       }
       __syncwarp();
     }
@@ -494,75 +541,141 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_tc05_kernel(GemmParams P) {
 }
 
 template <bool I8, int EPI>
-static cudaError_t launch_tc05_one(const GemmParams& P, int maxt, cudaStream_t s) {
+static cudaError_t launch_tc05_one(const GemmParams& P, const Tc05Maps& M, int maxt, cudaStream_t s) {
   cudaError_t err = ensure_smem_attr((const void*)gemm_tc05_kernel<I8, EPI>, SMEM);
   if (err != cudaSuccess) return err;
   const int gx = (EPI == kEpiStore) ? P.N / BN : (P.N / 2) / 64;
-  gemm_tc05_kernel<I8, EPI><<<dim3(gx, maxt), NTHREADS, SMEM, s>>>(P);
+  gemm_tc05_kernel<I8, EPI><<<dim3(gx, maxt), NTHREADS, SMEM, s>>>(P, M);
   return cudaGetLastError();
+}
+
+bool gemm_tc05_supported(int K, int N) {
+  return K > 0 && K % kGroup == 0 && K / kGroup <= kMaxG && N > 0 && N % BN == 0;
 }
 
 cudaError_t launch_gemm_tc05(bool int8, int epi, const GemmParams& P, int maxt, cudaStream_t s) {
   if (maxt <= 0) return cudaSuccess;
+  const int G = P.K / kGroup;
+  // A: expert-sorted contiguous rows; row scalars row-major with a stride of
+  // whole 4-group boxes; the SwiGLU epilogues write h scalars the same way
+  if (!gemm_tc05_supported(P.K, P.N) || P.E <= 0 || P.a_nrows <= 0 || P.a_rows || P.a_map ||
+      P.s_g != 1 || P.s_r < G || P.s_r % 4 != 0 || (int8 && !P.asc) || !P.ars ||
+      (epi != kEpiStore && (P.h_srow < P.N / 128 || P.h_srow % 4 != 0)))
+    return cudaErrorInvalidValue;
+  Tc05Maps M;
+  const unsigned long long rows = (unsigned long long)P.a_nrows;
+  const float* xs = P.asc ? P.asc : P.ars;
+  if (!encode_2d(&M.a, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, P.A, (unsigned long long)P.K, rows, 64,
+                 BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&M.xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xs, (unsigned long long)P.s_r, rows, 4,
+                 BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_2d(&M.xr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, P.ars, (unsigned long long)P.s_r, rows,
+                 4, BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_2d(&M.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, P.W, (unsigned long long)P.K / 8,
+                 (unsigned long long)P.E * P.N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&M.s, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, P.st, (unsigned long long)P.N,
+                 (unsigned long long)P.E * G, 32, G, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_2d(&M.b, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, P.bt, (unsigned long long)P.N,
+                 (unsigned long long)P.E * G, 32, G, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
   if (int8) {
-    if (epi == kEpiStore) return launch_tc05_one<true, kEpiStore>(P, maxt, s);
-    if (epi == kEpiSwigluQ8) return launch_tc05_one<true, kEpiSwigluQ8>(P, maxt, s);
-    return launch_tc05_one<true, kEpiSwigluH16>(P, maxt, s);
+    if (epi == kEpiStore) return launch_tc05_one<true, kEpiStore>(P, M, maxt, s);
+    if (epi == kEpiSwigluQ8) return launch_tc05_one<true, kEpiSwigluQ8>(P, M, maxt, s);
+    return launch_tc05_one<true, kEpiSwigluH16>(P, M, maxt, s);
   }
-  if (epi == kEpiStore) return launch_tc05_one<false, kEpiStore>(P, maxt, s);
-  if (epi == kEpiSwigluQ8) return launch_tc05_one<false, kEpiSwigluQ8>(P, maxt, s);
-  return launch_tc05_one<false, kEpiSwigluH16>(P, maxt, s);
+  if (epi == kEpiStore) return launch_tc05_one<false, kEpiStore>(P, M, maxt, s);
+  if (epi == kEpiSwigluQ8) return launch_tc05_one<false, kEpiSwigluQ8>(P, M, maxt, s);
+  return launch_tc05_one<false, kEpiSwigluH16>(P, M, maxt, s);
 }
 
-// Operand prep for the tcgen05 GEMMs: one warp per (row, 64-group), lane l
-// holds elements 2l, 2l+1.  QUANT: the int8 codes xu - 128 as fp16 plus the
-// per-group scale and exact sum; otherwise x itself in fp16 plus the sum.
+// Operand prep for the tcgen05 GEMMs: one warp per output row, lane l owns
+// the 64-groups l, l + 32, ...  QUANT: the int8 codes xu - 128 as fp16 plus
+// the per-group scale and exact sum; otherwise x itself in fp16 plus the sum.
 // Elements are stored in the (0,4,1,5,2,6,3,7) order of every 8-chunk.
+// Output row m reads x row m, or (gathered, expert-sorted) x row
+// a_map[a_rows[m]] / a_rows[m] / a_div; its scalars sit at m * srow + g.
+// The group sum is the pair sums (2j, 2j+1) reduced by the xor tree
+// 16, 8, 4, 2, 1 — the order of a butterfly over 32 lanes holding one pair
+// each — so every prep and the CPU oracle agree bit for bit.
 template <bool QUANT>
 __global__ void __launch_bounds__(256) prep_a16_kernel(const uint16_t* __restrict__ x, int R, int K,
+                                                        const int32_t* __restrict__ a_rows,
+                                                        const int32_t* __restrict__ a_map,
+                                                        int a_div, int srow,
                                                         uint16_t* __restrict__ a16,
                                                         float* __restrict__ xsc,
                                                         float* __restrict__ xrs) {
   const int lane = threadIdx.x & 31;
-  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long m = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (m >= R) return;
   const int G = K / kGroup;
-  if (w >= (long long)R * G) return;
-  const int m = (int)(w / G), g = (int)(w % G);
-  const uint32_t pr = *reinterpret_cast<const uint32_t*>(x + (size_t)m * K + g * kGroup + 2 * lane);
-  float a = bf2f((uint16_t)(pr & 0xffffu)), b = bf2f((uint16_t)(pr >> 16));
-  const float sum = warp_butterfly_sum(__fadd_rn(a, b));
-  if (!QUANT) {
-    // x itself becomes the fp16 operand: it overflows past 65504, and a group
-    // lying wholly below fp16's normal range keeps too few bits
-    const float gm = warp_max(fmaxf(fabsf(a), fabsf(b)));
-    if (lane == 0 && (gm >= 65504.0f || (gm > 0.0f && gm < 6.103515625e-05f)))
-      atomicExch(&g_tc05_error, 2);
+  const int src = !a_rows ? (int)m : (a_map ? a_map[a_rows[m]] : a_rows[m] / a_div);
+  for (int g = lane; g < G; g += 32) {
+    const uint4* xp = reinterpret_cast<const uint4*>(x + (size_t)src * K + g * kGroup);
+    uint4 raw[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) raw[i] = __ldg(xp + i);
+    float v[64];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) unpack8_bf16(raw[i], v + 8 * i);
+    float p[32];
+    float am = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      p[j] = __fadd_rn(v[2 * j], v[2 * j + 1]);
+      am = fmaxf(am, fmaxf(fabsf(v[2 * j]), fabsf(v[2 * j + 1])));
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+      for (int j = 0; j < off; ++j) p[j] = __fadd_rn(p[j], p[j + off]);
+    const float sum = p[0];
+    if (!QUANT) {
+      // x itself becomes the fp16 operand: it overflows past 65504, and a
+      // group lying wholly below fp16's normal range keeps too few bits
+      if (am >= 65504.0f || (am > 0.0f && am < 6.103515625e-05f)) atomicExch(&g_tc05_error, 2);
+    }
+    if (QUANT) {
+      const float sc = __fdiv_rn(fmaxf(am, 1e-30f), 127.0f);
+      const float inv = __fdiv_rn(1.0f, sc);
+#pragma unroll
+      for (int k = 0; k < 64; ++k)
+        v[k] = __fadd_rn(fminf(fmaxf(__fadd_rn(rintf(__fmul_rn(v[k], inv)), 128.0f), 0.0f), 255.0f),
+                         -128.0f);
+      xsc[(size_t)m * srow + g] = sc;
+    }
+    xrs[(size_t)m * srow + g] = sum;
+    uint4* dst = reinterpret_cast<uint4*>(a16 + (size_t)m * K + g * kGroup);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const float* e = v + 8 * c;   // stored order 0,4,1,5,2,6,3,7
+      auto h = [](float f) { return (uint32_t)__half_as_ushort(__float2half_rn(f)); };
+      uint4 pk;
+      pk.x = h(e[0]) | (h(e[4]) << 16);
+      pk.y = h(e[1]) | (h(e[5]) << 16);
+      pk.z = h(e[2]) | (h(e[6]) << 16);
+      pk.w = h(e[3]) | (h(e[7]) << 16);
+      dst[c] = pk;
+    }
   }
-  if (QUANT) {
-    const float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
-    const float sc = __fdiv_rn(fmaxf(amax, 1e-30f), 127.0f);
-    const float inv = __fdiv_rn(1.0f, sc);
-    a = __fadd_rn(fminf(fmaxf(__fadd_rn(rintf(__fmul_rn(a, inv)), 128.0f), 0.0f), 255.0f), -128.0f);
-    b = __fadd_rn(fminf(fmaxf(__fadd_rn(rintf(__fmul_rn(b, inv)), 128.0f), 0.0f), 255.0f), -128.0f);
-    if (lane == 0) xsc[(size_t)m * G + g] = sc;
-  }
-  if (lane == 0) xrs[(size_t)m * G + g] = sum;
-  uint16_t* dst = a16 + (size_t)m * K + g * kGroup;
-  const int k0 = 2 * lane;
-  dst[p8(k0)] = __half_as_ushort(__float2half_rn(a));
-  dst[p8(k0 + 1)] = __half_as_ushort(__float2half_rn(b));
+}
+
+cudaError_t launch_prep_a16_rows(const uint16_t* x, int R, int K, bool quant, const int32_t* a_rows,
+                                 const int32_t* a_map, int a_div, int srow, uint16_t* a16,
+                                 float* xsc, float* xrs, cudaStream_t s) {
+  if (R <= 0 || K <= 0) return cudaSuccess;
+  const unsigned blocks = (unsigned)(((long long)R * 32 + 255) / 256);
+  if (quant)
+    prep_a16_kernel<true><<<blocks, 256, 0, s>>>(x, R, K, a_rows, a_map, a_div, srow, a16, xsc, xrs);
+  else
+    prep_a16_kernel<false><<<blocks, 256, 0, s>>>(x, R, K, a_rows, a_map, a_div, srow, a16, xsc,
+                                                  xrs);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_prep_a16(const uint16_t* x, int R, int K, bool quant, uint16_t* a16, float* xsc,
                             float* xrs, cudaStream_t s) {
-  const long long warps = (long long)R * (K / kGroup);
-  if (warps <= 0) return cudaSuccess;
-  const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
-  if (quant)
-    prep_a16_kernel<true><<<blocks, 256, 0, s>>>(x, R, K, a16, xsc, xrs);
-  else
-    prep_a16_kernel<false><<<blocks, 256, 0, s>>>(x, R, K, a16, xsc, xrs);
-  return cudaGetLastError();
+  return launch_prep_a16_rows(x, R, K, quant, nullptr, nullptr, 1, K / kGroup, a16, xsc, xrs, s);
 }
 
 int tc05_error_flag() {

@@ -1,6 +1,7 @@
 // Internal launch interface between the C ABI (capi.cu) and the kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -33,6 +34,7 @@ struct GemmParams {
   const int32_t* a_rows;  // optional: sorted row r reads A row a_rows[r] / a_div,
   int a_div;              // or a_map[a_rows[r]] when a_map is set
   const int32_t* a_map;
+  int E;                // experts in W / st / bt (tcgen05 kernel: TMA map extents)
   const uint32_t* W;    // [E][N][K/8] packed int4
   const uint16_t* st;   // [E][G][N] bf16 scales
   const uint16_t* bt;   // [E][G][N] bf16 biases
@@ -48,6 +50,8 @@ struct GemmParams {
   float* hsc;           // [N/128][Rpad_h]
   float* hrs;           // [N/128][Rpad_h]
   int Rpad_h;
+  int h_srow;           // tcgen05 kernel: h scalars are written row-major, [rows][h_srow]
+  int a_nrows;          // tcgen05 kernel: rows of A (expert-sorted, contiguous; TMA extent)
   uint16_t* h16p;       // SwiGLU-H16: fp16 operand layout [Rpad][N/2]
   uint16_t* hbf;        // optional bf16 h [R][N/2]
 };
@@ -116,9 +120,20 @@ cudaError_t launch_quantize_rows(const uint16_t* x, int R, int K, int8_t* xq, fl
 cudaError_t launch_gemm_grouped(bool int8, int epi, const GemmParams& P, int maxt, cudaStream_t s);
 // tcgen05 version: A operands are fp16 [rows][K] with every 8-element chunk
 // in (0,4,1,5,2,6,3,7) order (prep_a16); SwiGLU epilogues write h the same way.
+// tcgen05 grouped GEMM: A expert-sorted ([a_nrows][K] fp16, no a_rows / a_map),
+// row scalars [a_nrows][s_r] (s_g = 1, s_r a multiple of 4), K <= 3072.
+bool gemm_tc05_supported(int K, int N);
 cudaError_t launch_gemm_tc05(bool int8, int epi, const GemmParams& P, int maxt, cudaStream_t s);
 cudaError_t launch_prep_a16(const uint16_t* x, int R, int K, bool quant, uint16_t* a16, float* xsc,
                             float* xrs, cudaStream_t s);
+// Gathered variant: output row m reads x row a_map[a_rows[m]] (a_map set) or
+// a_rows[m] / a_div (a_rows set, else m); scalars at m * srow + g.
+cudaError_t launch_prep_a16_rows(const uint16_t* x, int R, int K, bool quant, const int32_t* a_rows,
+                                 const int32_t* a_map, int a_div, int srow, uint16_t* a16,
+                                 float* xsc, float* xrs, cudaStream_t s);
+// Scalar row stride of the tcgen05 kernel's operands: groups padded to 4
+// (one 16-byte TMA box column per 4 groups).
+inline int tc05_srow(int G) { return (G + 3) & ~3; }
 int tc05_error_flag();
 
 // Persistent swap-AB grouped GEMM (gemm_sw.cu): weight rows on the MMA's M
@@ -254,6 +269,11 @@ cudaError_t launch_dense_tiles(int R, int tile_m, int32_t* tile_row, int32_t* ti
 cudaError_t ensure_smem_attr(const void* func, int bytes);
 // SMs of the current device, cached per device; thread-safe.
 int device_sm_count();
+// 2D TMA map over a row-major [rows][cols] array of `esize`-byte elements
+// (no interleave, L2 256B promotion, no OOB fill); false if it cannot be made.
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base,
+               unsigned long long cols, unsigned long long rows, unsigned box_cols,
+               unsigned box_rows, CUtensorMapSwizzle sw);
 
 // The decoder-layer steps either side of the block (norm.cu).
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps,

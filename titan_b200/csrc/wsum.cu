@@ -73,13 +73,96 @@ __global__ void __launch_bounds__(256) wsum_kernel(const uint16_t* __restrict__ 
   *reinterpret_cast<uint4*>(out + (size_t)t * D + d0) = pk;
 }
 
+// The same arithmetic with every expert row of the thread in flight at once:
+// the k source indices, scores and 16-byte row loads are issued before any
+// product, so a thread waits for one memory latency instead of k.  Slot s
+// accumulates the products j = s, s + 8, ... in order (clone mode rounds each
+// step to bf16), then the eight slots combine in order — the bits of
+// wsum_kernel.
+template <int KMAX>
+__global__ void __launch_bounds__(256) wsum_prefetch_kernel(const uint16_t* __restrict__ ys,
+                                                            const int32_t* __restrict__ inv,
+                                                            const uint16_t* __restrict__ scores,
+                                                            int T, int k, int D, int mode,
+                                                            const uint16_t* __restrict__ sh,
+                                                            const float* __restrict__ gate_logit,
+                                                            uint16_t* __restrict__ out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int dv = D / 8;
+  if (i >= (long long)T * dv) return;
+  const int t = (int)(i / dv), d0 = (int)(i % dv) * 8;
+  int src[KMAX];
+  float sc[KMAX];
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) {
+    if (j < k) {
+      const int p = t * k + j;
+      src[j] = inv ? __ldg(inv + p) : p;
+      sc[j] = bf2f(__ldg(scores + p));
+    }
+  }
+  uint4 raw[KMAX];
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j)
+    if (j < k) raw[j] = __ldg(reinterpret_cast<const uint4*>(ys + (size_t)src[j] * D + d0));
+  float sg = 0.0f;
+  if (sh) sg = bfround(csigmoid(bfround(gate_logit[t])));
+  uint16_t o[8];
+#pragma unroll
+  for (int v = 0; v < 8; ++v) {
+    float part[8];
+#pragma unroll
+    for (int a = 0; a < 8; ++a) part[a] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      if (j < k) {
+        const uint32_t wd = (v >> 1) == 0 ? raw[j].x
+                            : (v >> 1) == 1 ? raw[j].y
+                            : (v >> 1) == 2 ? raw[j].z : raw[j].w;
+        const uint32_t w = (v & 1) ? (wd & 0xffff0000u) : (wd << 16);
+        float prod = __fmul_rn(sc[j], __uint_as_float(w));
+        if (mode == 0) prod = bfround(prod);
+        const float tt = __fadd_rn(part[j & 7], prod);
+        part[j & 7] = (mode == 0) ? bfround(tt) : tt;
+      }
+    }
+    float a = part[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) {
+      a = __fadd_rn(a, part[j]);
+      if (mode == 0) a = bfround(a);
+    }
+    a = bfround(a);
+    if (sh) {
+      const float shv = bfround(__fmul_rn(sg, bf2f(sh[(size_t)t * D + d0 + v])));
+      a = __fadd_rn(a, shv);
+    }
+    o[v] = f2bf(a);
+  }
+  uint4 pk;
+  pk.x = o[0] | ((uint32_t)o[1] << 16);
+  pk.y = o[2] | ((uint32_t)o[3] << 16);
+  pk.z = o[4] | ((uint32_t)o[5] << 16);
+  pk.w = o[6] | ((uint32_t)o[7] << 16);
+  *reinterpret_cast<uint4*>(out + (size_t)t * D + d0) = pk;
+}
+
 cudaError_t launch_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
                         int D, int mode, const uint16_t* sh, const float* gate_logit, uint16_t* out,
                         cudaStream_t s) {
   const long long n = (long long)T * (D / 8);
-  if (n > 0)
-    wsum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ys, inv, scores, T, k, D, mode, sh,
-                                                            gate_logit, out);
+  if (n <= 0) return cudaGetLastError();
+  const unsigned grid = (unsigned)((n + 255) / 256);
+  if (k <= 8)
+    wsum_prefetch_kernel<8><<<grid, 256, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit, out);
+  else if (k <= 12)
+    wsum_prefetch_kernel<12><<<grid, 256, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit,
+                                                 out);
+  else if (k <= 16)
+    wsum_prefetch_kernel<16><<<grid, 256, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit,
+                                                 out);
+  else
+    wsum_kernel<<<grid, 256, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit, out);
   return cudaGetLastError();
 }
 
