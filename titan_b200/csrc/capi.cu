@@ -1095,7 +1095,7 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
   }
   if (fr) {
     const FastRoute rt{b.tile_row, b.tile_exp, b.ntiles, b.offsets, rmaxt, b.order, k, nullptr};
-    if (int rc = run_fast(routed_proj(L), x, T, R, i8, d8, rt, b.fr, b.ys, nullptr, nullptr, s,
+    if (int rc = run_fast(routed_proj(L), x, T, R, i8, d8, rt, b.fr, b.ys, b.order, nullptr, s,
                           kRoutedNames))
       return rc;
   } else {
@@ -1156,6 +1156,7 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
     dn.K = I;
     dn.N = H;
     dn.Y = b.ys;
+    dn.y_rows = b.order;   // pair-major: the weighted sum reads a token's k rows contiguously
     TMOE_TRY(gemm(d8, kEpiStore, dn, rmaxt), "gemm_down");
   }
   if (Is > 0) {
@@ -1211,7 +1212,7 @@ int tmoe_moe_forward(const tmoe_layer* L, const uint16_t* x, int T, const tmoe_o
       TMOE_TRY(gemm(false, kEpiStore, sd, st), "gemm_shared_down");
     }
   }
-  TMOE_TRY(launch_wsum(b.ys, b.inv, scores, T, k, H, opt_wsum(opt), Is > 0 ? b.ys_sh : nullptr,
+  TMOE_TRY(launch_wsum(b.ys, nullptr, scores, T, k, H, opt_wsum(opt), Is > 0 ? b.ys_sh : nullptr,
                        b.gate_logit, y, s),
            "weighted_sum");
   return TMOE_OK;

@@ -48,7 +48,7 @@ __device__ int g_tc05_error = 0;
 namespace tc {
 
 constexpr int BM = 128, BN = 128;
-constexpr int NA = 4;                             // activation tiles (one group each)
+constexpr int NA = 3;                             // activation tiles (one group each)
 constexpr int NB = 3;                             // widened weight tiles (one group each)
 constexpr int NQ = 2;                             // packed stages (4 groups each)
 constexpr int kMaxG = 48;                         // K <= 3072: scale / bias tables held whole
@@ -62,9 +62,9 @@ constexpr int A_OFF = 0;
 constexpr int B_OFF = A_OFF + NA * A_BYTES;
 constexpr int Q_OFF = B_OFF + NB * B_BYTES;
 constexpr int CS_OFF = Q_OFF + NQ * Q_BYTES;
-constexpr int TB_OFF = CS_OFF + NB * CS_BYTES;    // 8 table boxes [G][32] bf16 (s x 4, b x 4)
-constexpr int TB_BYTES = 8 * 64 * kMaxG;
-constexpr int XCH_OFF = TB_OFF + TB_BYTES;
+constexpr int TB_OFF = CS_OFF + NB * CS_BYTES;    // 2 x 8 table boxes [G][32] bf16 (s x 4, b x 4)
+constexpr int TB_BYTES = 8 * 64 * kMaxG;          // one work item's tables
+constexpr int XCH_OFF = TB_OFF + 2 * TB_BYTES;
 constexpr int BAR_OFF = XCH_OFF + BM * 36 * 4;
 constexpr int SMEM = BAR_OFF + 512 + 1024;        // + alignment slack
 static_assert(A_OFF % 1024 == 0 && B_OFF % 1024 == 0 && Q_OFF % 1024 == 0 && Q_BYTES % 1024 == 0 &&
@@ -75,10 +75,10 @@ constexpr int NTHREADS = 512;
 constexpr int NCONV = 192;                        // converter warps 2-7
 // barrier indices (uint64 each) at BAR_OFF
 constexpr int B_AF = 0, B_AE = B_AF + NA, B_BF = B_AE + NA, B_BE = B_BF + NB, B_QF = B_BE + NB,
-              B_QE = B_QF + NQ, B_TF = B_QE + NQ, B_TE = B_TF + 2, B_TBL = B_TE + 2,
-              B_DRAIN = B_TBL + 1, B_SLOT = B_DRAIN + 1, B_ABORT = B_SLOT + 1,
-              B_PRESCALE = B_ABORT + 1;
-static_assert((B_PRESCALE + 1) * 8 <= 512, "barrier area");
+              B_QE = B_QF + NQ, B_TF = B_QE + NQ, B_TE = B_TF + 2, B_TBF = B_TE + 2,
+              B_TBE = B_TBF + 2, B_DRAIN = B_TBE + 2, B_SLOT = B_DRAIN + 1,
+              B_ABORT = B_SLOT + 1, B_PRESCALE = B_ABORT + 1;   // 4 prescale flags (ints)
+static_assert((B_PRESCALE + 2) * 8 <= 512, "barrier area");
 // Bounded wait recording into this kernel's error flag.
 TMOE_DEV bool mbar_wait(uint32_t a, uint32_t parity, volatile int* abort_flag) {
   return tc::mbar_wait(a, parity, abort_flag, &g_tc05_error);
@@ -120,22 +120,20 @@ template <bool I8, int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc05_kernel(const __grid_constant__ GemmParams P, const __grid_constant__ Tc05Maps M) {
   extern __shared__ uint8_t smem_raw[];
-  const int tile = blockIdx.y;
-  if (tile >= P.ntiles[0]) return;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int e = P.tile_exp[tile], row0 = P.tile_row[tile], rowend = P.offsets[e + 1];
   const int G = P.K / kGroup;
   constexpr bool SW = EPI != kEpiStore;
   const int Ih = P.N / 2;
-  const int n0 = blockIdx.x * (SW ? 64 : BN);
+  const int gx = SW ? Ih / 64 : P.N / BN;     // column blocks per tile
+  const int nitems = P.ntiles[0] * gx;        // work items: (row tile, column block)
   const int TBS = (64 * G + 127) & ~127;      // bytes per table box, 128-byte aligned
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   auto bar = [&](int i) -> uint32_t { return smem_u32(bars + i); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_SLOT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + B_ABORT);
-  int* prescale_flag = reinterpret_cast<int*>(bars + B_PRESCALE);
+  int* prescale_flag = reinterpret_cast<int*>(bars + B_PRESCALE);   // [4], by item
   float* xch = reinterpret_cast<float*>(smem + XCH_OFF);           // [128][36]
 
   if (tid == 0) {
@@ -154,8 +152,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar(B_TF + b), 1);
       mbar_init(bar(B_TE + b), 8);
+      mbar_init(bar(B_TBF + b), 1);
+      mbar_init(bar(B_TBE + b), NCONV / 32);
     }
-    mbar_init(bar(B_TBL), 1);
     mbar_init(bar(B_DRAIN), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -163,9 +162,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tma_prefetch_desc(&M.w);
   }
   if (warp == 1) {
-    const uint32_t ncols = I8 ? 2 * BN : BN;
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)), "r"(ncols));
+                     smem_u32(tmem_slot)), "r"(2 * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -173,108 +171,137 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // weight row of B-tile row c: the SwiGLU tiles interleave 32-row segments
-  // (gate lo, up lo, gate hi, up hi) so that each epilogue half holds matching
-  // gate and up columns
-  auto wrow = [&](int c) -> int {
+  // weight row of B-tile row c of column block nb: the SwiGLU tiles
+  // interleave 32-row segments (gate lo, up lo, gate hi, up hi) so that each
+  // epilogue half holds matching gate and up columns
+  auto wrow = [&](int nb, int c) -> int {
+    const int n0 = nb * (SW ? 64 : BN);
     if (!SW) return n0 + c;
     const int q = c >> 5;
     const int j = c & 31;
     return ((q & 1) ? Ih : 0) + n0 + ((q >> 1) << 5) + j;
   };
-  const int nq = (G + 3) >> 2;                // packed stages of this tile
 
   if (warp == 0) {
     // ---------------------------------------------------------------- loader
-    // One thread issues every copy, all TMA (no multicast): the tables once,
-    // then per group the 16 KB activation tile and per 4 groups the packed
-    // weight rows (4 x 4 KB) and the row scalars (2 x 2 KB).  Coordinates:
-    // x of every box is a multiple of 16 bytes; rows past the operand's end
-    // read zeros.
+    // One thread issues every copy, all TMA (no multicast): per work item the
+    // scale / bias tables (double-buffered across items), per group the 16 KB
+    // activation tile, per 4 groups the packed weight rows (4 x 4 KB) and the
+    // row scalars (2 x 2 KB).  x of every box is a multiple of 16 bytes; rows
+    // past the operand's end read zeros.  Ring phases count across items.
     if (lane == 0) {
-      const uint32_t tbl = bar(B_TBL);
-      mbar_expect_tx(tbl, 8u * 64u * (uint32_t)G);
-      for (int seg = 0; seg < 4; ++seg) {
-        const int wr = wrow(seg * 32);
-        tma_load_2d(smem_u32(smem + TB_OFF + seg * TBS), &M.s, wr, e * G, tbl);
-        tma_load_2d(smem_u32(smem + TB_OFF + (4 + seg) * TBS), &M.b, wr, e * G, tbl);
-      }
       const uint32_t qtx = (uint32_t)QW_BYTES + (I8 ? 2u : 1u) * (uint32_t)QS_BYTES;
-      int issued_a = 0, issued_q = 0;
+      int ga = 0, gq = 0, it = 0;
       bool ok = true;
-      for (int g = 0; g < G && ok; ++g) {
-        if ((g & 3) == 0) {
-          const int q = g >> 2, sq = q % NQ;
-          if (!(ok = mbar_wait(bar(B_QE + sq), ((q / NQ) & 1) ^ 1, abort_flag))) break;
-          const uint32_t qb = bar(B_QF + sq);
-          uint8_t* qs = smem + Q_OFF + sq * Q_BYTES;
-          mbar_expect_tx(qb, qtx);
-          for (int seg = 0; seg < 4; ++seg)
-            tma_load_2d(smem_u32(qs + seg * 4096), &M.w, q * 32, e * P.N + wrow(seg * 32), qb);
-          if (I8) tma_load_2d(smem_u32(qs + QW_BYTES), &M.xs, q * 4, row0, qb);
-          tma_load_2d(smem_u32(qs + QW_BYTES + QS_BYTES), &M.xr, q * 4, row0, qb);
-          issued_q = q + 1;
+      for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++it) {
+        const int tile = item / gx, nb = item - tile * gx;
+        const int e = P.tile_exp[tile], row0 = P.tile_row[tile];
+        const int tb = it & 1;
+        if (!(ok = mbar_wait(bar(B_TBE + tb), ((it >> 1) & 1) ^ 1, abort_flag))) break;
+        mbar_expect_tx(bar(B_TBF + tb), 8u * 64u * (uint32_t)G);
+        uint8_t* tbs = smem + TB_OFF + tb * TB_BYTES;
+        for (int seg = 0; seg < 4; ++seg) {
+          const int wr = wrow(nb, seg * 32);
+          tma_load_2d(smem_u32(tbs + seg * TBS), &M.s, wr, e * G, bar(B_TBF + tb));
+          tma_load_2d(smem_u32(tbs + (4 + seg) * TBS), &M.b, wr, e * G, bar(B_TBF + tb));
         }
-        const int sa = g % NA;
-        if (!(ok = mbar_wait(bar(B_AE + sa), ((g / NA) & 1) ^ 1, abort_flag))) break;
-        mbar_expect_tx(bar(B_AF + sa), A_BYTES);
-        tma_load_2d(smem_u32(smem + A_OFF + sa * A_BYTES), &M.a, g * 64, row0, bar(B_AF + sa));
-        issued_a = g + 1;
+        for (int g = 0; g < G && ok; ++g) {
+          if ((g & 3) == 0) {
+            const int sq = gq % NQ;
+            if (!(ok = mbar_wait(bar(B_QE + sq), ((gq / NQ) & 1) ^ 1, abort_flag))) break;
+            const uint32_t qb = bar(B_QF + sq);
+            uint8_t* qs = smem + Q_OFF + sq * Q_BYTES;
+            mbar_expect_tx(qb, qtx);
+            for (int seg = 0; seg < 4; ++seg)
+              tma_load_2d(smem_u32(qs + seg * 4096), &M.w, (g >> 2) * 32,
+                          e * P.N + wrow(nb, seg * 32), qb);
+            if (I8) tma_load_2d(smem_u32(qs + QW_BYTES), &M.xs, (g >> 2) * 4, row0, qb);
+            tma_load_2d(smem_u32(qs + QW_BYTES + QS_BYTES), &M.xr, (g >> 2) * 4, row0, qb);
+            ++gq;
+          }
+          const int sa = ga % NA;
+          if (!(ok = mbar_wait(bar(B_AE + sa), ((ga / NA) & 1) ^ 1, abort_flag))) break;
+          mbar_expect_tx(bar(B_AF + sa), A_BYTES);
+          tma_load_2d(smem_u32(smem + A_OFF + sa * A_BYTES), &M.a, g * 64, row0, bar(B_AF + sa));
+          ++ga;
+        }
       }
       // copies still in flight (after an abort) land before the CTA exits
       auto drain_wait = [&](uint32_t b, uint32_t par) {
         for (uint32_t i = 0; i < kSpinLimit && !mbar_try(b, par); ++i) __nanosleep(128);
       };
-      drain_wait(tbl, 0);
-      for (int g = issued_a > NA ? issued_a - NA : 0; g < issued_a; ++g)
-        drain_wait(bar(B_AF + g % NA), (g / NA) & 1);
-      for (int q = issued_q > NQ ? issued_q - NQ : 0; q < issued_q; ++q)
-        drain_wait(bar(B_QF + q % NQ), (q / NQ) & 1);
+      for (int i = it > 2 ? it - 2 : 0; i < it; ++i) drain_wait(bar(B_TBF + (i & 1)), (i >> 1) & 1);
+      for (int g = ga > NA ? ga - NA : 0; g < ga; ++g) drain_wait(bar(B_AF + g % NA), (g / NA) & 1);
+      for (int q = gq > NQ ? gq - NQ : 0; q < gq; ++q) drain_wait(bar(B_QF + q % NQ), (q / NQ) & 1);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      for (int g = 0; g < G; ++g) {
-        const int sa = g % NA, sb = g % NB;
-        if (!mbar_wait(bar(B_AF + sa), (g / NA) & 1, abort_flag)) break;
-        if (!mbar_wait(bar(B_BF + sb), (g / NB) & 1, abort_flag)) break;
-        const int b = I8 ? (g & 1) : 0;
-        if (I8 && !mbar_wait(bar(B_TE + b), ((g >> 1) & 1) ^ 1, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + A_OFF + sa * A_BYTES);
-        const uint32_t b_base = smem_u32(smem + B_OFF + sb * B_BYTES);
-        const uint32_t d = tmem + (uint32_t)(b * BN);
+      int ga = 0, gb = 0, gt = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+        if (!I8) {   // STOCK: one accumulator buffer per item
+          if (!(ok = mbar_wait(bar(B_TE + (gt & 1)), ((gt >> 1) & 1) ^ 1, abort_flag))) break;
+        }
+        for (int g = 0; g < G; ++g) {
+          const int sa = ga % NA, sb = gb % NB;
+          if (!(ok = mbar_wait(bar(B_AF + sa), (ga / NA) & 1, abort_flag))) break;
+          if (!(ok = mbar_wait(bar(B_BF + sb), (gb / NB) & 1, abort_flag))) break;
+          if (I8 && !(ok = mbar_wait(bar(B_TE + (gt & 1)), ((gt >> 1) & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + A_OFF + sa * A_BYTES);
+          const uint32_t b_base = smem_u32(smem + B_OFF + sb * B_BYTES);
+          const uint32_t d = tmem + (uint32_t)((gt & 1) * BN);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_f16(d, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32),
-                  (kk > 0 || (!I8 && g > 0)) ? 1u : 0u);
-        mma_commit(bar(B_AE + sa));
-        mma_commit(bar(B_BE + sb));
-        if (I8) mma_commit(bar(B_TF + b));
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16(d, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32),
+                    (kk > 0 || (!I8 && g > 0)) ? 1u : 0u);
+          mma_commit(bar(B_AE + sa));
+          mma_commit(bar(B_BE + sb));
+          ++ga;
+          ++gb;
+          if (I8) {
+            mma_commit(bar(B_TF + (gt & 1)));
+            ++gt;
+          }
+        }
+        if (!I8 && ok) {
+          mma_commit(bar(B_TF + (gt & 1)));
+          ++gt;
+        }
       }
-      if (!I8) mma_commit(bar(B_TF));
     }
     __syncwarp();
   } else if (warp < 8) {
     // ------------------------------------------------------------- converters
-    // Widen group g's packed rows into the fp16 B operand (128B-swizzled
+    // Widen each group's packed rows into the fp16 B operand (128B-swizzled
     // K-major) and write the group's fp32 column scalars.  Work item
     // i = (tile row i / 8, word i % 8): a warp covers 4 rows x 8 words per
-    // step; both the swizzled packed stage and the B tile are read / written
-    // without bank conflicts.  The six items of a thread are loaded before any
-    // is widened.
+    // step; the swizzled packed stage and the B tile are read / written
+    // without bank conflicts.  The items of a thread are loaded before any is
+    // widened.
     const int ct = tid - 64;
-    if (!mbar_wait(bar(B_TBL), 0, abort_flag)) {
-      converters_and(false);
-    } else {
-      const uint8_t* tb = smem + TB_OFF;
+    constexpr int NIT = (BN * 8 + NCONV - 1) / NCONV;
+    int gb = 0, gq = 0, it = 0;
+    bool ok = true;
+    // Every converter thread reaches the same named barriers in the same
+    // order: a failed wait only ends the item, and the next item's barrier
+    // ends the loop for all of them at once.
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++it) {
+      const int tb = it & 1;
+      const bool tok = ok && mbar_wait(bar(B_TBF + tb), (it >> 1) & 1, abort_flag);
+      if (!converters_and(tok)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* tbs = smem + TB_OFF + tb * TB_BYTES;
       auto tab = [&](int which, int g, int c) -> uint16_t {   // which: 0 = s, 1 = b
-        return *reinterpret_cast<const uint16_t*>(tb + (which * 4 + (c >> 5)) * TBS + g * 64 +
+        return *reinterpret_cast<const uint16_t*>(tbs + (which * 4 + (c >> 5)) * TBS + g * 64 +
                                                   (c & 31) * 2);
       };
       // INT8: B can carry the scale, (q - 8) * s exact in fp16, when every
-      // scale of the tile is 0 or inside [2^-14, 2^12): then the MMA returns
+      // scale of the item is 0 or inside [2^-14, 2^12): then the MMA returns
       // D * s exactly (|D| <= 2^16, so D * s needs at most 24 bits).
       bool safe = true;
       for (int i = ct; i < G * BN; i += NCONV) {
@@ -283,18 +310,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         safe = safe && (((bv & 0x7fffu) == 0u) || (ex >= 113u && ex <= 138u));
       }
       const bool prescale = converters_and(safe);
-      if (ct == 0) *prescale_flag = prescale ? 1 : 0;
-      // STOCK accumulates every group in TMEM, so B must carry the scale: a
-      // tile whose scales fall outside fp16's exact range is reported (error
+      if (ct == 0) prescale_flag[it & 3] = prescale ? 1 : 0;
+      // STOCK accumulates every group in TMEM, so B must carry the scale: an
+      // item whose scales fall outside fp16's exact range is reported (error
       // 2, tmoe_device_status) — the swap-AB kernel with row normalisers has
       // no such limit.
       if (!I8 && !prescale && ct == 0) atomicExch(&g_tc05_error, 2);
       const bool scale_b = !I8 || prescale;
-      constexpr int NIT = (BN * 8 + NCONV - 1) / NCONV;
       for (int g = 0; g < G; ++g) {
-        const int q = g >> 2, sq = q % NQ, sb = g % NB;
-        if (!mbar_wait(bar(B_QF + sq), (q / NQ) & 1, abort_flag)) break;
-        if (!mbar_wait(bar(B_BE + sb), ((g / NB) & 1) ^ 1, abort_flag)) break;
+        const int sq = gq % NQ, sb = gb % NB;
+        if (!(ok = mbar_wait(bar(B_QF + sq), (gq / NQ) & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(bar(B_BE + sb), ((gb / NB) & 1) ^ 1, abort_flag))) break;
         const uint8_t* qs = smem + Q_OFF + sq * Q_BYTES;
         uint8_t* sB = smem + B_OFF + sb * B_BYTES;
         const int gg = g & 3;
@@ -335,189 +361,211 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) {
           mbar_arrive(bar(B_BF + sb));
           if (gg == 3 || g == G - 1) mbar_arrive(bar(B_QE + sq));
+          if (g == G - 1) mbar_arrive(bar(B_TBE + tb));   // this item's tables consumed
         }
+        ++gb;
+        if (gg == 3 || g == G - 1) ++gq;
       }
     }
   } else {
     // ---------------------------------------------------------------- epilogue
+    // Every epilogue warp walks every item (after a failed wait it skips the
+    // waits and stores nothing), so the named barriers of the SwiGLU tail are
+    // reached by all 256 threads the same number of times.
     const int q = warp & 3;                      // TMEM lane quadrant
     const int half = (warp - 8) >> 2;            // column half
     const int lr = q * 32 + lane;                // tile row of this thread
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    // accumulators as column pairs: the per-group rescale issues as packed
-    // f32x2 FMAs (each component rounds exactly as a scalar fma.rn)
-    float2 acc2[32];
-#pragma unroll
-    for (int c = 0; c < 32; ++c) acc2[c] = make_float2(0.0f, 0.0f);
-    auto acc = [&](int c) -> float { return (c & 1) ? acc2[c >> 1].y : acc2[c >> 1].x; };
+    int gb = 0, gq = 0, gt = 0, it = 0;
     bool ok = true;
-    bool prescaled = false;
-    for (int g = 0; g < G && ok; ++g) {
-      const int qd = g >> 2, sq = qd % NQ, sb = g % NB, gg = g & 3;
-      // row scalars of the packed stage (TMA), column scalars of the group
-      // (converters)
-      if (!mbar_wait(bar(B_QF + sq), (qd / NQ) & 1, abort_flag) ||
-          !mbar_wait(bar(B_BF + sb), (g / NB) & 1, abort_flag)) {
-        ok = false;
-        break;
-      }
-      if (g == 0) prescaled = *reinterpret_cast<volatile int*>(prescale_flag) != 0;
-      const float* qsc = reinterpret_cast<const float*>(smem + Q_OFF + sq * Q_BYTES + QW_BYTES);
-      const float xs = I8 ? qsc[lr * 4 + gg] : 0.0f;
-      const float xr = qsc[BM * 4 + lr * 4 + gg];
-      const float* csb = reinterpret_cast<const float*>(smem + CS_OFF + sb * CS_BYTES);
-      const float* cs = csb + 64 * half;
-      const float* cb = csb + BN + 64 * half;
-      if (I8) {
-        const int b = g & 1;
-        if (!mbar_wait(bar(B_TF + b), (g >> 1) & 1, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t ta = tmem + lane_addr + (uint32_t)(b * BN + 64 * half);
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++it) {
+      const int tile = item / gx, nb = item - tile * gx;
+      const int e = P.tile_exp[tile], row0 = P.tile_row[tile], rowend = P.offsets[e + 1];
+      const int n0 = nb * (SW ? 64 : BN);
+      // accumulators as column pairs: the per-group rescale issues as packed
+      // f32x2 FMAs (each component rounds exactly as a scalar fma.rn)
+      float2 acc2[32];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {       // two 32-column halves: fewer registers
-          float d[32];
-          tmem_ld16(ta + 32 * hh, d);
-          tmem_ld16(ta + 32 * hh + 16, d + 16);
-          tmem_wait_ld();
-          if (hh == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(B_TE + b));
-          }
-          // column scalars read 4 at a time (16-byte aligned in the stage)
-          const float4* cb4 = reinterpret_cast<const float4*>(cb + 32 * hh);
-          const float4* cs4 = reinterpret_cast<const float4*>(cs + 32 * hh);
-          const float2 xs2 = make_float2(xs, xs), xr2 = make_float2(xr, xr);
-          float2* a2 = acc2 + 16 * hh;
-          if (prescaled) {                     // d = D * s already (exact)
+      for (int c = 0; c < 32; ++c) acc2[c] = make_float2(0.0f, 0.0f);
+      auto acc = [&](int c) -> float { return (c & 1) ? acc2[c >> 1].y : acc2[c >> 1].x; };
+      bool prescaled = false;
+      for (int g = 0; g < G; ++g) {
+        const int sq = gq % NQ, sb = gb % NB, gg = g & 3;
+        const bool qend = gg == 3 || g == G - 1;
+        // row scalars of the packed stage (TMA), column scalars of the group
+        // (converters)
+        if (ok) ok = mbar_wait(bar(B_QF + sq), (gq / NQ) & 1, abort_flag) &&
+                     mbar_wait(bar(B_BF + sb), (gb / NB) & 1, abort_flag);
+        if (ok) {
+          if (g == 0) prescaled = reinterpret_cast<volatile int*>(prescale_flag)[it & 3] != 0;
+          const float* qsc = reinterpret_cast<const float*>(smem + Q_OFF + sq * Q_BYTES + QW_BYTES);
+          const float xs = I8 ? qsc[lr * 4 + gg] : 0.0f;
+          const float xr = qsc[BM * 4 + lr * 4 + gg];
+          const float* csb = reinterpret_cast<const float*>(smem + CS_OFF + sb * CS_BYTES);
+          const float* cs = csb + 64 * half;
+          const float* cb = csb + BN + 64 * half;
+          if (I8) {
+            const int b = gt & 1;
+            ok = mbar_wait(bar(B_TF + b), (gt >> 1) & 1, abort_flag);
+            if (ok) {
+              tc_fence_after();
+              const uint32_t ta = tmem + lane_addr + (uint32_t)(b * BN + 64 * half);
 #pragma unroll
-            for (int c4 = 0; c4 < 8; ++c4) {
-              const float4 b4 = cb4[c4];
-              a2[2 * c4] = __ffma2_rn(make_float2(d[4 * c4], d[4 * c4 + 1]), xs2, a2[2 * c4]);
-              a2[2 * c4] = __ffma2_rn(xr2, make_float2(b4.x, b4.y), a2[2 * c4]);
-              a2[2 * c4 + 1] =
-                  __ffma2_rn(make_float2(d[4 * c4 + 2], d[4 * c4 + 3]), xs2, a2[2 * c4 + 1]);
-              a2[2 * c4 + 1] = __ffma2_rn(xr2, make_float2(b4.z, b4.w), a2[2 * c4 + 1]);
+              for (int hh = 0; hh < 2; ++hh) {       // two 32-column halves: fewer registers
+                float d[32];
+                tmem_ld16(ta + 32 * hh, d);
+                tmem_ld16(ta + 32 * hh + 16, d + 16);
+                tmem_wait_ld();
+                if (hh == 1) {
+                  tc_fence_before();
+                  __syncwarp();
+                  if (lane == 0) mbar_arrive(bar(B_TE + b));
+                }
+                // column scalars read 4 at a time (16-byte aligned)
+                const float4* cb4 = reinterpret_cast<const float4*>(cb + 32 * hh);
+                const float4* cs4 = reinterpret_cast<const float4*>(cs + 32 * hh);
+                const float2 xs2 = make_float2(xs, xs), xr2 = make_float2(xr, xr);
+                float2* a2 = acc2 + 16 * hh;
+                if (prescaled) {                     // d = D * s already (exact)
+#pragma unroll
+                  for (int c4 = 0; c4 < 8; ++c4) {
+                    const float4 b4 = cb4[c4];
+                    a2[2 * c4] = __ffma2_rn(make_float2(d[4 * c4], d[4 * c4 + 1]), xs2, a2[2 * c4]);
+                    a2[2 * c4] = __ffma2_rn(xr2, make_float2(b4.x, b4.y), a2[2 * c4]);
+                    a2[2 * c4 + 1] =
+                        __ffma2_rn(make_float2(d[4 * c4 + 2], d[4 * c4 + 3]), xs2, a2[2 * c4 + 1]);
+                    a2[2 * c4 + 1] = __ffma2_rn(xr2, make_float2(b4.z, b4.w), a2[2 * c4 + 1]);
+                  }
+                } else {
+#pragma unroll
+                  for (int c4 = 0; c4 < 8; ++c4) {
+                    const float4 b4 = cb4[c4], s4 = cs4[c4];
+                    const float2 t0 = __fmul2_rn(make_float2(d[4 * c4], d[4 * c4 + 1]),
+                                                 make_float2(s4.x, s4.y));
+                    const float2 t1 = __fmul2_rn(make_float2(d[4 * c4 + 2], d[4 * c4 + 3]),
+                                                 make_float2(s4.z, s4.w));
+                    a2[2 * c4] = __ffma2_rn(t0, xs2, a2[2 * c4]);
+                    a2[2 * c4] = __ffma2_rn(xr2, make_float2(b4.x, b4.y), a2[2 * c4]);
+                    a2[2 * c4 + 1] = __ffma2_rn(t1, xs2, a2[2 * c4 + 1]);
+                    a2[2 * c4 + 1] = __ffma2_rn(xr2, make_float2(b4.z, b4.w), a2[2 * c4 + 1]);
+                  }
+                }
+              }
             }
           } else {
+            const float4* cb4 = reinterpret_cast<const float4*>(cb);
+            const float2 xr2 = make_float2(xr, xr);
 #pragma unroll
-            for (int c4 = 0; c4 < 8; ++c4) {
-              const float4 b4 = cb4[c4], s4 = cs4[c4];
-              const float2 t0 =
-                  __fmul2_rn(make_float2(d[4 * c4], d[4 * c4 + 1]), make_float2(s4.x, s4.y));
-              const float2 t1 =
-                  __fmul2_rn(make_float2(d[4 * c4 + 2], d[4 * c4 + 3]), make_float2(s4.z, s4.w));
-              a2[2 * c4] = __ffma2_rn(t0, xs2, a2[2 * c4]);
-              a2[2 * c4] = __ffma2_rn(xr2, make_float2(b4.x, b4.y), a2[2 * c4]);
-              a2[2 * c4 + 1] = __ffma2_rn(t1, xs2, a2[2 * c4 + 1]);
-              a2[2 * c4 + 1] = __ffma2_rn(xr2, make_float2(b4.z, b4.w), a2[2 * c4 + 1]);
+            for (int c4 = 0; c4 < 16; ++c4) {
+              const float4 b4 = cb4[c4];
+              acc2[2 * c4] = __ffma2_rn(xr2, make_float2(b4.x, b4.y), acc2[2 * c4]);
+              acc2[2 * c4 + 1] = __ffma2_rn(xr2, make_float2(b4.z, b4.w), acc2[2 * c4 + 1]);
             }
           }
-        }
-      } else {
-        const float4* cb4 = reinterpret_cast<const float4*>(cb);
-        const float2 xr2 = make_float2(xr, xr);
-#pragma unroll
-        for (int c4 = 0; c4 < 16; ++c4) {
-          const float4 b4 = cb4[c4];
-          acc2[2 * c4] = __ffma2_rn(xr2, make_float2(b4.x, b4.y), acc2[2 * c4]);
-          acc2[2 * c4 + 1] = __ffma2_rn(xr2, make_float2(b4.z, b4.w), acc2[2 * c4 + 1]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar(B_BE + sb));
-        if (gg == 3 || g == G - 1) mbar_arrive(bar(B_QE + sq));
-      }
-    }
-    if (!I8 && ok) {
-      if (mbar_wait(bar(B_TF), 0, abort_flag)) {
-        tc_fence_after();
-        const uint32_t ta = tmem + lane_addr + (uint32_t)(64 * half);
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float d[32];
-          tmem_ld16(ta + 32 * hh, d);
-          tmem_ld16(ta + 32 * hh + 16, d + 16);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 16; ++c)
-            acc2[16 * hh + c] = make_float2(__fadd_rn(d[2 * c], acc2[16 * hh + c].x),
-                                            __fadd_rn(d[2 * c + 1], acc2[16 * hh + c].y));
-        }
-        tc_fence_before();
-      } else {
-        ok = false;
-      }
-    }
-    const int row = row0 + lr;
-    const bool live = ok && row < rowend;
-    if constexpr (EPI == kEpiStore) {
-      if (live) {
-        const int orow = P.y_rows ? P.y_rows[row] : row;
-        uint16_t* yrow = P.y_ptr ? P.y_ptr[orow] : P.Y + (size_t)orow * P.N;
-        uint4* dst = reinterpret_cast<uint4*>(yrow + n0 + 64 * half);
-#pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          uint4 pk;
-          pk.x = (uint32_t)f2bf(acc(8 * v + 0)) | ((uint32_t)f2bf(acc(8 * v + 1)) << 16);
-          pk.y = (uint32_t)f2bf(acc(8 * v + 2)) | ((uint32_t)f2bf(acc(8 * v + 3)) << 16);
-          pk.z = (uint32_t)f2bf(acc(8 * v + 4)) | ((uint32_t)f2bf(acc(8 * v + 5)) << 16);
-          pk.w = (uint32_t)f2bf(acc(8 * v + 6)) | ((uint32_t)f2bf(acc(8 * v + 7)) << 16);
-          dst[v] = pk;
-        }
-        // stores into other GPUs' memory (the expert-parallel return) are
-        // performed at system scope before this kernel ends, ahead of the
-        // flag the next launch posts
-        if (P.y_ptr) __threadfence_system();
-      }
-    } else {
-      // SwiGLU of the 32 (gate, up) pairs this thread holds; h columns
-      // n0 + 32*half + j.  The 64-column quantisation group spans the two
-      // halves: pair sums and amax are exchanged through shared memory.
-      float h[32];
-      float am = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        h[j] = swiglu_bf16(bfround(acc(j)), bfround(acc(32 + j)));
-        am = fmaxf(am, fabsf(h[j]));
-      }
-#pragma unroll
-      for (int l = 0; l < 16; ++l) xch[lr * 36 + 16 * half + l] = __fadd_rn(h[2 * l], h[2 * l + 1]);
-      xch[lr * 36 + 32 + half] = am;
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      const float amax = fmaxf(xch[lr * 36 + 32], xch[lr * 36 + 33]);
-      const float sum = serial_butterfly32(xch + lr * 36, 1);
-      const float scl = __fdiv_rn(fmaxf(amax, 1e-30f), 127.0f);
-      const float inv = __fdiv_rn(1.0f, scl);
-      if (live) {
-        const size_t o = (size_t)row * P.h_srow + blockIdx.x;   // row-major, padded stride
-        if (half == 0) {
-          if (EPI == kEpiSwigluQ8) P.hsc[o] = scl;
-          P.hrs[o] = sum;
-        }
-        uint16_t* dst = P.h16p + (size_t)row * Ih + n0 + 32 * half;
-#pragma unroll
-        for (int cch = 0; cch < 4; ++cch) {
-          uint16_t v[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            float val = h[8 * cch + k];
-            if (EPI == kEpiSwigluQ8)
-              val = __fadd_rn(fminf(fmaxf(__fadd_rn(rintf(__fmul_rn(val, inv)), 128.0f), 0.0f), 255.0f),
-                              -128.0f);
-            v[p8(k)] = __half_as_ushort(__float2half_rn(val));
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(bar(B_BE + sb));
+            if (qend) mbar_arrive(bar(B_QE + sq));
           }
-          uint4 pk;
-          pk.x = v[0] | ((uint32_t)v[1] << 16);
-          pk.y = v[2] | ((uint32_t)v[3] << 16);
-          pk.z = v[4] | ((uint32_t)v[5] << 16);
-          pk.w = v[6] | ((uint32_t)v[7] << 16);
-          reinterpret_cast<uint4*>(dst)[cch] = pk;
         }
-        if (P.hbf) {
+        ++gb;
+        if (qend) ++gq;
+        if (I8) ++gt;
+      }
+      if (!I8) {   // STOCK: the whole K sum is in this item's TMEM buffer
+        const int b = gt & 1;
+        if (ok) ok = mbar_wait(bar(B_TF + b), (gt >> 1) & 1, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t ta = tmem + lane_addr + (uint32_t)(b * BN + 64 * half);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) P.hbf[(size_t)row * Ih + n0 + 32 * half + j] = f2bf(h[j]);
+          for (int hh = 0; hh < 2; ++hh) {
+            float d[32];
+            tmem_ld16(ta + 32 * hh, d);
+            tmem_ld16(ta + 32 * hh + 16, d + 16);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              acc2[16 * hh + c] = make_float2(__fadd_rn(d[2 * c], acc2[16 * hh + c].x),
+                                              __fadd_rn(d[2 * c + 1], acc2[16 * hh + c].y));
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_TE + b));
+        }
+        ++gt;
+      }
+      const int row = row0 + lr;
+      const bool live = ok && row < rowend;
+      if constexpr (EPI == kEpiStore) {
+        if (live) {
+          const int orow = P.y_rows ? P.y_rows[row] : row;
+          uint16_t* yrow = P.y_ptr ? P.y_ptr[orow] : P.Y + (size_t)orow * P.N;
+          uint4* dst = reinterpret_cast<uint4*>(yrow + n0 + 64 * half);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            uint4 pk;
+            pk.x = (uint32_t)f2bf(acc(8 * v + 0)) | ((uint32_t)f2bf(acc(8 * v + 1)) << 16);
+            pk.y = (uint32_t)f2bf(acc(8 * v + 2)) | ((uint32_t)f2bf(acc(8 * v + 3)) << 16);
+            pk.z = (uint32_t)f2bf(acc(8 * v + 4)) | ((uint32_t)f2bf(acc(8 * v + 5)) << 16);
+            pk.w = (uint32_t)f2bf(acc(8 * v + 6)) | ((uint32_t)f2bf(acc(8 * v + 7)) << 16);
+            dst[v] = pk;
+          }
+          // stores into other GPUs' memory (the expert-parallel return) are
+          // performed at system scope before this kernel ends, ahead of the
+          // flag the next launch posts
+          if (P.y_ptr) __threadfence_system();
+        }
+      } else {
+        // SwiGLU of the 32 (gate, up) pairs this thread holds; h columns
+        // n0 + 32*half + j.  The 64-column quantisation group spans the two
+        // halves: pair sums and amax are exchanged through shared memory.
+        float h[32];
+        float am = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          h[j] = swiglu_bf16(bfround(acc(j)), bfround(acc(32 + j)));
+          am = fmaxf(am, fabsf(h[j]));
+        }
+#pragma unroll
+        for (int l = 0; l < 16; ++l) xch[lr * 36 + 16 * half + l] = __fadd_rn(h[2 * l], h[2 * l + 1]);
+        xch[lr * 36 + 32 + half] = am;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        const float amax = fmaxf(xch[lr * 36 + 32], xch[lr * 36 + 33]);
+        const float sum = serial_butterfly32(xch + lr * 36, 1);
+        asm volatile("bar.sync 1, 256;" ::: "memory");   // xch is rewritten by the next item
+        const float scl = __fdiv_rn(fmaxf(amax, 1e-30f), 127.0f);
+        const float inv = __fdiv_rn(1.0f, scl);
+        if (live) {
+          const size_t o = (size_t)row * P.h_srow + nb;   // row-major, padded stride
+          if (half == 0) {
+            if (EPI == kEpiSwigluQ8) P.hsc[o] = scl;
+            P.hrs[o] = sum;
+          }
+          uint16_t* dst = P.h16p + (size_t)row * Ih + n0 + 32 * half;
+#pragma unroll
+          for (int cch = 0; cch < 4; ++cch) {
+            uint16_t v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              float val = h[8 * cch + k];
+              if (EPI == kEpiSwigluQ8)
+                val = __fadd_rn(
+                    fminf(fmaxf(__fadd_rn(rintf(__fmul_rn(val, inv)), 128.0f), 0.0f), 255.0f),
+                    -128.0f);
+              v[p8(k)] = __half_as_ushort(__float2half_rn(val));
+            }
+            uint4 pk;
+            pk.x = v[0] | ((uint32_t)v[1] << 16);
+            pk.y = v[2] | ((uint32_t)v[3] << 16);
+            pk.z = v[4] | ((uint32_t)v[5] << 16);
+            pk.w = v[6] | ((uint32_t)v[7] << 16);
+            reinterpret_cast<uint4*>(dst)[cch] = pk;
+          }
+          if (P.hbf) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) P.hbf[(size_t)row * Ih + n0 + 32 * half + j] = f2bf(h[j]);
+          }
         }
       }
     }
@@ -535,8 +583,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       __syncwarp();
     }
     tc_fence_after();
-    const uint32_t ncols = I8 ? 2 * BN : BN;
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
   }
 }
 
@@ -544,8 +591,11 @@ template <bool I8, int EPI>
 static cudaError_t launch_tc05_one(const GemmParams& P, const Tc05Maps& M, int maxt, cudaStream_t s) {
   cudaError_t err = ensure_smem_attr((const void*)gemm_tc05_kernel<I8, EPI>, SMEM);
   if (err != cudaSuccess) return err;
-  const int gx = (EPI == kEpiStore) ? P.N / BN : (P.N / 2) / 64;
-  gemm_tc05_kernel<I8, EPI><<<dim3(gx, maxt), NTHREADS, SMEM, s>>>(P, M);
+  // persistent: one CTA per SM walks (row tile, column block) items
+  const long long items = (long long)maxt * ((EPI == kEpiStore) ? P.N / BN : (P.N / 2) / 64);
+  const int sms = device_sm_count();
+  const int grid = (int)(items < sms ? items : sms);
+  gemm_tc05_kernel<I8, EPI><<<grid, NTHREADS, SMEM, s>>>(P, M);
   return cudaGetLastError();
 }
 
