@@ -72,7 +72,7 @@ static_assert(A_OFF % 1024 == 0 && B_OFF % 1024 == 0 && Q_OFF % 1024 == 0 && Q_B
               "TMA / UMMA tiles 1024-byte aligned, other TMA destinations 128-byte aligned");
 static_assert(SMEM <= 232448, "shared memory per CTA");
 constexpr int NTHREADS = 512;
-constexpr int NCONV = 192;                        // converter warps 2-7
+constexpr int NCONV = 128;                        // converter warps 4-7 (one per SM sub-partition)
 // barrier indices (uint64 each) at BAR_OFF
 constexpr int B_AF = 0, B_AE = B_AF + NA, B_BF = B_AE + NA, B_BE = B_BF + NB, B_QF = B_BE + NB,
               B_QE = B_QF + NQ, B_TF = B_QE + NQ, B_TE = B_TF + 2, B_TBF = B_TE + 2,
@@ -273,16 +273,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp < 8) {
+  } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------- converters
-    // Widen each group's packed rows into the fp16 B operand (128B-swizzled
-    // K-major) and write the group's fp32 column scalars.  Work item
-    // i = (tile row i / 8, word i % 8): a warp covers 4 rows x 8 words per
-    // step; the swizzled packed stage and the B tile are read / written
-    // without bank conflicts.  The items of a thread are loaded before any is
-    // widened.
-    const int ct = tid - 64;
-    constexpr int NIT = (BN * 8 + NCONV - 1) / NCONV;
+    // Thread ct widens B-tile row ct of each group: its 8 packed words (two
+    // 16-byte loads from the swizzled packed stage), one scale, eight fp16
+    // chunks into the 128B-swizzled K-major B tile — conflict-free on both
+    // sides (8 consecutive rows touch 8 different 16-byte slots) — and the
+    // fp32 scalars of column ct.  Warps 2-3 stay idle.
+    const int ct = tid - 128;
     int gb = 0, gq = 0, it = 0;
     bool ok = true;
     // Every converter thread reaches the same named barriers in the same
@@ -304,8 +302,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // scale of the item is 0 or inside [2^-14, 2^12): then the MMA returns
       // D * s exactly (|D| <= 2^16, so D * s needs at most 24 bits).
       bool safe = true;
-      for (int i = ct; i < G * BN; i += NCONV) {
-        const uint32_t bv = tab(0, i >> 7, i & 127);
+      for (int g = 0; g < G; ++g) {
+        const uint32_t bv = tab(0, g, ct);
         const uint32_t ex = (bv >> 7) & 0xffu;
         safe = safe && (((bv & 0x7fffu) == 0u) || (ex >= 113u && ex <= 138u));
       }
@@ -317,42 +315,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // no such limit.
       if (!I8 && !prescale && ct == 0) atomicExch(&g_tc05_error, 2);
       const bool scale_b = !I8 || prescale;
+      const int r = ct, r7 = r & 7;
+      const uint32_t qrow = (r >> 5) * 4096 + (r & 31) * 128;   // row in the packed stage
       for (int g = 0; g < G; ++g) {
-        const int sq = gq % NQ, sb = gb % NB;
+        const int sq = gq % NQ, sb = gb % NB, gg = g & 3;
         if (!(ok = mbar_wait(bar(B_QF + sq), (gq / NQ) & 1, abort_flag))) break;
         if (!(ok = mbar_wait(bar(B_BE + sb), ((gb / NB) & 1) ^ 1, abort_flag))) break;
-        const uint8_t* qs = smem + Q_OFF + sq * Q_BYTES;
-        uint8_t* sB = smem + B_OFF + sb * B_BYTES;
-        const int gg = g & 3;
-        uint32_t wv[NIT];
-        __half sh[NIT];
+        const uint8_t* qs = smem + Q_OFF + sq * Q_BYTES + qrow;
+        uint8_t* sB = smem + B_OFF + sb * B_BYTES + r * 128;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(qs + (((2 * gg) ^ r7) << 4));
+        const uint4 w1 = *reinterpret_cast<const uint4*>(qs + (((2 * gg + 1) ^ r7) << 4));
+        const uint16_t sbits = tab(0, g, r);
+        const __half sh = __float2half_rn(bf2f(sbits));
+        const __half2 s2 = __halves2half2(sh, sh);
+        const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int k = 0; k < NIT; ++k) {
-          const int i = ct + k * NCONV;
-          if (i < BN * 8) {
-            const int r = i >> 3, c = i & 7;
-            wv[k] = *reinterpret_cast<const uint32_t*>(
-                qs + (r >> 5) * 4096 + (r & 31) * 128 + (((2 * gg + (c >> 2)) ^ (r & 7)) << 4) +
-                (c & 3) * 4);
-            sh[k] = __float2half_rn(bf2f(tab(0, g, r)));
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < NIT; ++k) {
-          const int i = ct + k * NCONV;
-          if (i < BN * 8) {
-            const int r = i >> 3, c = i & 7;
-            *reinterpret_cast<uint4*>(sB + r * 128 + ((c ^ (r & 7)) << 4)) =
-                widen8(wv[k], scale_b, __halves2half2(sh[k], sh[k]));
-          }
-        }
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(sB + ((c ^ r7) << 4)) = widen8(wv[c], scale_b, s2);
         // column scalars: s and the folded bias b + 8s
-        if (ct < BN) {
-          const float sv = bf2f(tab(0, g, ct));
-          const float bb = __fadd_rn(bf2f(tab(1, g, ct)), __fmul_rn(8.0f, sv));
+        {
+          const float sv = bf2f(sbits);
+          const float bb = __fadd_rn(bf2f(tab(1, g, r)), __fmul_rn(8.0f, sv));
           float* cs = reinterpret_cast<float*>(smem + CS_OFF + sb * CS_BYTES);
-          cs[ct] = sv;
-          cs[BN + ct] = I8 ? bfround(bb) : bb;
+          cs[r] = sv;
+          cs[BN + r] = I8 ? bfround(bb) : bb;
         }
         // each writer makes its stores visible to the async proxy; one
         // arrival per warp
@@ -367,7 +353,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (gg == 3 || g == G - 1) ++gq;
       }
     }
-  } else {
+  } else if (warp >= 8) {
     // ---------------------------------------------------------------- epilogue
     // Every epilogue warp walks every item (after a failed wait it skips the
     // waits and stores nothing), so the named barriers of the SwiGLU tail are
