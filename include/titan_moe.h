@@ -333,8 +333,9 @@ int tmoe_moe_local(const tmoe_layer* layer, const uint16_t* x, int T, const tmoe
                    uint16_t* shared_out, void* stream);
 
 /* Source side: the block's top-k weighted sum (moe_weighted_sum.py:142-195;
- * mode 0 clone, 1 fast) of every token's k expert outputs ys[inv[t*k+j]] plus
- * the sigmoid-gated shared expert (language.py:85-91; shared_out [T, D] bf16
+ * mode 0 clone, 1 fast) of every token's k expert outputs ys[inv[t*k+j]]
+ * (inv NULL: ys[t*k+j], rows already token-major) plus the sigmoid-gated
+ * shared expert (language.py:85-91; shared_out [T, D] bf16
  * and gate_logit [T] fp32, both NULL when there is none).  y [T, D] bf16. */
 int tmoe_moe_combine(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
                      int D, int mode, const uint16_t* shared_out, const float* gate_logit,

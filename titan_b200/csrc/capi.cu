@@ -1763,7 +1763,7 @@ int tmoe_ep_guard(const int32_t* counts, int world, uint16_t* y, int64_t n, void
 int tmoe_moe_combine(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
                      int D, int mode, const uint16_t* shared_out, const float* gate_logit,
                      uint16_t* y, void* stream) {
-  if (!ys || !inv || !scores || !y || T < 0 || k <= 0 || (mode != 0 && mode != 1) ||
+  if (!ys || !scores || !y || T < 0 || k <= 0 || (mode != 0 && mode != 1) ||
       (!shared_out) != (!gate_logit))
     return fail(TMOE_ERR_INVALID, "tmoe_moe_combine: bad arguments");
   if (D <= 0 || D % 8) return fail(TMOE_ERR_UNSUPPORTED, "tmoe_moe_combine: need D %% 8 == 0");

@@ -76,6 +76,58 @@ TMOE_DEV float swiglu_bf16(float g, float u) {
   return bfround(__fmul_rn(a, u));
 }
 
+// Two lanes of cexp at once, bit-identical per component: rint(x * log2e)
+// as (t + 1.5*2^23) - 1.5*2^23 (exact round-to-nearest-even for |t| < 2^22),
+// the integer n read from the same sum's bits, the reduction and polynomial
+// as packed f32x2 FMAs, the special cases selected afterwards.
+TMOE_DEV float2 cexp2(float2 x) {
+  const float2 t = __fmul2_rn(x, make_float2(1.44269504088896341f, 1.44269504088896341f));
+  const float2 big = __fadd2_rn(t, make_float2(12582912.0f, 12582912.0f));
+  const float2 n = __fadd2_rn(big, make_float2(-12582912.0f, -12582912.0f));
+  const float2 mn = make_float2(-n.x, -n.y);
+  float2 r = __ffma2_rn(mn, make_float2(0.693145751953125f, 0.693145751953125f), x);
+  r = __ffma2_rn(mn, make_float2(1.42860682030941723e-06f, 1.42860682030941723e-06f), r);
+  auto k2 = [](float c) { return make_float2(c, c); };
+  float2 p = k2(1.98412698412698413e-4f);
+  p = __ffma2_rn(p, r, k2(1.38888888888888889e-3f));
+  p = __ffma2_rn(p, r, k2(8.33333333333333333e-3f));
+  p = __ffma2_rn(p, r, k2(4.16666666666666667e-2f));
+  p = __ffma2_rn(p, r, k2(1.66666666666666667e-1f));
+  p = __ffma2_rn(p, r, k2(0.5f));
+  p = __ffma2_rn(p, r, k2(1.0f));
+  p = __ffma2_rn(p, r, k2(1.0f));
+  const int nx = (int)n.x, ny = (int)n.y;
+  const int n1x = nx / 2, n1y = ny / 2;
+  auto p2 = [](int k) { return __uint_as_float((uint32_t)(k + 127) << 23); };   // 2^k
+  // the 2^n scaling stays scalar (two multiplies per lane)
+  const float2 v = make_float2(__fmul_rn(__fmul_rn(p.x, p2(n1x)), p2(nx - n1x)),
+                               __fmul_rn(__fmul_rn(p.y, p2(n1y)), p2(ny - n1y)));
+  auto fix = [](float xi, float vi) {
+    if (xi != xi) return xi;
+    if (xi > 88.7228393554688f) return __int_as_float(0x7f800000);
+    if (xi < -103.972084045410f) return 0.0f;
+    return vi;
+  };
+  return make_float2(fix(x.x, v.x), fix(x.y, v.y));
+}
+
+// Two bf16 roundings in one conversion (round to nearest even, as f2bf).
+TMOE_DEV float2 bfround2(float2 v) {
+  const __nv_bfloat162 b = __float22bfloat162_rn(v);
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&b);
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
+// swiglu_bf16 on two lanes, bit-identical per component: the reciprocal is
+// the correctly rounded 1 / y, as __fdiv_rn(1, y) is.
+TMOE_DEV float2 swiglu_bf16x2(float2 g, float2 u) {
+  const float2 e = cexp2(make_float2(-g.x, -g.y));
+  const float2 y = __fadd2_rn(make_float2(1.0f, 1.0f), e);
+  const float2 sg = bfround2(make_float2(__frcp_rn(y.x), __frcp_rn(y.y)));
+  const float2 a = bfround2(__fmul2_rn(g, sg));
+  return bfround2(__fmul2_rn(a, u));
+}
+
 // fp32 SiLU(g)*u of the decode path (decode-fusion semantics).
 TMOE_DEV float silu_mul_f32(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, cexp(-g))), u);

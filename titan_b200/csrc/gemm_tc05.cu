@@ -51,6 +51,8 @@ constexpr int BM = 128, BN = 128;
 constexpr int NA = 3;                             // activation tiles (one group each)
 constexpr int NB = 3;                             // widened weight tiles (one group each)
 constexpr int NQ = 2;                             // packed stages (4 groups each)
+constexpr int ND = 4;                             // TMEM accumulator buffers (128 columns each)
+constexpr int NCS = 8;                            // column-scalar slots (one group each)
 constexpr int kMaxG = 48;                         // K <= 3072: scale / bias tables held whole
 constexpr int A_BYTES = BM * 128;                 // 128 rows x 64 fp16, 128B-swizzled
 constexpr int B_BYTES = BN * 128;
@@ -62,7 +64,7 @@ constexpr int A_OFF = 0;
 constexpr int B_OFF = A_OFF + NA * A_BYTES;
 constexpr int Q_OFF = B_OFF + NB * B_BYTES;
 constexpr int CS_OFF = Q_OFF + NQ * Q_BYTES;
-constexpr int TB_OFF = CS_OFF + NB * CS_BYTES;    // 2 x 8 table boxes [G][32] bf16 (s x 4, b x 4)
+constexpr int TB_OFF = CS_OFF + NCS * CS_BYTES;    // 2 x 8 table boxes [G][32] bf16 (s x 4, b x 4)
 constexpr int TB_BYTES = 8 * 64 * kMaxG;          // one work item's tables
 constexpr int XCH_OFF = TB_OFF + 2 * TB_BYTES;
 constexpr int BAR_OFF = XCH_OFF + BM * 36 * 4;
@@ -75,7 +77,8 @@ constexpr int NTHREADS = 512;
 constexpr int NCONV = 128;                        // converter warps 4-7 (one per SM sub-partition)
 // barrier indices (uint64 each) at BAR_OFF
 constexpr int B_AF = 0, B_AE = B_AF + NA, B_BF = B_AE + NA, B_BE = B_BF + NB, B_QF = B_BE + NB,
-              B_QE = B_QF + NQ, B_TF = B_QE + NQ, B_TE = B_TF + 2, B_TBF = B_TE + 2,
+              B_QE = B_QF + NQ, B_CSF = B_QE + NQ, B_CSE = B_CSF + NCS, B_TF = B_CSE + NCS,
+              B_TE = B_TF + ND, B_TBF = B_TE + ND,
               B_TBE = B_TBF + 2, B_DRAIN = B_TBE + 2, B_SLOT = B_DRAIN + 1,
               B_ABORT = B_SLOT + 1, B_PRESCALE = B_ABORT + 1;   // 4 prescale flags (ints)
 static_assert((B_PRESCALE + 2) * 8 <= 512, "barrier area");
@@ -143,15 +146,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int i = 0; i < NB; ++i) {
       mbar_init(bar(B_BF + i), NCONV / 32); // one arrival per converter warp
-      mbar_init(bar(B_BE + i), 9);          // MMA commit + the 8 epilogue warps
+      mbar_init(bar(B_BE + i), 1);          // MMA commit
+    }
+    for (int i = 0; i < NCS; ++i) {
+      mbar_init(bar(B_CSF + i), NCONV / 32);  // converters wrote the group's column scalars
+      mbar_init(bar(B_CSE + i), 8);           // the 8 epilogue warps read them
+    }
+    for (int i = 0; i < ND; ++i) {
+      mbar_init(bar(B_TF + i), 1);
+      mbar_init(bar(B_TE + i), 8);
     }
     for (int i = 0; i < NQ; ++i) {
       mbar_init(bar(B_QF + i), 1);
       mbar_init(bar(B_QE + i), NCONV / 32 + 8);   // converters (packed rows), epilogue (row scalars)
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(B_TF + b), 1);
-      mbar_init(bar(B_TE + b), 8);
       mbar_init(bar(B_TBF + b), 1);
       mbar_init(bar(B_TBE + b), NCONV / 32);
     }
@@ -163,7 +172,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)), "r"(2 * BN));
+                     smem_u32(tmem_slot)), "r"(ND * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -242,17 +251,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool ok = true;
       for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
         if (!I8) {   // STOCK: one accumulator buffer per item
-          if (!(ok = mbar_wait(bar(B_TE + (gt & 1)), ((gt >> 1) & 1) ^ 1, abort_flag))) break;
+          if (!(ok = mbar_wait(bar(B_TE + gt % ND), ((gt / ND) & 1) ^ 1, abort_flag))) break;
         }
         for (int g = 0; g < G; ++g) {
           const int sa = ga % NA, sb = gb % NB;
           if (!(ok = mbar_wait(bar(B_AF + sa), (ga / NA) & 1, abort_flag))) break;
           if (!(ok = mbar_wait(bar(B_BF + sb), (gb / NB) & 1, abort_flag))) break;
-          if (I8 && !(ok = mbar_wait(bar(B_TE + (gt & 1)), ((gt >> 1) & 1) ^ 1, abort_flag))) break;
+          if (I8 && !(ok = mbar_wait(bar(B_TE + gt % ND), ((gt / ND) & 1) ^ 1, abort_flag))) break;
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + A_OFF + sa * A_BYTES);
           const uint32_t b_base = smem_u32(smem + B_OFF + sb * B_BYTES);
-          const uint32_t d = tmem + (uint32_t)((gt & 1) * BN);
+          const uint32_t d = tmem + (uint32_t)((gt % ND) * BN);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             mma_f16(d, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32),
@@ -262,12 +271,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           ++ga;
           ++gb;
           if (I8) {
-            mma_commit(bar(B_TF + (gt & 1)));
+            mma_commit(bar(B_TF + gt % ND));
             ++gt;
           }
         }
         if (!I8 && ok) {
-          mma_commit(bar(B_TF + (gt & 1)));
+          mma_commit(bar(B_TF + gt % ND));
           ++gt;
         }
       }
@@ -321,6 +330,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int sq = gq % NQ, sb = gb % NB, gg = g & 3;
         if (!(ok = mbar_wait(bar(B_QF + sq), (gq / NQ) & 1, abort_flag))) break;
         if (!(ok = mbar_wait(bar(B_BE + sb), ((gb / NB) & 1) ^ 1, abort_flag))) break;
+        const int sc = gb % NCS;
+        if (!(ok = mbar_wait(bar(B_CSE + sc), ((gb / NCS) & 1) ^ 1, abort_flag))) break;
         const uint8_t* qs = smem + Q_OFF + sq * Q_BYTES + qrow;
         uint8_t* sB = smem + B_OFF + sb * B_BYTES + r * 128;
         const uint4 w0 = *reinterpret_cast<const uint4*>(qs + (((2 * gg) ^ r7) << 4));
@@ -336,7 +347,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         {
           const float sv = bf2f(sbits);
           const float bb = __fadd_rn(bf2f(tab(1, g, r)), __fmul_rn(8.0f, sv));
-          float* cs = reinterpret_cast<float*>(smem + CS_OFF + sb * CS_BYTES);
+          float* cs = reinterpret_cast<float*>(smem + CS_OFF + sc * CS_BYTES);
           cs[r] = sv;
           cs[BN + r] = I8 ? bfround(bb) : bb;
         }
@@ -346,6 +357,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(bar(B_BF + sb));
+          mbar_arrive(bar(B_CSF + sc));
           if (gg == 3 || g == G - 1) mbar_arrive(bar(B_QE + sq));
           if (g == G - 1) mbar_arrive(bar(B_TBE + tb));   // this item's tables consumed
         }
@@ -376,23 +388,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       auto acc = [&](int c) -> float { return (c & 1) ? acc2[c >> 1].y : acc2[c >> 1].x; };
       bool prescaled = false;
       for (int g = 0; g < G; ++g) {
-        const int sq = gq % NQ, sb = gb % NB, gg = g & 3;
+        const int sq = gq % NQ, sc = gb % NCS, gg = g & 3;
         const bool qend = gg == 3 || g == G - 1;
         // row scalars of the packed stage (TMA), column scalars of the group
         // (converters)
         if (ok) ok = mbar_wait(bar(B_QF + sq), (gq / NQ) & 1, abort_flag) &&
-                     mbar_wait(bar(B_BF + sb), (gb / NB) & 1, abort_flag);
+                     mbar_wait(bar(B_CSF + sc), (gb / NCS) & 1, abort_flag);
         if (ok) {
           if (g == 0) prescaled = reinterpret_cast<volatile int*>(prescale_flag)[it & 3] != 0;
           const float* qsc = reinterpret_cast<const float*>(smem + Q_OFF + sq * Q_BYTES + QW_BYTES);
           const float xs = I8 ? qsc[lr * 4 + gg] : 0.0f;
           const float xr = qsc[BM * 4 + lr * 4 + gg];
-          const float* csb = reinterpret_cast<const float*>(smem + CS_OFF + sb * CS_BYTES);
+          const float* csb = reinterpret_cast<const float*>(smem + CS_OFF + sc * CS_BYTES);
           const float* cs = csb + 64 * half;
           const float* cb = csb + BN + 64 * half;
           if (I8) {
-            const int b = gt & 1;
-            ok = mbar_wait(bar(B_TF + b), (gt >> 1) & 1, abort_flag);
+            const int b = gt % ND;
+            ok = mbar_wait(bar(B_TF + b), (gt / ND) & 1, abort_flag);
             if (ok) {
               tc_fence_after();
               const uint32_t ta = tmem + lane_addr + (uint32_t)(b * BN + 64 * half);
@@ -450,7 +462,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           __syncwarp();
           if (lane == 0) {
-            mbar_arrive(bar(B_BE + sb));
+            mbar_arrive(bar(B_CSE + sc));
             if (qend) mbar_arrive(bar(B_QE + sq));
           }
         }
@@ -459,8 +471,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (I8) ++gt;
       }
       if (!I8) {   // STOCK: the whole K sum is in this item's TMEM buffer
-        const int b = gt & 1;
-        if (ok) ok = mbar_wait(bar(B_TF + b), (gt >> 1) & 1, abort_flag);
+        const int b = gt % ND;
+        if (ok) ok = mbar_wait(bar(B_TF + b), (gt / ND) & 1, abort_flag);
         if (ok) {
           tc_fence_after();
           const uint32_t ta = tmem + lane_addr + (uint32_t)(b * BN + 64 * half);
@@ -497,10 +509,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             pk.w = (uint32_t)f2bf(acc(8 * v + 6)) | ((uint32_t)f2bf(acc(8 * v + 7)) << 16);
             dst[v] = pk;
           }
-          // stores into other GPUs' memory (the expert-parallel return) are
-          // performed at system scope before this kernel ends, ahead of the
-          // flag the next launch posts
-          if (P.y_ptr) __threadfence_system();
         }
       } else {
         // SwiGLU of the 32 (gate, up) pairs this thread holds; h columns
@@ -509,9 +517,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float h[32];
         float am = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          h[j] = swiglu_bf16(bfround(acc(j)), bfround(acc(32 + j)));
-          am = fmaxf(am, fabsf(h[j]));
+        for (int j = 0; j < 32; j += 2) {
+          const float2 hv = swiglu_bf16x2(bfround2(acc2[j >> 1]), bfround2(acc2[16 + (j >> 1)]));
+          h[j] = hv.x;
+          h[j + 1] = hv.y;
+          am = fmaxf(am, fmaxf(fabsf(hv.x), fabsf(hv.y)));
         }
 #pragma unroll
         for (int l = 0; l < 16; ++l) xch[lr * 36 + 16 * half + l] = __fadd_rn(h[2 * l], h[2 * l + 1]);
@@ -557,6 +567,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   }
 
+  // stores into other GPUs' memory (the expert-parallel return) are performed
+  // at system scope before this kernel ends, ahead of the flag the next
+  // launch posts: one fence per storing thread, after its last item
+  if (EPI == kEpiStore && P.y_ptr && warp >= 8) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -569,7 +583,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       __syncwarp();
     }
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ND * BN));
   }
 }
 
@@ -624,15 +638,16 @@ cudaError_t launch_gemm_tc05(bool int8, int epi, const GemmParams& P, int maxt, 
   return launch_tc05_one<false, kEpiSwigluH16>(P, M, maxt, s);
 }
 
-// Operand prep for the tcgen05 GEMMs: one warp per output row, lane l owns
-// the 64-groups l, l + 32, ...  QUANT: the int8 codes xu - 128 as fp16 plus
-// the per-group scale and exact sum; otherwise x itself in fp16 plus the sum.
-// Elements are stored in the (0,4,1,5,2,6,3,7) order of every 8-chunk.
-// Output row m reads x row m, or (gathered, expert-sorted) x row
-// a_map[a_rows[m]] / a_rows[m] / a_div; its scalars sit at m * srow + g.
+// Operand prep for the tcgen05 GEMMs: one warp per output row, four 64-groups
+// per step; lane l handles the 8-element chunk l % 8 of group l / 8, so every
+// load and store of the warp is 512 contiguous bytes.  QUANT: the int8 codes
+// xu - 128 as fp16 plus the per-group scale and exact sum; otherwise x itself
+// in fp16 plus the sum.  Elements are stored in the (0,4,1,5,2,6,3,7) order of
+// every 8-chunk.  Output row m reads x row m, or (gathered, expert-sorted) x
+// row a_map[a_rows[m]] / a_rows[m] / a_div; its scalars sit at m * srow + g.
 // The group sum is the pair sums (2j, 2j+1) reduced by the xor tree
-// 16, 8, 4, 2, 1 — the order of a butterfly over 32 lanes holding one pair
-// each — so every prep and the CPU oracle agree bit for bit.
+// 16, 8, 4, 2, 1 (p[j] += p[j + off] for j < off) — the order of a butterfly
+// over 32 lanes holding one pair each — evaluated across the group's 8 lanes.
 template <bool QUANT>
 __global__ void __launch_bounds__(256) prep_a16_kernel(const uint16_t* __restrict__ x, int R, int K,
                                                         const int32_t* __restrict__ a_rows,
@@ -646,53 +661,61 @@ __global__ void __launch_bounds__(256) prep_a16_kernel(const uint16_t* __restric
   if (m >= R) return;
   const int G = K / kGroup;
   const int src = !a_rows ? (int)m : (a_map ? a_map[a_rows[m]] : a_rows[m] / a_div);
-  for (int g = lane; g < G; g += 32) {
-    const uint4* xp = reinterpret_cast<const uint4*>(x + (size_t)src * K + g * kGroup);
-    uint4 raw[8];
+  const int sub = lane >> 3, c = lane & 7;
+  for (int g0 = 0; g0 < G; g0 += 4) {
+    const int g = g0 + sub;
+    const bool act = g < G;
+    float v[8];
+    if (act) {
+      unpack8_bf16(__ldg(reinterpret_cast<const uint4*>(x + (size_t)src * K + g * kGroup + c * 8)),
+                   v);
+    } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) raw[i] = __ldg(xp + i);
-    float v[64];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) unpack8_bf16(raw[i], v + 8 * i);
-    float p[32];
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    float p[4];
     float am = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      p[j] = __fadd_rn(v[2 * j], v[2 * j + 1]);
-      am = fmaxf(am, fmaxf(fabsf(v[2 * j]), fabsf(v[2 * j + 1])));
+    for (int i = 0; i < 4; ++i) {
+      p[i] = __fadd_rn(v[2 * i], v[2 * i + 1]);
+      am = fmaxf(am, fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1])));
     }
+    // pairs j = 4c + i: off 16, 8, 4 cross lanes (c + 4, c + 2, c + 1), off 2, 1 stay in lane 0
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1)
+    for (int i = 0; i < 4; ++i) p[i] = __fadd_rn(p[i], __shfl_down_sync(0xffffffffu, p[i], 4, 8));
 #pragma unroll
-      for (int j = 0; j < off; ++j) p[j] = __fadd_rn(p[j], p[j + off]);
-    const float sum = p[0];
+    for (int i = 0; i < 4; ++i) p[i] = __fadd_rn(p[i], __shfl_down_sync(0xffffffffu, p[i], 2, 8));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = __fadd_rn(p[i], __shfl_down_sync(0xffffffffu, p[i], 1, 8));
+    p[0] = __fadd_rn(p[0], p[2]);
+    p[1] = __fadd_rn(p[1], p[3]);
+    const float sum = __fadd_rn(p[0], p[1]);          // meaningful in lane c == 0
+#pragma unroll
+    for (int off = 4; off >= 1; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off, 8));
+    if (!act) continue;
     if (!QUANT) {
       // x itself becomes the fp16 operand: it overflows past 65504, and a
       // group lying wholly below fp16's normal range keeps too few bits
-      if (am >= 65504.0f || (am > 0.0f && am < 6.103515625e-05f)) atomicExch(&g_tc05_error, 2);
+      if (c == 0 && (am >= 65504.0f || (am > 0.0f && am < 6.103515625e-05f)))
+        atomicExch(&g_tc05_error, 2);
     }
     if (QUANT) {
       const float sc = __fdiv_rn(fmaxf(am, 1e-30f), 127.0f);
       const float inv = __fdiv_rn(1.0f, sc);
 #pragma unroll
-      for (int k = 0; k < 64; ++k)
+      for (int k = 0; k < 8; ++k)
         v[k] = __fadd_rn(fminf(fmaxf(__fadd_rn(rintf(__fmul_rn(v[k], inv)), 128.0f), 0.0f), 255.0f),
                          -128.0f);
-      xsc[(size_t)m * srow + g] = sc;
+      if (c == 0) xsc[(size_t)m * srow + g] = sc;
     }
-    xrs[(size_t)m * srow + g] = sum;
-    uint4* dst = reinterpret_cast<uint4*>(a16 + (size_t)m * K + g * kGroup);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const float* e = v + 8 * c;   // stored order 0,4,1,5,2,6,3,7
-      auto h = [](float f) { return (uint32_t)__half_as_ushort(__float2half_rn(f)); };
-      uint4 pk;
-      pk.x = h(e[0]) | (h(e[4]) << 16);
-      pk.y = h(e[1]) | (h(e[5]) << 16);
-      pk.z = h(e[2]) | (h(e[6]) << 16);
-      pk.w = h(e[3]) | (h(e[7]) << 16);
-      dst[c] = pk;
-    }
+    if (c == 0) xrs[(size_t)m * srow + g] = sum;
+    auto h = [](float f) { return (uint32_t)__half_as_ushort(__float2half_rn(f)); };
+    uint4 pk;                                        // stored order 0,4,1,5,2,6,3,7
+    pk.x = h(v[0]) | (h(v[4]) << 16);
+    pk.y = h(v[1]) | (h(v[5]) << 16);
+    pk.z = h(v[2]) | (h(v[6]) << 16);
+    pk.w = h(v[3]) | (h(v[7]) << 16);
+    *reinterpret_cast<uint4*>(a16 + (size_t)m * K + g * kGroup + c * 8) = pk;
   }
 }
 

@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(256) wsum_kernel(const uint16_t* __restrict__ 
 // step to bf16), then the eight slots combine in order — the bits of
 // wsum_kernel.
 template <int KMAX>
-__global__ void __launch_bounds__(256) wsum_prefetch_kernel(const uint16_t* __restrict__ ys,
+__global__ void __launch_bounds__(128) wsum_prefetch_kernel(const uint16_t* __restrict__ ys,
                                                             const int32_t* __restrict__ inv,
                                                             const uint16_t* __restrict__ scores,
                                                             int T, int k, int D, int mode,
@@ -106,7 +106,11 @@ __global__ void __launch_bounds__(256) wsum_prefetch_kernel(const uint16_t* __re
   for (int j = 0; j < KMAX; ++j)
     if (j < k) raw[j] = __ldg(reinterpret_cast<const uint4*>(ys + (size_t)src[j] * D + d0));
   float sg = 0.0f;
-  if (sh) sg = bfround(csigmoid(bfround(gate_logit[t])));
+  float shv8[8];
+  if (sh) {
+    sg = bfround(csigmoid(bfround(gate_logit[t])));
+    unpack8_bf16(__ldg(reinterpret_cast<const uint4*>(sh + (size_t)t * D + d0)), shv8);
+  }
   uint16_t o[8];
 #pragma unroll
   for (int v = 0; v < 8; ++v) {
@@ -133,10 +137,7 @@ __global__ void __launch_bounds__(256) wsum_prefetch_kernel(const uint16_t* __re
       if (mode == 0) a = bfround(a);
     }
     a = bfround(a);
-    if (sh) {
-      const float shv = bfround(__fmul_rn(sg, bf2f(sh[(size_t)t * D + d0 + v])));
-      a = __fadd_rn(a, shv);
-    }
+    if (sh) a = __fadd_rn(a, bfround(__fmul_rn(sg, shv8[v])));
     o[v] = f2bf(a);
   }
   uint4 pk;
@@ -152,17 +153,17 @@ cudaError_t launch_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* 
                         cudaStream_t s) {
   const long long n = (long long)T * (D / 8);
   if (n <= 0) return cudaGetLastError();
-  const unsigned grid = (unsigned)((n + 255) / 256);
+  const unsigned grid = (unsigned)((n + 127) / 128), grid256 = (unsigned)((n + 255) / 256);
   if (k <= 8)
-    wsum_prefetch_kernel<8><<<grid, 256, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit, out);
+    wsum_prefetch_kernel<8><<<grid, 128, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit, out);
   else if (k <= 12)
-    wsum_prefetch_kernel<12><<<grid, 256, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit,
+    wsum_prefetch_kernel<12><<<grid, 128, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit,
                                                  out);
   else if (k <= 16)
-    wsum_prefetch_kernel<16><<<grid, 256, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit,
+    wsum_prefetch_kernel<16><<<grid, 128, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit,
                                                  out);
   else
-    wsum_kernel<<<grid, 256, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit, out);
+    wsum_kernel<<<grid256, 256, 0, s>>>(ys, inv, scores, T, k, D, mode, sh, gate_logit, out);
   return cudaGetLastError();
 }
 

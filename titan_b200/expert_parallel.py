@@ -377,7 +377,7 @@ def peer_forward(x: torch.Tensor, idx: torch.Tensor, ex: PeerExchange, experts_p
     _lib.check(lib.tmoe_ep_wait(ex.ptr, ex.offsets, 1, W, ep, ex.returned.data_ptr(), stream),
                "tmoe_ep_wait")
     _mark(marks, "wait")
-    y = combine_fn(ex.ret[:T * k], ex.arange(T * k))
+    y = combine_fn(ex.ret[:T * k], None)      # returned rows are token-major
     # a negative return count (an owner's or this rank's wait gave up): the
     # output becomes NaN and tmoe_device_status reports the timeout
     _lib.check(lib.tmoe_ep_guard(ex.returned.data_ptr(), W, y.data_ptr(), y.numel(), stream),
@@ -559,12 +559,14 @@ class ExpertParallelMoE(torch.nn.Module):
                    "tmoe_moe_experts_slots")
 
     def combine(self, ys, inv, scores, shared_out, gate_logit, mode: int = 0):
-        """The block's weighted sum plus gated shared expert (tmoe_moe_combine)."""
+        """The block's weighted sum plus gated shared expert (tmoe_moe_combine);
+        inv None: ys is already token-major."""
         T, k = scores.shape
         y = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=scores.device)
         if T == 0:
             return y
-        _lib.call("tmoe_moe_combine", ys.data_ptr(), inv.data_ptr(), scores.data_ptr(), T, k,
+        _lib.call("tmoe_moe_combine", ys.data_ptr(), None if inv is None else inv.data_ptr(),
+                  scores.data_ptr(), T, k,
                   self.hidden, mode, None if shared_out is None else shared_out.data_ptr(),
                   None if gate_logit is None else gate_logit.data_ptr(), y.data_ptr(),
                   ops.stream_ptr(scores.device))
