@@ -374,7 +374,7 @@ def prefill_ops_per_token(c):
 
 def bench_prefill(args, world, device):
     """The cold-prefill block (H=3072, 512 experts, I=768, top-10, shared
-    expert 3072) at each --prefill-T on the default tile-per-CTA kernel, and
+    expert 3072) at each --prefill-T on the default persistent tile kernel, and
     the swap-AB kernel at the first T: ms, tok/s, TOP/s and the fraction of
     the measured dense bf16 peak (the kernels issue f16 MMAs; the nominal
     int8 fraction is given for context)."""
@@ -410,7 +410,7 @@ def bench_prefill(args, world, device):
         tops = ops / (ms * 1e-3) / 1e12
         stages, launches = stage_profile([lambda: blk(x, options=o)], reps=1)
         key = str(T) if kernel == 0 else f"{T}_swap_ab_kernel"
-        out[key] = {"gemm": "tcgen05 tile-per-CTA" if kernel == 0 else "tcgen05 swap-AB persistent",
+        out[key] = {"gemm": "tcgen05 persistent tile (TMA)" if kernel == 0 else "tcgen05 swap-AB persistent",
                     "ms": round(ms, 4), "tok_per_s": round(T / (ms * 1e-3), 1),
                     "TOPs": round(tops, 2),
                     "frac_of_measured_bf16_peak": round(tops / peaks["bf16_tflops"], 4),

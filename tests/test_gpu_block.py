@@ -37,7 +37,7 @@ def _block(oracle, H, E, k, I, Is, seed, cuda):
 
 
 def _opts(min_tokens, int8=1, down_int8=1, wsum=0, kernel=0, decode_kernel=0):
-    """kernel 0 = the tile-per-CTA tcgen05 grouped GEMMs (default), 1 =
+    """kernel 0 = the persistent tile tcgen05 grouped GEMMs (default), 1 =
     mma.sync baseline, 2 = the persistent swap-AB tcgen05 kernel;
     decode_kernel 0 = the layer in one launch where it applies, 1 = three."""
     from titan_b200 import _lib
@@ -302,7 +302,7 @@ def test_empty_batch_and_determinism(cuda, oracle):
 def test_prefill_swap_ab_kernel_launches(cuda, oracle):
     """The swap-AB tcgen05 kernel (gemm_kernel 2) runs the routed experts with
     its own h quantiser, and the shared expert always: the launches the block
-    makes, and the same bits as the tile-per-CTA kernel."""
+    makes, and the same bits as the tile kernel."""
     blk, L = _block(oracle, 512, 16, 4, 128, 256, seed=12, cuda=cuda)
     x = oracle.make_x(96, 512, seed=12)
     y, names = _launches(lambda: blk(bf(x), options=_opts(min_tokens=1, kernel=2)))
