@@ -226,8 +226,9 @@ typedef struct tmoe_options {
   int wsum_mode;    /* 0 clone, 1 fast */
   int int8_prefill; /* 1: int8 gate_up (the overlay installed); 0: the stock
                        bf16-activation grouped GEMMs for the prefill path */
-  int gemm_kernel;  /* routed int8 prefill GEMMs: 0 = tile-per-CTA tcgen05
-                       kernel (default), 1 = mma.sync (the comparison
+  int gemm_kernel;  /* routed int8 prefill GEMMs: 0 = persistent TMA-fed tile
+                       tcgen05 kernel (default; K <= 3072, else mma.sync),
+                       1 = mma.sync (the comparison
                        baseline), 2 = persistent swap-AB tcgen05 kernel
                        (weight rows on the MMA's M side, TMA-fed; needs the
                        row normalisers).  All three keep the int8 algebra's

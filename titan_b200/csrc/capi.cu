@@ -772,7 +772,7 @@ int opt_down_int8(const tmoe_options* o) { return o ? (o->down_int8 != 0) : 1; }
 int opt_wsum(const tmoe_options* o) { return o ? o->wsum_mode : 0; }
 int opt_int8(const tmoe_options* o) { return o ? (o->int8_prefill != 0) : 1; }
 int opt_gemm(const tmoe_options* o) { return o ? o->gemm_kernel : 0; }
-// the tile-per-CTA tcgen05 kernel (else mma.sync) where the swap-AB one is not used
+// the persistent tile tcgen05 kernel (else mma.sync) where the swap-AB one is not used
 int opt_tc05(const tmoe_options* o) { return opt_gemm(o) != 1; }
 // The per-group tcgen05 kernel runs every grouped GEMM of the layer when it is
 // selected and takes all of the layer's shapes (K <= 3072, N % 128 == 0);
