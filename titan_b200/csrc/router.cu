@@ -7,8 +7,9 @@
 //   * router_logits_gemv  — decode shapes: 4 experts per warp (8 lanes = the
 //     8 canonical partials each), every weight row streamed once from HBM;
 //   * router_logits_tiled — prefill shapes: a 64-token x 32-expert CTA tile,
-//     x and W staged through shared memory by cp.async, 64 accumulators per
-//     thread (8 tokens x 8 experts) for one canonical partial.
+//     x and W staged through a 4-stage cp.async ring in shared memory, 64
+//     accumulators per thread (8 tokens x 8 experts, packed in expert pairs
+//     for f32x2 FMAs) for one canonical partial.
 // The optional shared-expert gate row wg is evaluated as expert row E; its
 // fp32 logit goes to gate_logit[T].
 #include "common.cuh"
@@ -94,8 +95,9 @@ __global__ void __launch_bounds__(256) router_logits_tiled(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
     const uint16_t* __restrict__ wg, int T, int H, int E, uint16_t* __restrict__ logits,
     float* __restrict__ gate_logit) {
-  __shared__ uint4 xs[2][64][8];
-  __shared__ uint4 ws[2][32][8];
+  constexpr int NS = 4;              // cp.async stages: 3 K steps of loads in flight
+  __shared__ uint4 xs[NS][64][8];
+  __shared__ uint4 ws[NS][32][8];
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int p = lane & 7;
@@ -125,36 +127,58 @@ __global__ void __launch_bounds__(256) router_logits_tiled(
     cp_async_commit();
   };
 
-  float acc[8][8];
+  // accumulators of expert pairs (ee = 2q, 2q + 1) as float2: packed f32x2
+  // FMAs, each component in the scalar order (u ascending within a K step)
+  float2 acc2[8][4];
 #pragma unroll
   for (int a = 0; a < 8; ++a)
 #pragma unroll
-    for (int b = 0; b < 8; ++b) acc[a][b] = 0.0f;
+    for (int b = 0; b < 4; ++b) acc2[a][b] = make_float2(0.0f, 0.0f);
 
-  load_stage(0, 0);
-  for (int ks = 0; ks < nk; ++ks) {
-    if (ks + 1 < nk) {
-      load_stage((ks + 1) & 1, ks + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const int st = ks & 1;
-    float xf[8][8];
-#pragma unroll
-    for (int tt = 0; tt < 8; ++tt) unpack8_bf16(xs[st][tt * 8 + gt][p], xf[tt]);
-#pragma unroll
-    for (int ee = 0; ee < 8; ++ee) {
-      float wf[8];
-      unpack8_bf16(ws[st][ee * 4 + ge][p], wf);
-#pragma unroll
-      for (int tt = 0; tt < 8; ++tt)
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc[tt][ee] = __fmaf_rn(xf[tt][u], wf[u], acc[tt][ee]);
-    }
-    __syncthreads();
+  for (int s = 0; s < NS - 1; ++s) {   // one commit group per stage, empty ones too
+    if (s < nk)
+      load_stage(s, s);
+    else
+      cp_async_commit();
   }
+  for (int ks = 0; ks < nk; ++ks) {
+    cp_async_wait<NS - 2>();             // this thread's copies of step ks landed
+    __syncthreads();                     // ... every thread's; step ks - 1 is consumed
+    const int kn = ks + NS - 1;          // refill the stage step ks - 1 used
+    if (kn < nk)
+      load_stage(kn % NS, kn);
+    else
+      cp_async_commit();
+    const int st = ks % NS;
+    float2 w2[4][8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float wa[8], wb[8];
+      unpack8_bf16(ws[st][(2 * q) * 4 + ge][p], wa);
+      unpack8_bf16(ws[st][(2 * q + 1) * 4 + ge][p], wb);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) w2[q][u] = make_float2(wa[u], wb[u]);
+    }
+#pragma unroll
+    for (int tt = 0; tt < 8; ++tt) {
+      float xf[8];
+      unpack8_bf16(xs[st][tt * 8 + gt][p], xf);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float2 x2 = make_float2(xf[u], xf[u]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc2[tt][q] = __ffma2_rn(x2, w2[q][u], acc2[tt][q]);
+      }
+    }
+  }
+  float acc[8][8];
+#pragma unroll
+  for (int tt = 0; tt < 8; ++tt)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      acc[tt][2 * q] = acc2[tt][q].x;
+      acc[tt][2 * q + 1] = acc2[tt][q].y;
+    }
 #pragma unroll
   for (int tt = 0; tt < 8; ++tt)
 #pragma unroll
