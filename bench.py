@@ -623,7 +623,9 @@ def _run_ep(args, world, rank, local, device):
                 "us_per_launch": round(st["us_per_launch"], 2),
                 "launches_per_step": st["launches"],
                 "dominant_of_step": dom[0],
-                "traffic": traffic.get(f"{name}_ep"),
+                # captured at N = 1 (one rank serves every expert); at N > 1 a
+                # rank's launch reads another weight set, so none is claimed
+                "traffic": traffic.get(f"{name}_ep") if world == 1 else None,
                 "note": "f16 MMA per 64-wide group (exact int8 x int4 sums) and the "
                         "reference's fp32 rescale; flops = 2 x routed pairs of rank 0 x N x K, "
                         "no padding counted"}
