@@ -464,9 +464,11 @@ __global__ void __launch_bounds__(sw::NTHREADS, 1)
       const int wr0 = wrow0(EPI, P.Nw, t.mp, 0) + lr, wr1 = wrow0(EPI, P.Nw, t.mp, 1) + lr;
       const float rs0 = P.rscale[(size_t)t.e * P.Nw + wr0];
       const float rs1 = P.rscale[(size_t)t.e * P.Nw + wr1];
-      float acc0[32], acc1[32];
+      // accumulators as token-column pairs: the per-group rescale issues as
+      // packed f32x2 FMAs (each component rounds exactly as a scalar fma.rn)
+      float2 acc0[16], acc1[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) acc0[i] = acc1[i] = 0.0f;
+      for (int i = 0; i < 16; ++i) acc0[i] = acc1[i] = make_float2(0.0f, 0.0f);
       for (int g = 0; g < G; ++g) {
         const int d = bc % ND, sb = bc % NB, se = bc % NES;
         if (!warp_wait(bar(BAR_DF + d), (bc / ND) & 1, abort_flag) ||
@@ -485,7 +487,7 @@ __global__ void __launch_bounds__(sw::NTHREADS, 1)
               tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(d * 2 * kSwTileN + 32 * h);
 #pragma unroll
           for (int m = 0; m < 2; ++m) {
-            float* acc = m ? acc1 : acc0;
+            float2* acc = m ? acc1 : acc0;
             const float bv = m ? bv1 : bv0;
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {          // 16 columns at a time: fewer registers
@@ -496,13 +498,14 @@ __global__ void __launch_bounds__(sw::NTHREADS, 1)
               for (int c4 = 0; c4 < 4; ++c4) {
                 const float4 a1 = *reinterpret_cast<const float4*>(c1 + 16 * hh + 4 * c4);
                 const float4 a2 = *reinterpret_cast<const float4*>(c2 + 16 * hh + 4 * c4);
-                const float x1[4] = {a1.x, a1.y, a1.z, a1.w}, x2[4] = {a2.x, a2.y, a2.z, a2.w};
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  const int c = 16 * hh + 4 * c4 + u;
-                  acc[c] = __fmaf_rn(v[4 * c4 + u], x1[u], acc[c]);
-                  acc[c] = __fmaf_rn(x2[u], bv, acc[c]);
-                }
+                const float2 bv2 = make_float2(bv, bv);
+                const int c = (16 * hh + 4 * c4) >> 1;
+                acc[c] = __ffma2_rn(make_float2(v[4 * c4], v[4 * c4 + 1]), make_float2(a1.x, a1.y),
+                                    acc[c]);
+                acc[c] = __ffma2_rn(make_float2(a2.x, a2.y), bv2, acc[c]);
+                acc[c + 1] = __ffma2_rn(make_float2(v[4 * c4 + 2], v[4 * c4 + 3]),
+                                        make_float2(a1.z, a1.w), acc[c + 1]);
+                acc[c + 1] = __ffma2_rn(make_float2(a2.z, a2.w), bv2, acc[c + 1]);
               }
             }
           }
@@ -521,27 +524,37 @@ __global__ void __launch_bounds__(sw::NTHREADS, 1)
         const float inv0 = __fdiv_rn(1.0f, rs0), inv1 = __fdiv_rn(1.0f, rs1);
         const int n = min(32, t.ntok - 32 * h);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          uint16_t* dst = reinterpret_cast<uint16_t*>(
+        for (int i = 0; i < 32; i += 2) {
+          uint16_t* dst0 = reinterpret_cast<uint16_t*>(
               __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(myrow), i));
-          if (i < n) {
-            if (EPI == kEpiStore) {
-              dst[wr0] = f2bf(__fmul_rn(acc0[i], inv0));
-              dst[wr1] = f2bf(__fmul_rn(acc1[i], inv1));
-            } else {
-              const float gt = bfround(__fmul_rn(acc0[i], inv0));
-              const float ut = bfround(__fmul_rn(acc1[i], inv1));
-              dst[t.mp * 128 + lr] = f2bf(swiglu_bf16(gt, ut));
+          uint16_t* dst1 = reinterpret_cast<uint16_t*>(
+              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(myrow), i + 1));
+          const float2 a = acc0[i >> 1], b = acc1[i >> 1];
+          if (EPI == kEpiStore) {
+            if (i < n) {
+              dst0[wr0] = f2bf(__fmul_rn(a.x, inv0));
+              dst0[wr1] = f2bf(__fmul_rn(b.x, inv1));
             }
+            if (i + 1 < n) {
+              dst1[wr0] = f2bf(__fmul_rn(a.y, inv0));
+              dst1[wr1] = f2bf(__fmul_rn(b.y, inv1));
+            }
+          } else if (i < n) {
+            const float2 gt = bfround2(__fmul2_rn(a, make_float2(inv0, inv0)));
+            const float2 ut = bfround2(__fmul2_rn(b, make_float2(inv1, inv1)));
+            const float2 hv = swiglu_bf16x2(gt, ut);
+            dst0[t.mp * 128 + lr] = f2bf(hv.x);
+            if (i + 1 < n) dst1[t.mp * 128 + lr] = f2bf(hv.y);
           }
         }
-        // stores into other GPUs' memory are performed at system scope before
-        // the kernel ends (the expert-parallel return posts after it)
-        if (EPI == kEpiStore && P.y_ptr) __threadfence_system();
       }
     }
   }
 
+  // stores into other GPUs' memory (the expert-parallel return) are performed
+  // at system scope before the kernel ends: one fence per storing thread,
+  // after its last item
+  if (EPI == kEpiStore && P.y_ptr && warp >= 8) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
