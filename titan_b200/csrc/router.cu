@@ -24,9 +24,10 @@ TMOE_DEV float tree8_sum(float v) {
   return v;
 }
 
-// One warp = 4 expert rows (8 lanes each, one per canonical partial).  The
-// warp first copies its 4 weight rows and up to 8 token rows into shared
-// memory with cp.async (every byte in flight at once), then reduces.
+// One warp = 4 expert rows (8 lanes each, one per canonical partial) x one
+// chunk of up to 8 tokens (blockIdx.y).  The warp first copies its 4 weight
+// rows and its token rows into shared memory with cp.async (every byte in
+// flight at once), then reduces.
 constexpr int kGemvTok = 8;
 
 __global__ void __launch_bounds__(32) router_logits_gemv(
@@ -50,7 +51,9 @@ __global__ void __launch_bounds__(32) router_logits_gemv(
     const uint16_t* row = ok ? ((er < E) ? wr + (size_t)er * H : wg) : wr;
     cp_async16_zfill(&ws[i], row + (size_t)c * 8, ok);
   }
-  for (int t0 = 0; t0 < T; t0 += kGemvTok) {
+  // token chunks of kGemvTok are spread over blockIdx.y (and strided, should
+  // the grid be smaller than T needs)
+  for (int t0 = blockIdx.y * kGemvTok; t0 < T; t0 += gridDim.y * kGemvTok) {
     const int nt = min(kGemvTok, T - t0);
     __syncwarp();
     for (int i = lane; i < nt * nch; i += 32)
@@ -277,7 +280,8 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const ui
     const size_t smem = (size_t)(4 + kGemvTok) * H * 2;
     cudaError_t e = ensure_smem_attr((const void*)router_logits_gemv, (int)smem);
     if (e != cudaSuccess) return e;
-    router_logits_gemv<<<(nrows + 3) / 4, 32, smem, s>>>(x, wr, wg, T, H, E, logits, gate_logit);
+    router_logits_gemv<<<dim3((nrows + 3) / 4, (T + kGemvTok - 1) / kGemvTok), 32, smem, s>>>(
+        x, wr, wg, T, H, E, logits, gate_logit);
   } else {
     dim3 grid((T + 63) / 64, (nrows + 31) / 32);
     router_logits_tiled<<<grid, 256, 0, s>>>(x, wr, wg, T, H, E, logits, gate_logit);
