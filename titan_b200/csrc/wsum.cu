@@ -111,41 +111,38 @@ __global__ void __launch_bounds__(128) wsum_prefetch_kernel(const uint16_t* __re
     sg = bfround(csigmoid(bfround(gate_logit[t])));
     unpack8_bf16(__ldg(reinterpret_cast<const uint4*>(sh + (size_t)t * D + d0)), shv8);
   }
-  uint16_t o[8];
+  // two columns at a time (the two bf16 of one 32-bit word): packed f32x2
+  // multiplies and adds and bf16x2 roundings, the same operations per column
+  uint32_t o2[4];
 #pragma unroll
-  for (int v = 0; v < 8; ++v) {
-    float part[8];
+  for (int vp = 0; vp < 4; ++vp) {
+    float2 part[8];
 #pragma unroll
-    for (int a = 0; a < 8; ++a) part[a] = 0.0f;
+    for (int a = 0; a < 8; ++a) part[a] = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int j = 0; j < KMAX; ++j) {
       if (j < k) {
-        const uint32_t wd = (v >> 1) == 0 ? raw[j].x
-                            : (v >> 1) == 1 ? raw[j].y
-                            : (v >> 1) == 2 ? raw[j].z : raw[j].w;
-        const uint32_t w = (v & 1) ? (wd & 0xffff0000u) : (wd << 16);
-        float prod = __fmul_rn(sc[j], __uint_as_float(w));
-        if (mode == 0) prod = bfround(prod);
-        const float tt = __fadd_rn(part[j & 7], prod);
-        part[j & 7] = (mode == 0) ? bfround(tt) : tt;
+        const uint32_t wd = vp == 0 ? raw[j].x : vp == 1 ? raw[j].y : vp == 2 ? raw[j].z : raw[j].w;
+        const float2 y2 = make_float2(__uint_as_float(wd << 16), __uint_as_float(wd & 0xffff0000u));
+        float2 prod = __fmul2_rn(make_float2(sc[j], sc[j]), y2);
+        if (mode == 0) prod = bfround2(prod);
+        const float2 tt = __fadd2_rn(part[j & 7], prod);
+        part[j & 7] = (mode == 0) ? bfround2(tt) : tt;
       }
     }
-    float a = part[0];
+    float2 a = part[0];
 #pragma unroll
     for (int j = 1; j < 8; ++j) {
-      a = __fadd_rn(a, part[j]);
-      if (mode == 0) a = bfround(a);
+      a = __fadd2_rn(a, part[j]);
+      if (mode == 0) a = bfround2(a);
     }
-    a = bfround(a);
-    if (sh) a = __fadd_rn(a, bfround(__fmul_rn(sg, shv8[v])));
-    o[v] = f2bf(a);
+    a = bfround2(a);
+    if (sh)
+      a = __fadd2_rn(a, bfround2(__fmul2_rn(make_float2(sg, sg),
+                                            make_float2(shv8[2 * vp], shv8[2 * vp + 1]))));
+    o2[vp] = (uint32_t)f2bf(a.x) | ((uint32_t)f2bf(a.y) << 16);
   }
-  uint4 pk;
-  pk.x = o[0] | ((uint32_t)o[1] << 16);
-  pk.y = o[2] | ((uint32_t)o[3] << 16);
-  pk.z = o[4] | ((uint32_t)o[5] << 16);
-  pk.w = o[6] | ((uint32_t)o[7] << 16);
-  *reinterpret_cast<uint4*>(out + (size_t)t * D + d0) = pk;
+  *reinterpret_cast<uint4*>(out + (size_t)t * D + d0) = make_uint4(o2[0], o2[1], o2[2], o2[3]);
 }
 
 cudaError_t launch_wsum(const uint16_t* ys, const int32_t* inv, const uint16_t* scores, int T, int k,
