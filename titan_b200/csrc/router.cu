@@ -8,8 +8,8 @@
 //     8 canonical partials each), every weight row streamed once from HBM;
 //   * router_logits_tiled — prefill shapes: a 64-token x 32-expert CTA tile,
 //     x and W staged through a 4-stage cp.async ring in shared memory, 64
-//     accumulators per thread (8 tokens x 8 experts, packed in expert pairs
-//     for f32x2 FMAs) for one canonical partial.
+//     accumulators per thread (4 tokens x 8 experts, packed in expert pairs
+//     for f32x2 FMAs) for one canonical partial, 512 threads.
 // The optional shared-expert gate row wg is evaluated as expert row E; its
 // fp32 logit goes to gate_logit[T].
 #include "common.cuh"
@@ -90,11 +90,12 @@ __global__ void __launch_bounds__(32) router_logits_gemv(
   }
 }
 
-// CTA tile: 64 tokens x 32 experts, K step 64 elements (8 chunks).
-// Thread roles: p = lane & 7 is the canonical partial (chunk p of each step),
-// gid = warp*4 + (lane>>3) in [0,32): gt = gid & 7 selects tokens
-// tt*8 + gt, ge = gid >> 3 selects experts ee*4 + ge (conflict-free smem).
-__global__ void __launch_bounds__(256) router_logits_tiled(
+// CTA tile: 64 tokens x 32 experts, K step 64 elements (8 chunks), 512
+// threads.  Thread roles: p = lane & 7 is the canonical partial (chunk p of
+// each step), gid = warp*4 + (lane>>3) in [0,64): gt = gid & 15 selects tokens
+// tt*16 + gt (tt < 4), ge = gid >> 4 selects experts ee*4 + ge
+// (conflict-free smem).
+__global__ void __launch_bounds__(512) router_logits_tiled(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
     const uint16_t* __restrict__ wg, int T, int H, int E, uint16_t* __restrict__ logits,
     float* __restrict__ gate_logit) {
@@ -104,14 +105,14 @@ __global__ void __launch_bounds__(256) router_logits_tiled(
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int p = lane & 7;
-  const int gid = warp * 4 + (lane >> 3);
-  const int gt = gid & 7, ge = gid >> 3;
+  const int gid = warp * 4 + (lane >> 3);      // [0, 64)
+  const int gt = gid & 15, ge = gid >> 4;       // tokens tt*16 + gt, experts ee*4 + ge
   const int tok0 = blockIdx.x * 64, exp0 = blockIdx.y * 32;
   const int nrows = E + (wg ? 1 : 0);
   const int nk = H / 64;
 
   auto load_stage = [&](int stage, int ks) {
-    for (int i = tid; i < 768; i += 256) {
+    for (int i = tid; i < 768; i += 512) {
       if (i < 512) {
         int r = i >> 3, ch = i & 7;
         int t = tok0 + r;
@@ -132,9 +133,9 @@ __global__ void __launch_bounds__(256) router_logits_tiled(
 
   // accumulators of expert pairs (ee = 2q, 2q + 1) as float2: packed f32x2
   // FMAs, each component in the scalar order (u ascending within a K step)
-  float2 acc2[8][4];
+  float2 acc2[4][4];
 #pragma unroll
-  for (int a = 0; a < 8; ++a)
+  for (int a = 0; a < 4; ++a)
 #pragma unroll
     for (int b = 0; b < 4; ++b) acc2[a][b] = make_float2(0.0f, 0.0f);
 
@@ -163,9 +164,9 @@ __global__ void __launch_bounds__(256) router_logits_tiled(
       for (int u = 0; u < 8; ++u) w2[q][u] = make_float2(wa[u], wb[u]);
     }
 #pragma unroll
-    for (int tt = 0; tt < 8; ++tt) {
+    for (int tt = 0; tt < 4; ++tt) {
       float xf[8];
-      unpack8_bf16(xs[st][tt * 8 + gt][p], xf);
+      unpack8_bf16(xs[st][tt * 16 + gt][p], xf);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const float2 x2 = make_float2(xf[u], xf[u]);
@@ -174,23 +175,23 @@ __global__ void __launch_bounds__(256) router_logits_tiled(
       }
     }
   }
-  float acc[8][8];
+  float acc[4][8];
 #pragma unroll
-  for (int tt = 0; tt < 8; ++tt)
+  for (int tt = 0; tt < 4; ++tt)
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       acc[tt][2 * q] = acc2[tt][q].x;
       acc[tt][2 * q + 1] = acc2[tt][q].y;
     }
 #pragma unroll
-  for (int tt = 0; tt < 8; ++tt)
+  for (int tt = 0; tt < 4; ++tt)
 #pragma unroll
     for (int ee = 0; ee < 8; ++ee) acc[tt][ee] = tree8_sum(acc[tt][ee]);
-  // lane p stores token tt = p of its group.
+  // lane p < 4 stores token tt = p of its group.
 #pragma unroll
-  for (int tt = 0; tt < 8; ++tt) {
+  for (int tt = 0; tt < 4; ++tt) {
     if (tt != p) continue;
-    int t = tok0 + tt * 8 + gt;
+    int t = tok0 + tt * 16 + gt;
     if (t >= T) continue;
 #pragma unroll
     for (int ee = 0; ee < 8; ++ee) {
@@ -284,7 +285,7 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const ui
         x, wr, wg, T, H, E, logits, gate_logit);
   } else {
     dim3 grid((T + 63) / 64, (nrows + 31) / 32);
-    router_logits_tiled<<<grid, 256, 0, s>>>(x, wr, wg, T, H, E, logits, gate_logit);
+    router_logits_tiled<<<grid, 512, 0, s>>>(x, wr, wg, T, H, E, logits, gate_logit);
   }
   return cudaGetLastError();
 }
