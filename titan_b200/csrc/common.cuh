@@ -76,12 +76,21 @@ TMOE_DEV float swiglu_bf16(float g, float u) {
   return bfround(__fmul_rn(a, u));
 }
 
+// Packed f32x2 arithmetic, checked on the B200 with nvcc 12.9: a
+// __fmul2_rn whose result feeds a __fadd2_rn is contracted into one fused
+// multiply-add (the scalar __fmul_rn never is).  Every packed product in this
+// library therefore feeds a rounding (bfround2) or an FMA multiplicand; a
+// product that must be rounded before an add is computed with __fmul_rn.
+//
 // Two lanes of cexp at once, bit-identical per component: rint(x * log2e)
 // as (t + 1.5*2^23) - 1.5*2^23 (exact round-to-nearest-even for |t| < 2^22),
 // the integer n read from the same sum's bits, the reduction and polynomial
 // as packed f32x2 FMAs, the special cases selected afterwards.
 TMOE_DEV float2 cexp2(float2 x) {
-  const float2 t = __fmul2_rn(x, make_float2(1.44269504088896341f, 1.44269504088896341f));
+  // the product stays scalar: __fmul_rn is never fused into the add below,
+  // so rint sees the rounded product exactly as cexp does
+  const float2 t = make_float2(__fmul_rn(x.x, 1.44269504088896341f),
+                               __fmul_rn(x.y, 1.44269504088896341f));
   const float2 big = __fadd2_rn(t, make_float2(12582912.0f, 12582912.0f));
   const float2 n = __fadd2_rn(big, make_float2(-12582912.0f, -12582912.0f));
   const float2 mn = make_float2(-n.x, -n.y);

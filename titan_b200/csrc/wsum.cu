@@ -124,7 +124,8 @@ __global__ void __launch_bounds__(128) wsum_prefetch_kernel(const uint16_t* __re
       if (j < k) {
         const uint32_t wd = vp == 0 ? raw[j].x : vp == 1 ? raw[j].y : vp == 2 ? raw[j].z : raw[j].w;
         const float2 y2 = make_float2(__uint_as_float(wd << 16), __uint_as_float(wd & 0xffff0000u));
-        float2 prod = __fmul2_rn(make_float2(sc[j], sc[j]), y2);
+        // scalar products (never fused into the following add)
+        float2 prod = make_float2(__fmul_rn(sc[j], y2.x), __fmul_rn(sc[j], y2.y));
         if (mode == 0) prod = bfround2(prod);
         const float2 tt = __fadd2_rn(part[j & 7], prod);
         part[j & 7] = (mode == 0) ? bfround2(tt) : tt;
