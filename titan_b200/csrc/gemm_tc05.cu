@@ -699,22 +699,39 @@ __global__ void __launch_bounds__(256) prep_a16_kernel(const uint16_t* __restric
       if (c == 0 && (am >= 65504.0f || (am > 0.0f && am < 6.103515625e-05f)))
         atomicExch(&g_tc05_error, 2);
     }
+    // element pairs (i, i + 4): the stored order 0,4,1,5,2,6,3,7
+    float2 pr[4];
     if (QUANT) {
       const float sc = __fdiv_rn(fmaxf(am, 1e-30f), 127.0f);
       const float inv = __fdiv_rn(1.0f, sc);
+      // xu - 128 = clamp(rint(v / sc) + 128, 0, 255) - 128, two lanes at a
+      // time.  The products stay scalar (__fmul_rn is never fused into the
+      // add after it); rint is (t + 1.5*2^23) - 1.5*2^23, exact for |t| < 2^22
+      // (here |t| <= 127).
+      const float2 big = make_float2(12582912.0f, 12582912.0f),
+                   nbig = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        v[k] = __fadd_rn(fminf(fmaxf(__fadd_rn(rintf(__fmul_rn(v[k], inv)), 128.0f), 0.0f), 255.0f),
-                         -128.0f);
+      for (int i = 0; i < 4; ++i) {
+        const float2 t = make_float2(__fmul_rn(v[i], inv), __fmul_rn(v[i + 4], inv));
+        const float2 q = __fadd2_rn(__fadd2_rn(__fadd2_rn(t, big), nbig), make_float2(128.0f, 128.0f));
+        pr[i] = __fadd2_rn(make_float2(fminf(fmaxf(q.x, 0.0f), 255.0f), fminf(fmaxf(q.y, 0.0f), 255.0f)),
+                           make_float2(-128.0f, -128.0f));
+      }
       if (c == 0) xsc[(size_t)m * srow + g] = sc;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pr[i] = make_float2(v[i], v[i + 4]);
     }
     if (c == 0) xrs[(size_t)m * srow + g] = sum;
-    auto h = [](float f) { return (uint32_t)__half_as_ushort(__float2half_rn(f)); };
-    uint4 pk;                                        // stored order 0,4,1,5,2,6,3,7
-    pk.x = h(v[0]) | (h(v[4]) << 16);
-    pk.y = h(v[1]) | (h(v[5]) << 16);
-    pk.z = h(v[2]) | (h(v[6]) << 16);
-    pk.w = h(v[3]) | (h(v[7]) << 16);
+    auto h2 = [](float2 f) {                         // .x in the low half
+      const __half2 hh = __float22half2_rn(f);
+      return *reinterpret_cast<const uint32_t*>(&hh);
+    };
+    uint4 pk;
+    pk.x = h2(pr[0]);
+    pk.y = h2(pr[1]);
+    pk.z = h2(pr[2]);
+    pk.w = h2(pr[3]);
     *reinterpret_cast<uint4*>(a16 + (size_t)m * K + g * kGroup + c * 8) = pk;
   }
 }
